@@ -1,0 +1,558 @@
+// Grouped bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM, TMA-fed), used for
+// the MoE expert GEMMs (K4 gate|up with optional fused SwiGLU, K6 down), the shared expert
+// and the MLA kv up-projection (K9).  Replaces the per-expert cublasGemmEx host loops of
+// src/kernels/moe/gemm1.cu:84-155 and gemm2.cu:75-124 and the single call of
+// src/kernels/mla/kv_upproj.cu:77-119.
+//
+// Structure (one persistent CTA per SM, 192 threads):
+//   warp 0       TMA producer: A tile 128x64 and B tile 256x64 (two 128-row boxes) per
+//                k-block into a 4-stage shared-memory ring (128-byte swizzle).
+//   warp 1       MMA issuer: tcgen05.mma kind::f16, M=128 N=256 K=16, f32 accumulator in
+//                TMEM, two accumulator buffers (2 x 256 columns) so the epilogue of tile i
+//                overlaps the MMAs of tile i+1.
+//   warps 2-5    epilogue: tcgen05.ld 32x32b -> registers -> bf16 (optionally SwiGLU) ->
+//                global, one accumulator row per thread, rows masked at the group end.
+// Tiles are enumerated m-tile-major over a per-group tile prefix that every CTA builds
+// from the device-side group offsets (no host synchronisation); CTA c takes tiles
+// c, c + gridDim.x, ...  Every mbarrier wait is bounded (ptx::mbar_wait).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <mutex>
+
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace ds {
+namespace gemm {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t A_BYTES = BM * BK * 2;        // 16 KiB
+constexpr uint32_t B_HALF_BYTES = 128 * BK * 2;  // 16 KiB
+constexpr uint32_t B_BYTES = BN * BK * 2;        // 32 KiB
+constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
+constexpr int kMaxGroups = 512;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTailBytes = 256;  // barriers + tmem holder + flags
+constexpr size_t kSmemBytes = 1024 + STAGES * (A_BYTES + B_BYTES) + kTailBytes +
+                              2 * (kMaxGroups + 1) * sizeof(int);
+constexpr long long kDefaultTimeoutCycles = 4000000000LL;  // ~2 s at 2 GHz
+
+struct Params {
+  const int32_t* offsets;
+  int groups;
+  int dense_rows;
+  int k_blocks;
+  int n_tiles;
+  int b_rows_per_group;
+  int b_tile_stride;
+  int b_half1_off;
+  int weight_group_mod;
+  __nv_bfloat16* out;
+  int ldo;
+  int epilogue;
+  const int32_t* out_row_map;
+  int* status;
+  long long timeout_cycles;
+};
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+struct TileInfo {
+  int row0;
+  int rows;
+  int brow0;
+  int nt;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(int t, const Params& p, const int* goff,
+                                                const int* gtile) {
+  TileInfo ti;
+  const int mtg = t / p.n_tiles;
+  ti.nt = t - mtg * p.n_tiles;
+  int lo = 0, hi = p.groups;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (gtile[mid] <= mtg) lo = mid;
+    else hi = mid;
+  }
+  ti.row0 = goff[lo] + (mtg - gtile[lo]) * BM;
+  ti.rows = min(BM, goff[lo + 1] - ti.row0);
+  ti.brow0 = (lo % p.weight_group_mod) * p.b_rows_per_group + ti.nt * p.b_tile_stride;
+  return ti;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sA = ptx::smem_u32(smem);
+  const uint32_t sB = sA + STAGES * A_BYTES;
+  uint8_t* tail = smem + STAGES * (A_BYTES + B_BYTES);
+  const uint32_t bar0 = ptx::smem_u32(tail);
+  // barrier k lives at bar0 + 8k: full[0..S), empty[S..2S), tfull[2], tempty[2], drain
+  const uint32_t full0 = bar0, empty0 = bar0 + 8u * STAGES;
+  const uint32_t tfull0 = bar0 + 16u * STAGES, tempty0 = tfull0 + 16u;
+  const uint32_t drain_bar = tempty0 + 16u;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 8 * (2 * STAGES + 5));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* never_flag = abort_flag + 1;
+  int* goff = reinterpret_cast<int*>(tail + kTailBytes);
+  int* gtile = goff + (kMaxGroups + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = p.groups;
+
+  for (int i = threadIdx.x; i <= G; i += kThreads)
+    goff[i] = p.offsets ? __ldg(p.offsets + i) : (i == 0 ? 0 : p.dense_rows);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(full0 + 8u * s, 1);
+      ptx::mbar_init(empty0 + 8u * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(tfull0 + 8u * a, 1);
+      ptx::mbar_init(tempty0 + 8u * a, 4);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    *never_flag = 0;
+    ptx::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int g = 0; g < G; ++g) {
+      gtile[g] = acc;
+      const int m = goff[g + 1] - goff[g];
+      acc += m > 0 ? (m + BM - 1) / BM : 0;
+    }
+    gtile[G] = acc;
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int total_tiles = gtile[G] * p.n_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t used_mask = 0, phase_mask = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+        const TileInfo ti = decode_tile(t, p, goff, gtile);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!ptx::mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag, p.status,
+                              p.timeout_cycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + 8u * stage;
+          ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
+          const uint32_t a_dst = sA + stage * A_BYTES;
+          const uint32_t b_dst = sB + stage * B_BYTES;
+          ptx::tma_load_2d(a_dst, &tmA, fb, kb * BK, ti.row0);
+          ptx::tma_load_2d(b_dst, &tmB, fb, kb * BK, ti.brow0);
+          ptx::tma_load_2d(b_dst + B_HALF_BYTES, &tmB, fb, kb * BK, ti.brow0 + p.b_half1_off);
+          used_mask |= 1u << stage;
+          phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Every load issued here must land before the CTA may exit.
+      for (int s = 0; s < STAGES; ++s) {
+        if (used_mask & (1u << s))
+          ptx::mbar_wait(full0 + 8u * s, (phase_mask >> s) & 1u, never_flag, p.status,
+                         p.timeout_cycles, DS_ERR_TIMEOUT);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+        if (!ptx::mbar_wait(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag, p.status,
+                            p.timeout_cycles, DS_ERR_TIMEOUT))
+          break;
+        ptx::tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!ptx::mbar_wait(full0 + 8u * stage, phase, abort_flag, p.status, p.timeout_cycles,
+                              DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a0 = sA + stage * A_BYTES;
+          const uint32_t b0 = sB + stage * B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            ptx::umma_f16(d, ptx::sw128_kmajor_desc(a0 + kk * 32u),
+                          ptx::sw128_kmajor_desc(b0 + kk * 32u), idesc,
+                          (kb | kk) != 0 ? 1u : 0u);
+          }
+          ptx::umma_commit(empty0 + 8u * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        ptx::umma_commit(tfull0 + 8u * acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // No MMA may still be writing TMEM when it is released.
+      ptx::umma_commit(drain_bar);
+      ptx::mbar_wait(drain_bar, 0, never_flag, p.status, p.timeout_cycles, DS_ERR_TIMEOUT);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = decode_tile(t, p, goff, gtile);
+      int ok = 1;
+      if (lane == 0)
+        ok = ptx::mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag, p.status,
+                            p.timeout_cycles, DS_ERR_TIMEOUT)
+                 ? 1
+                 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      ptx::tc_fence_after();
+      const uint32_t tb =
+          tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      const bool valid = r < ti.rows;
+      int64_t orow = ti.row0 + r;
+      if (valid && p.out_row_map != nullptr) orow = __ldg(p.out_row_map + orow);
+      if (p.epilogue == kSwiGLU) {
+        __nv_bfloat16* dst = p.out + orow * p.ldo + ti.nt * 128;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t g[32], u[32];
+          ptx::tmem_ld32(tb + cc * 32, g);
+          ptx::tmem_ld32(tb + 128 + cc * 32, u);
+          ptx::tmem_wait_ld2(g, u);
+          if (valid) {
+            uint32_t o[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              o[i] = pack2(silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
+                           silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1])));
+            uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t v[32];
+          ptx::tmem_ld32(tb + cc * 32, v);
+          ptx::tmem_wait_ld(v);
+          if (valid) {
+            const int col = ti.nt * p.b_tile_stride + (cc >> 2) * p.b_half1_off + (cc & 3) * 32;
+            uint4* d4 = reinterpret_cast<uint4*>(p.out + orow * p.ldo + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(pack2(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
+                                 pack2(__uint_as_float(v[8 * i + 2]), __uint_as_float(v[8 * i + 3])),
+                                 pack2(__uint_as_float(v[8 * i + 4]), __uint_as_float(v[8 * i + 5])),
+                                 pack2(__uint_as_float(v[8 * i + 6]), __uint_as_float(v[8 * i + 7])));
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(tempty0 + 8u * acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncwarp();  // lanes 1..31 of warps 0/1 rejoin their role lane before the CTA barrier
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Zero rows [0, off[0]) and [off[G], S) of out (the parts no group covers).
+__global__ void zero_uncovered_kernel(uint4* __restrict__ out, int64_t S, int ld8,
+                                      const int32_t* __restrict__ offsets, int G) {
+  const int64_t lo = min(S, static_cast<int64_t>(max(0, __ldg(offsets))));
+  const int64_t hi = min(S, static_cast<int64_t>(max(0, __ldg(offsets + G))));
+  const int64_t n_lo = lo * ld8;
+  const int64_t n_hi = (S - max(hi, lo)) * ld8;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_lo + n_hi;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (i < n_lo) out[i] = z;
+    else out[max(hi, lo) * ld8 + (i - n_lo)] = z;
+  }
+}
+
+// ---- host side --------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_err = cudaSuccess;
+bool g_attr_set[64] = {};
+std::mutex g_attr_mutex;
+
+int get_encode(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    g_encode_err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q);
+    if (g_encode_err == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  if (g_encode == nullptr)
+    return fail(DS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)",
+                cudaGetErrorString(g_encode_err));
+  *fn = g_encode;
+  return DS_OK;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box 64 x 128, 128-byte swizzle,
+// zero fill outside the matrix.
+int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int cols) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  DS_TRY(get_encode(&enc));
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), 128u};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%d", (int)r,
+                (long long)rows, cols);
+  return DS_OK;
+}
+
+}  // namespace
+
+int launch(const Problem& pr, cudaStream_t s) {
+  if (pr.a_rows <= 0) return DS_OK;
+  DS_REQUIRE(pr.A && pr.B && pr.out, "gemm: null pointer");
+  DS_REQUIRE(aligned16(pr.A) && aligned16(pr.B) && aligned16(pr.out),
+             "gemm: A, B and out must be 16-byte aligned");
+  DS_REQUIRE(pr.K > 0 && pr.K % 8 == 0, "gemm: K=%d must be a positive multiple of 8", pr.K);
+  DS_REQUIRE(pr.ldo % 8 == 0, "gemm: output leading dimension must be a multiple of 8");
+  DS_REQUIRE(pr.groups >= 1 && pr.groups <= kMaxGroups, "gemm: groups=%d outside [1, %d]",
+             pr.groups, kMaxGroups);
+  DS_REQUIRE(pr.n_tiles >= 1 && pr.weight_group_mod >= 1, "gemm: bad tiling");
+  DS_REQUIRE(pr.a_rows < (1LL << 31) && pr.b_rows < (1LL << 31), "gemm: too many rows");
+  DeviceInfo di;
+  DS_TRY(device_info(&di));
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (!g_attr_set[di.device]) {
+      DS_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(kSmemBytes)));
+      g_attr_set[di.device] = true;
+    }
+  }
+  CUtensorMap tmA, tmB;
+  DS_TRY(make_tmap(&tmA, pr.A, pr.a_rows, pr.K));
+  DS_TRY(make_tmap(&tmB, pr.B, pr.b_rows, pr.K));
+  Params p{};
+  p.offsets = pr.offsets;
+  p.groups = pr.offsets ? pr.groups : 1;
+  p.dense_rows = static_cast<int>(pr.a_rows);
+  p.k_blocks = (pr.K + BK - 1) / BK;
+  p.n_tiles = pr.n_tiles;
+  p.b_rows_per_group = pr.b_rows_per_group;
+  p.b_tile_stride = pr.b_tile_stride;
+  p.b_half1_off = pr.b_half1_off;
+  p.weight_group_mod = pr.weight_group_mod;
+  p.out = static_cast<__nv_bfloat16*>(pr.out);
+  p.ldo = pr.ldo;
+  p.epilogue = pr.epilogue;
+  p.out_row_map = pr.out_row_map;
+  p.status = device_status_ptr();
+  p.timeout_cycles = kDefaultTimeoutCycles;
+  if (p.status == nullptr) return fail(DS_ERR_CUDA, "device status word unavailable");
+  const int64_t max_mtiles = (pr.a_rows + BM - 1) / BM + (pr.offsets ? p.groups : 0);
+  const int64_t max_tiles = max_mtiles * pr.n_tiles;
+  const int grid = static_cast<int>(max_tiles < di.num_sms ? max_tiles : di.num_sms);
+  grouped_gemm_kernel<<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, p);
+  DS_LAUNCH_CHECK("grouped_gemm_kernel");
+  return DS_OK;
+}
+
+int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,
+                          cudaStream_t s) {
+  if (S <= 0) return DS_OK;
+  DeviceInfo di;
+  DS_TRY(device_info(&di));
+  zero_uncovered_kernel<<<di.num_sms, 256, 0, s>>>(static_cast<uint4*>(out), S, ldo / 8, offsets,
+                                                   groups);
+  DS_LAUNCH_CHECK("zero_uncovered_kernel");
+  return DS_OK;
+}
+
+}  // namespace gemm
+}  // namespace ds
+
+// ---- C ABI -----------------------------------------------------------------------------------
+using ds::fail;
+
+namespace {
+
+int moe_gemm1_impl(const void* dispatched, const void* packed_w1, const int32_t* offsets,
+                   void* out, int S, int E, int H, int twoI, int epilogue, void* stream) {
+  DS_REQUIRE(S >= 0 && E >= 1 && H > 0 && twoI > 0, "gemm1: bad shape");
+  DS_REQUIRE(twoI % 256 == 0, "gemm1: 2*intermediate_size=%d must be a multiple of 256", twoI);
+  DS_REQUIRE(H % 8 == 0, "gemm1: hidden_size must be a multiple of 8");
+  if (S == 0) return DS_OK;
+  DS_REQUIRE(offsets != nullptr, "gemm1: expert_offsets is null");
+  const int I = twoI / 2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ds::gemm::Problem pr{};
+  pr.A = dispatched;
+  pr.a_rows = S;
+  pr.K = H;
+  pr.B = packed_w1;
+  pr.b_rows = static_cast<int64_t>(E) * twoI;
+  pr.offsets = offsets;
+  pr.groups = E;
+  pr.n_tiles = I / 128;
+  pr.b_rows_per_group = twoI;
+  pr.b_tile_stride = 128;
+  pr.b_half1_off = I;
+  pr.weight_group_mod = E;
+  pr.out = out;
+  pr.ldo = epilogue == ds::gemm::kSwiGLU ? I : twoI;
+  pr.epilogue = epilogue;
+  pr.out_row_map = nullptr;
+  DS_TRY(ds::gemm::launch_zero_uncovered(out, S, pr.ldo, offsets, E, s));
+  return ds::gemm::launch(pr, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ds_moe_gemm1(const void* dispatched_bf16, const void* packed_w1_bf16,
+                 const int32_t* expert_offsets, void* gemm1_out_bf16, int total_slots,
+                 int num_experts, int hidden_size, int double_intermed, void* stream) {
+  return moe_gemm1_impl(dispatched_bf16, packed_w1_bf16, expert_offsets, gemm1_out_bf16,
+                        total_slots, num_experts, hidden_size, double_intermed,
+                        ds::gemm::kPlain, stream);
+}
+
+int ds_moe_gemm1_swiglu(const void* dispatched_bf16, const void* packed_w1_bf16,
+                        const int32_t* expert_offsets, void* swiglu_out_bf16,
+                        int total_slots, int num_experts, int hidden_size,
+                        int double_intermed, void* stream) {
+  return moe_gemm1_impl(dispatched_bf16, packed_w1_bf16, expert_offsets, swiglu_out_bf16,
+                        total_slots, num_experts, hidden_size, double_intermed,
+                        ds::gemm::kSwiGLU, stream);
+}
+
+int ds_moe_gemm2(const void* swiglu_out_bf16, const void* w2_bf16,
+                 const int32_t* expert_offsets, void* gemm2_out_bf16, int total_slots,
+                 int num_experts, int intermediate_size, int hidden_size, void* stream) {
+  DS_REQUIRE(total_slots >= 0 && num_experts >= 1 && intermediate_size > 0 && hidden_size > 0,
+             "gemm2: bad shape");
+  DS_REQUIRE(hidden_size % 256 == 0, "gemm2: hidden_size=%d must be a multiple of 256",
+             hidden_size);
+  DS_REQUIRE(intermediate_size % 8 == 0, "gemm2: intermediate_size must be a multiple of 8");
+  if (total_slots == 0) return DS_OK;
+  DS_REQUIRE(expert_offsets != nullptr, "gemm2: expert_offsets is null");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ds::gemm::Problem pr{};
+  pr.A = swiglu_out_bf16;
+  pr.a_rows = total_slots;
+  pr.K = intermediate_size;
+  pr.B = w2_bf16;
+  pr.b_rows = static_cast<int64_t>(num_experts) * hidden_size;
+  pr.offsets = expert_offsets;
+  pr.groups = num_experts;
+  pr.n_tiles = hidden_size / 256;
+  pr.b_rows_per_group = hidden_size;
+  pr.b_tile_stride = 256;
+  pr.b_half1_off = 128;
+  pr.weight_group_mod = num_experts;
+  pr.out = gemm2_out_bf16;
+  pr.ldo = hidden_size;
+  pr.epilogue = ds::gemm::kPlain;
+  pr.out_row_map = nullptr;
+  DS_TRY(ds::gemm::launch_zero_uncovered(gemm2_out_bf16, total_slots, hidden_size, expert_offsets,
+                                         num_experts, s));
+  return ds::gemm::launch(pr, s);
+}
+
+int ds_kv_upproj(const void* normed_kv_bf16, const void* weight_bf16, void* kv_up_bf16,
+                 int rows, int kv_lora_rank, int out_dim, void* stream) {
+  DS_REQUIRE(rows >= 0 && kv_lora_rank > 0 && out_dim > 0, "kv_upproj: bad shape");
+  DS_REQUIRE(out_dim % 256 == 0, "kv_upproj: out_dim=%d must be a multiple of 256", out_dim);
+  DS_REQUIRE(kv_lora_rank % 8 == 0, "kv_upproj: kv_lora_rank must be a multiple of 8");
+  if (rows == 0) return DS_OK;
+  ds::gemm::Problem pr{};
+  pr.A = normed_kv_bf16;
+  pr.a_rows = rows;
+  pr.K = kv_lora_rank;
+  pr.B = weight_bf16;
+  pr.b_rows = out_dim;
+  pr.offsets = nullptr;
+  pr.groups = 1;
+  pr.n_tiles = out_dim / 256;
+  pr.b_rows_per_group = out_dim;
+  pr.b_tile_stride = 256;
+  pr.b_half1_off = 128;
+  pr.weight_group_mod = 1;
+  pr.out = kv_up_bf16;
+  pr.ldo = out_dim;
+  pr.epilogue = ds::gemm::kPlain;
+  pr.out_row_map = nullptr;
+  return ds::gemm::launch(pr, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,79 @@
+// Internal launchers shared by the C-ABI entry points and the fused layer.
+#pragma once
+
+#include "common.cuh"
+
+namespace ds {
+
+// Routing granularity: tokens per routing block; histograms and ranks are per block.
+constexpr int kRouteTokens = 64;
+constexpr int kMaxExperts = 64;
+constexpr int kMaxTopK = 8;
+
+inline int route_blocks(int num_tokens) { return (num_tokens + kRouteTokens - 1) / kRouteTokens; }
+
+// logits [T, E] -> idx/w [T, K]; optional: counts (atomic adds into pre-zeroed [E]),
+// blk_hist [nblk, E], local_rank [T, K] (rank of the token among the block's tokens routed
+// to the same expert).
+int launch_route(const float* logits, int T, int E, int K, int32_t* idx, float* w,
+                 int32_t* counts, int32_t* blk_hist, int32_t* local_rank, cudaStream_t s);
+
+// idx [T, K] -> blk_hist [nblk, E], local_rank [T, K].
+int launch_rank(const int32_t* idx, int T, int E, int K, int32_t* blk_hist,
+                int32_t* local_rank, cudaStream_t s);
+
+// blk_hist [nblk, E] -> counts [E], offsets [E+1], blk_base [nblk, E].  When offsets_in is
+// given the expert bases come from it instead of from the scan of the column sums.
+int launch_plan(const int32_t* blk_hist, int nblk, int E, const int32_t* offsets_in,
+                int32_t* counts, int32_t* offsets, int32_t* blk_base, cudaStream_t s);
+
+// Exclusive scan of n ints into out[0..n] (out[n] = total).  Single CTA, any n.
+int launch_exclusive_scan(const int32_t* in, int n, int32_t* out, cudaStream_t s);
+
+// Scatter token rows into expert-contiguous slots (read each row once, write K copies).
+int launch_scatter(const void* x, int T, int H, int E, int K, const int32_t* idx,
+                   const float* w, const int32_t* blk_base, const int32_t* local_rank,
+                   void* dispatched, int32_t* token_map, float* dispatched_weights,
+                   int32_t* slot_of, int S, cudaStream_t s);
+
+// out[t] = sum_j w[t,j] * eo[slot_of[t,j]] (+ shared[t]), slots in ascending order.
+int launch_combine_gather(const void* eo, const int32_t* slot_of, const float* w, int K,
+                          const void* shared_out, void* out, int T, int H, cudaStream_t s);
+
+int launch_swiglu(const void* in, void* out, int64_t rows, int I, cudaStream_t s);
+
+namespace gemm {
+
+enum Epilogue : int { kPlain = 0, kSwiGLU = 1 };
+
+// Grouped / dense bf16 GEMM on tcgen05: for each row group g (rows [off[g], off[g+1]) of A)
+// out[rows, cols] = A[rows, :] @ B_w[...]^T with w = g % weight_group_mod.  B rows for
+// n-tile nt: two 128-row halves at (w*b_rows_per_group + nt*b_tile_stride) and
+// (+ b_half1_off); output columns are the same offsets without the group base.
+struct Problem {
+  const void* A;            // bf16 [a_rows, K]
+  int64_t a_rows;
+  int K;
+  const void* B;            // bf16 [b_rows, K]
+  int64_t b_rows;
+  const int32_t* offsets;   // device [groups+1], or nullptr for one dense group of a_rows
+  int groups;
+  int n_tiles;
+  int b_rows_per_group;
+  int b_tile_stride;
+  int b_half1_off;
+  int weight_group_mod;
+  void* out;                // bf16
+  int ldo;
+  int epilogue;
+  const int32_t* out_row_map;  // optional: destination row for each A row
+};
+
+int launch(const Problem& pr, cudaStream_t s);
+
+// Rows of out [S, ldo] outside [offsets[0], offsets[groups]) are set to zero.
+int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,
+                          cudaStream_t s);
+
+}  // namespace gemm
+}  // namespace ds

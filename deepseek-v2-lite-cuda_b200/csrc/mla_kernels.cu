@@ -1,0 +1,256 @@
+// MLA projection-path bandwidth kernels: RMSNorm over the 512-d kv latent (K8) and RoPE on
+// the 64-d rope slices of q and k (K10), with their C-ABI entry points.
+//
+// RMSNorm follows src/reference/mla.py:59-64 (f32 statistics) with the single rounding of
+// src/kernels/mla/rms_norm.cu:104-114; RoPE implements the interleave->half rotation of
+// src/reference/mla.py:183-206 in the per-element form of src/kernels/mla/rope.cu:23-26.
+#include "kernels.cuh"
+
+namespace ds {
+namespace {
+
+// One warp per row.  Rows of up to 2048 elements stay in registers (8 x 16 B per lane);
+// longer rows take a second pass over global memory.
+__global__ void __launch_bounds__(256)
+    rms_norm_kernel(const __nv_bfloat16* __restrict__ in, int64_t in_stride,
+                    const float* __restrict__ weight, __nv_bfloat16* __restrict__ out,
+                    int64_t out_stride, int rows, int H, float eps, int vec_ok) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const float inv_h = 1.f / static_cast<float>(H);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const __nv_bfloat16* x = in + static_cast<int64_t>(r) * in_stride;
+    __nv_bfloat16* y = out + static_cast<int64_t>(r) * out_stride;
+    if (vec_ok && H <= 2048) {
+      const int H8 = H >> 3;
+      uint4 v[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = u * 32 + lane;
+        if (c < H8) {
+          v[u] = __ldg(reinterpret_cast<const uint4*>(x) + c);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[u]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            ss = fmaf(f.x, f.x, ss);
+            ss = fmaf(f.y, f.y, ss);
+          }
+        }
+      }
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+      const float scale = rsqrtf(ss * inv_h + eps);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = u * 32 + lane;
+        if (c < H8) {
+          const float4 w0 = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c);
+          const float4 w1 = __ldg(reinterpret_cast<const float4*>(weight) + 2 * c + 1);
+          const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[u]);
+          uint4 o;
+          uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            const __nv_bfloat162 b =
+                __floats2bfloat162_rn(f.x * scale * wv[2 * i], f.y * scale * wv[2 * i + 1]);
+            ou[i] = *reinterpret_cast<const uint32_t*>(&b);
+          }
+          reinterpret_cast<uint4*>(y)[c] = o;
+        }
+      }
+    } else {
+      const int H2 = H >> 1;
+      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(x);
+      float ss = 0.f;
+      for (int c = lane; c < H2; c += 32) {
+        const float2 f = __bfloat1622float2(x2[c]);
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+      const float scale = rsqrtf(ss * inv_h + eps);
+      __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(y);
+      for (int c = lane; c < H2; c += 32) {
+        const float2 f = __bfloat1622float2(x2[c]);
+        y2[c] = __floats2bfloat162_rn(f.x * scale * weight[2 * c], f.y * scale * weight[2 * c + 1]);
+      }
+    }
+  }
+}
+
+// One thread per 8 input elements (4 rotation pairs) of a row; q rows then k rows.
+// cos/sin rows are shared by every head of a (batch, position).
+__global__ void __launch_bounds__(256)
+    rope_vec_kernel(const uint4* __restrict__ q, const uint4* __restrict__ k,
+                    const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t,
+                    uint4* __restrict__ qo, uint4* __restrict__ ko, int64_t q_rows,
+                    int64_t k_rows, int heads, int seq, int D) {
+  const int D8 = D >> 3, half = D >> 1;
+  const int64_t total = (q_rows + k_rows) * D8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / D8;
+    const int c = static_cast<int>(i - row * D8);
+    const bool is_q = row < q_rows;
+    const int64_t lrow = is_q ? row : row - q_rows;
+    // (b, h, s) for q rows, (b, s) for k rows -> cos/sin row b*seq + s
+    int64_t cs_row;
+    if (is_q) {
+      const int64_t s_ = lrow % seq;
+      const int64_t b_ = lrow / (static_cast<int64_t>(seq) * heads);
+      cs_row = b_ * seq + s_;
+    } else {
+      cs_row = lrow;
+    }
+    const uint4 xv = __ldg((is_q ? q : k) + lrow * D8 + c);
+    const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
+    const __nv_bfloat16* cr = cos_t + cs_row * D;
+    const __nv_bfloat16* sr = sin_t + cs_row * D;
+    const uint2 c_lo = __ldg(reinterpret_cast<const uint2*>(cr + 4 * c));
+    const uint2 c_hi = __ldg(reinterpret_cast<const uint2*>(cr + half + 4 * c));
+    const uint2 s_lo = __ldg(reinterpret_cast<const uint2*>(sr + 4 * c));
+    const uint2 s_hi = __ldg(reinterpret_cast<const uint2*>(sr + half + 4 * c));
+    const __nv_bfloat162* clo = reinterpret_cast<const __nv_bfloat162*>(&c_lo);
+    const __nv_bfloat162* chi = reinterpret_cast<const __nv_bfloat162*>(&c_hi);
+    const __nv_bfloat162* slo = reinterpret_cast<const __nv_bfloat162*>(&s_lo);
+    const __nv_bfloat162* shi = reinterpret_cast<const __nv_bfloat162*>(&s_hi);
+    float lo[4], hi[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float2 xx = __bfloat1622float2(xp[p]);  // x[2k], x[2k+1] with k = 4c + p
+      const float2 cl = __bfloat1622float2(clo[p >> 1]);
+      const float2 ch = __bfloat1622float2(chi[p >> 1]);
+      const float2 sl = __bfloat1622float2(slo[p >> 1]);
+      const float2 sh = __bfloat1622float2(shi[p >> 1]);
+      const float ckl = (p & 1) ? cl.y : cl.x, ckh = (p & 1) ? ch.y : ch.x;
+      const float skl = (p & 1) ? sl.y : sl.x, skh = (p & 1) ? sh.y : sh.x;
+      lo[p] = xx.x * ckl - xx.y * skl;
+      hi[p] = xx.y * ckh + xx.x * skh;
+    }
+    uint2 olo, ohi;
+    const __nv_bfloat162 a0 = __floats2bfloat162_rn(lo[0], lo[1]);
+    const __nv_bfloat162 a1 = __floats2bfloat162_rn(lo[2], lo[3]);
+    const __nv_bfloat162 b0 = __floats2bfloat162_rn(hi[0], hi[1]);
+    const __nv_bfloat162 b1 = __floats2bfloat162_rn(hi[2], hi[3]);
+    olo.x = *reinterpret_cast<const uint32_t*>(&a0);
+    olo.y = *reinterpret_cast<const uint32_t*>(&a1);
+    ohi.x = *reinterpret_cast<const uint32_t*>(&b0);
+    ohi.y = *reinterpret_cast<const uint32_t*>(&b1);
+    __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>((is_q ? qo : ko) + lrow * D8);
+    *reinterpret_cast<uint2*>(orow + 4 * c) = olo;
+    *reinterpret_cast<uint2*>(orow + half + 4 * c) = ohi;
+  }
+}
+
+// Scalar fallback for rope_dim not divisible by 8: one thread per rotation pair.
+__global__ void rope_pair_kernel(const __nv_bfloat16* __restrict__ q,
+                                 const __nv_bfloat16* __restrict__ k,
+                                 const __nv_bfloat16* __restrict__ cos_t,
+                                 const __nv_bfloat16* __restrict__ sin_t,
+                                 __nv_bfloat16* __restrict__ qo, __nv_bfloat16* __restrict__ ko,
+                                 int64_t q_rows, int64_t k_rows, int heads, int seq, int D) {
+  const int half = D >> 1;
+  const int64_t total = (q_rows + k_rows) * half;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / half;
+    const int kk = static_cast<int>(i - row * half);
+    const bool is_q = row < q_rows;
+    const int64_t lrow = is_q ? row : row - q_rows;
+    const int64_t cs_row =
+        is_q ? (lrow / (static_cast<int64_t>(seq) * heads)) * seq + lrow % seq : lrow;
+    const __nv_bfloat16* x = (is_q ? q : k) + lrow * D;
+    const float x0 = __bfloat162float(x[2 * kk]), x1 = __bfloat162float(x[2 * kk + 1]);
+    const __nv_bfloat16* cr = cos_t + cs_row * D;
+    const __nv_bfloat16* sr = sin_t + cs_row * D;
+    __nv_bfloat16* o = (is_q ? qo : ko) + lrow * D;
+    o[kk] = __float2bfloat16_rn(x0 * __bfloat162float(cr[kk]) - x1 * __bfloat162float(sr[kk]));
+    o[kk + half] = __float2bfloat16_rn(x1 * __bfloat162float(cr[kk + half]) +
+                                       x0 * __bfloat162float(sr[kk + half]));
+  }
+}
+
+int grid_cap(int64_t items, int per_block, int num_sms) {
+  const int64_t need = (items + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(num_sms) * 8;
+  return static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
+}
+
+}  // namespace
+}  // namespace ds
+
+extern "C" {
+
+int ds_rms_norm_strided(const void* input_bf16, int64_t in_stride, const float* weight,
+                        void* output_bf16, int64_t out_stride, int rows, int hidden_size,
+                        float eps, void* stream) {
+  DS_REQUIRE(hidden_size > 0 && hidden_size % 2 == 0,
+             "rms_norm: hidden_size must be even for bfloat162 vectorisation.");
+  DS_REQUIRE(rows >= 0, "rms_norm: rows must be >= 0");
+  DS_REQUIRE(in_stride >= hidden_size && out_stride >= hidden_size,
+             "rms_norm: row strides must be >= hidden_size");
+  if (rows == 0) return DS_OK;
+  DS_REQUIRE(input_bf16 && weight && output_bf16, "rms_norm: null pointer");
+  ds::DeviceInfo di;
+  DS_TRY(ds::device_info(&di));
+  const int vec_ok = (hidden_size % 8 == 0 && in_stride % 8 == 0 && out_stride % 8 == 0 &&
+                      ds::aligned16(input_bf16) && ds::aligned16(output_bf16) &&
+                      ds::aligned16(weight))
+                         ? 1
+                         : 0;
+  const int grid = ds::grid_cap(rows, 8, di.num_sms);
+  ds::rms_norm_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(input_bf16), in_stride, weight,
+      static_cast<__nv_bfloat16*>(output_bf16), out_stride, rows, hidden_size, eps, vec_ok);
+  DS_LAUNCH_CHECK("rms_norm_kernel");
+  return DS_OK;
+}
+
+int ds_rms_norm(const void* input_bf16, const float* weight, void* output_bf16, int rows,
+                int hidden_size, float eps, void* stream) {
+  return ds_rms_norm_strided(input_bf16, hidden_size, weight, output_bf16, hidden_size, rows,
+                             hidden_size, eps, stream);
+}
+
+int ds_rope(const void* q_pe_bf16, const void* k_pe_bf16, const void* cos_bf16,
+            const void* sin_bf16, void* q_out_bf16, void* k_out_bf16, int bsz, int heads,
+            int seq, int rope_dim, void* stream) {
+  DS_REQUIRE(rope_dim > 0 && rope_dim % 2 == 0, "rope: rope_dim must be even.");
+  DS_REQUIRE(bsz >= 0 && heads >= 1 && seq >= 0, "rope: bad shape");
+  const int64_t q_rows = static_cast<int64_t>(bsz) * heads * seq;
+  const int64_t k_rows = static_cast<int64_t>(bsz) * seq;
+  if (q_rows + k_rows == 0) return DS_OK;
+  DS_REQUIRE(q_pe_bf16 && k_pe_bf16 && cos_bf16 && sin_bf16 && q_out_bf16 && k_out_bf16,
+             "rope: null pointer");
+  ds::DeviceInfo di;
+  DS_TRY(ds::device_info(&di));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = rope_dim % 8 == 0 && ds::aligned16(q_pe_bf16) && ds::aligned16(k_pe_bf16) &&
+                   ds::aligned16(q_out_bf16) && ds::aligned16(k_out_bf16) &&
+                   (reinterpret_cast<uintptr_t>(cos_bf16) & 7u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(sin_bf16) & 7u) == 0;
+  if (vec) {
+    const int grid = ds::grid_cap((q_rows + k_rows) * (rope_dim / 8), 256, di.num_sms);
+    ds::rope_vec_kernel<<<grid, 256, 0, s>>>(
+        static_cast<const uint4*>(q_pe_bf16), static_cast<const uint4*>(k_pe_bf16),
+        static_cast<const __nv_bfloat16*>(cos_bf16), static_cast<const __nv_bfloat16*>(sin_bf16),
+        static_cast<uint4*>(q_out_bf16), static_cast<uint4*>(k_out_bf16), q_rows, k_rows, heads,
+        seq, rope_dim);
+  } else {
+    const int grid = ds::grid_cap((q_rows + k_rows) * (rope_dim / 2), 256, di.num_sms);
+    ds::rope_pair_kernel<<<grid, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(q_pe_bf16), static_cast<const __nv_bfloat16*>(k_pe_bf16),
+        static_cast<const __nv_bfloat16*>(cos_bf16), static_cast<const __nv_bfloat16*>(sin_bf16),
+        static_cast<__nv_bfloat16*>(q_out_bf16), static_cast<__nv_bfloat16*>(k_out_bf16), q_rows,
+        k_rows, heads, seq, rope_dim);
+  }
+  DS_LAUNCH_CHECK("rope_kernel");
+  return DS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,496 @@
+"""ds_kernels — drop-in for the reference's `ds_kernels` extension module.
+
+Same function names, argument names, defaults and return conventions as the reference
+binding (src/kernels/bindings.cu:186-301): `moe_routing`, `moe_scan`, `moe_dispatch`,
+`moe_combine`, `swiglu`, `moe_gemm1`, `moe_gemm2`, `rms_norm`, `kv_upproj`, `rope`,
+`run_hello`; plus the additive ops `moe_gemm1_swiglu` and `moe_layer_forward`.
+
+Every op validates its tensors with the reference's messages (raising RuntimeError, as
+TORCH_CHECK does), allocates outputs with torch on the input's device, and calls the
+C ABI of libds_kernels_sm100.so (include/ds_kernels.h) through ctypes on the current torch
+stream.  There is no fallback: if the library cannot be loaded, importing this module
+raises ImportError, and every op requires CUDA tensors.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import List, Optional, Sequence
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY_PATH = os.path.join(_HERE, "libds_kernels_sm100.so")
+
+DS_OK = 0
+DS_ERR_INVALID_ARG = 1
+DS_ERR_UNSUPPORTED = 2
+DS_ERR_CUDA = 3
+DS_ERR_TIMEOUT = 4
+DS_ERR_WORKSPACE = 5
+LAYER_NUM_EVENTS = 9
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_i64 = ctypes.c_int64
+_sz = ctypes.c_size_t
+_f = ctypes.c_float
+
+# name -> (restype, argtypes); must match include/ds_kernels.h.
+SIGNATURES = {
+    "ds_last_error": (ctypes.c_char_p, []),
+    "ds_version": (ctypes.c_char_p, []),
+    "ds_get_device_status": (_i, [ctypes.POINTER(_i)]),
+    "ds_clear_device_status": (_i, []),
+    "ds_run_hello": (_i, [_vp]),
+    "ds_moe_routing": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "ds_moe_scan": (_i, [_vp, _vp, _i, _vp]),
+    "ds_moe_dispatch_workspace_size": (_sz, [_i, _i, _i]),
+    "ds_moe_dispatch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "ds_moe_combine_workspace_size": (_sz, [_i, _i]),
+    "ds_moe_combine": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    "ds_swiglu": (_i, [_vp, _vp, _i, _i, _vp]),
+    "ds_moe_gemm1": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "ds_moe_gemm1_swiglu": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "ds_moe_gemm2": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "ds_rms_norm": (_i, [_vp, _vp, _vp, _i, _i, _f, _vp]),
+    "ds_rms_norm_strided": (_i, [_vp, _i64, _vp, _vp, _i64, _i, _i, _f, _vp]),
+    "ds_kv_upproj": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "ds_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "ds_moe_layer_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "ds_moe_layer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
+                                  _vp, _sz, _vp, _vp]),
+    "ds_debug_wait_probe": (_i, [ctypes.c_longlong, _vp]),
+}
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIBRARY_PATH):
+        raise ImportError(
+            f"ds_kernels: {LIBRARY_PATH} is missing; build it with "
+            "`python deepseek-v2-lite-cuda_b200/build.py` (or __graft_entry__.build())")
+    lib = ctypes.CDLL(LIBRARY_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_lib = _load()
+
+
+def library() -> ctypes.CDLL:
+    """The loaded libds_kernels_sm100.so handle (for direct C-ABI calls)."""
+    return _lib
+
+
+def version() -> str:
+    return _lib.ds_version().decode()
+
+
+def _check(status: int, op: str) -> None:
+    if status != DS_OK:
+        msg = _lib.ds_last_error().decode(errors="replace")
+        raise RuntimeError(f"{op}: {msg} (status {status})")
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+class _on_device:
+    """Make the tensor's device current for the duration of a C-ABI call."""
+
+    def __init__(self, t: torch.Tensor):
+        self.ctx = torch.cuda.device(t.device)
+
+    def __enter__(self):
+        self.ctx.__enter__()
+
+    def __exit__(self, *exc):
+        return self.ctx.__exit__(*exc)
+
+
+# --------------------------------------------------------------------------------------------
+def run_hello() -> None:
+    """Executes the hello world CUDA kernel (toolchain smoke test)."""
+    _check(_lib.ds_run_hello(torch.cuda.current_stream().cuda_stream), "run_hello")
+    torch.cuda.synchronize()
+
+
+def moe_routing(logits: torch.Tensor, top_k: int = 6) -> List[torch.Tensor]:
+    """Fused softmax and top-K MoE routing kernel.
+
+    Mirrors moe_routing_forward (src/kernels/moe/routing.cu:266-301).  Returns
+    [topk_indices int32 [T, top_k], topk_weights float32 [T, top_k], expert_counts int32 [E]].
+    Experts per token are ordered by descending logit, ties broken toward lower index.
+    """
+    _require(logits.is_cuda, "Input logits must reside on a CUDA device.")
+    _require(logits.is_contiguous(), "Input logits must be contiguous in memory.")
+    _require(logits.dtype == torch.float32, "Input logits must be of type float32.")
+    _require(logits.dim() == 2, "Input logits must be a 2-D tensor [tokens, experts].")
+    num_tokens, num_experts = logits.shape
+    _require(num_experts <= 64, "num_experts must not exceed 64.")
+    _require(1 <= top_k <= min(8, num_experts), "top_k must be in [1, min(8, num_experts)].")
+    dev = logits.device
+    idx = torch.empty((num_tokens, top_k), dtype=torch.int32, device=dev)
+    w = torch.empty((num_tokens, top_k), dtype=torch.float32, device=dev)
+    counts = torch.empty((num_experts,), dtype=torch.int32, device=dev)
+    with _on_device(logits):
+        _check(_lib.ds_moe_routing(_ptr(logits), _ptr(idx), _ptr(w), _ptr(counts), num_tokens,
+                                   num_experts, top_k, _stream(logits)), "moe_routing")
+    return [idx, w, counts]
+
+
+def moe_scan(expert_counts: torch.Tensor) -> torch.Tensor:
+    """Exclusive prefix sum of expert token counts -> expert_offsets int32 [E + 1].
+
+    Mirrors moe_scan_forward (src/kernels/moe/scan.cu:86-130) without its host syncs.
+    """
+    _require(expert_counts.is_cuda, "Input expert_counts must reside on a CUDA device.")
+    _require(expert_counts.is_contiguous(), "Input expert_counts must be contiguous in memory.")
+    _require(expert_counts.dtype == torch.int32, "Input expert_counts must be of type int32.")
+    _require(expert_counts.dim() == 1, "Input expert_counts must be a 1-D tensor [num_experts].")
+    num_experts = expert_counts.shape[0]
+    out = torch.empty((num_experts + 1,), dtype=torch.int32, device=expert_counts.device)
+    if num_experts == 0:
+        out.zero_()
+        return out
+    with _on_device(expert_counts):
+        _check(_lib.ds_moe_scan(_ptr(expert_counts), _ptr(out), num_experts,
+                                _stream(expert_counts)), "moe_scan")
+    return out
+
+
+def _check_tensor(t: torch.Tensor, name: str, dtype: torch.dtype, dtype_name: str, dim: int,
+                  shape_doc: str) -> None:
+    _require(t.is_cuda, f"{name} must reside on a CUDA device.")
+    _require(t.is_contiguous(), f"{name} must be contiguous in memory.")
+    _require(t.dtype == dtype, f"{name} must be of type {dtype_name}.")
+    _require(t.dim() == dim, f"{name} must be a {dim}-D tensor {shape_doc}.")
+
+
+def moe_dispatch(input: torch.Tensor, topk_indices: torch.Tensor, topk_weights: torch.Tensor,
+                 expert_offsets: torch.Tensor) -> List[torch.Tensor]:
+    """Scatters token hidden states into an expert-contiguous output buffer.
+
+    Mirrors moe_dispatch_forward (src/kernels/moe/dispatch.cu:156-218).  Returns
+    [dispatched bf16 [T*k, H], token_map int32 [T*k], dispatched_weights float32 [T*k]].
+    Slots inside an expert hold its tokens in ascending token order.
+    """
+    _check_tensor(input, "input", torch.bfloat16, "bfloat16", 2, "[num_tokens, hidden_size]")
+    _check_tensor(topk_indices, "topk_indices", torch.int32, "int32", 2, "[num_tokens, top_k]")
+    _check_tensor(topk_weights, "topk_weights", torch.float32, "float32", 2,
+                  "[num_tokens, top_k]")
+    _check_tensor(expert_offsets, "expert_offsets", torch.int32, "int32", 1,
+                  "[num_experts + 1]")
+    num_tokens, hidden = input.shape
+    top_k = topk_indices.shape[1]
+    num_experts = expert_offsets.shape[0] - 1
+    _require(hidden % 8 == 0, "hidden_size must be divisible by 8 for 128-bit vectorized access.")
+    total = num_tokens * top_k
+    dev = input.device
+    dispatched = torch.empty((total, hidden), dtype=torch.bfloat16, device=dev)
+    token_map = torch.empty((total,), dtype=torch.int32, device=dev)
+    dweights = torch.empty((total,), dtype=torch.float32, device=dev)
+    if total == 0:
+        return [dispatched, token_map, dweights]
+    ws_bytes = _lib.ds_moe_dispatch_workspace_size(num_tokens, num_experts, top_k)
+    ws = _workspace(ws_bytes, dev)
+    with _on_device(input):
+        _check(_lib.ds_moe_dispatch(_ptr(input), _ptr(topk_indices), _ptr(topk_weights),
+                                    _ptr(expert_offsets), _ptr(dispatched), _ptr(token_map),
+                                    _ptr(dweights), num_tokens, hidden, num_experts, top_k,
+                                    _ptr(ws), ws_bytes, _stream(input)), "moe_dispatch")
+    return [dispatched, token_map, dweights]
+
+
+def moe_combine(expert_output: torch.Tensor, token_map: torch.Tensor,
+                dispatched_weights: torch.Tensor, num_tokens: int) -> torch.Tensor:
+    """Accumulates weighted expert outputs back to token-ordered positions.
+
+    Mirrors moe_combine_forward (src/kernels/moe/combine.cu:107-176): f32 accumulation,
+    one bf16 rounding; token_map may hold any multiplicity.  Deterministic.
+    """
+    _check_tensor(expert_output, "expert_output", torch.bfloat16, "bfloat16", 2,
+                  "[total_slots, hidden_size]")
+    _check_tensor(token_map, "token_map", torch.int32, "int32", 1, "[total_slots]")
+    _check_tensor(dispatched_weights, "dispatched_weights", torch.float32, "float32", 1,
+                  "[total_slots]")
+    _require(num_tokens > 0, "num_tokens must be positive.")
+    total, hidden = expert_output.shape
+    dev = expert_output.device
+    out = torch.empty((num_tokens, hidden), dtype=torch.bfloat16, device=dev)
+    ws_bytes = _lib.ds_moe_combine_workspace_size(total, num_tokens)
+    ws = _workspace(ws_bytes, dev)
+    with _on_device(expert_output):
+        _check(_lib.ds_moe_combine(_ptr(expert_output), _ptr(token_map),
+                                   _ptr(dispatched_weights), _ptr(out), total, hidden,
+                                   num_tokens, _ptr(ws), ws_bytes, _stream(expert_output)),
+               "moe_combine")
+    return out
+
+
+def swiglu(input: torch.Tensor) -> torch.Tensor:
+    """SwiGLU activation: silu(gate_half) * up_half  ([S, 2I] bf16 -> [S, I] bf16).
+
+    Mirrors swiglu_forward (src/kernels/moe/swiglu.cu:142-170).
+    """
+    _require(input.is_cuda, "swiglu: input must be a CUDA tensor.")
+    _require(input.is_contiguous(), "swiglu: input must be contiguous.")
+    _require(input.dtype == torch.bfloat16, "swiglu: input must be bfloat16.")
+    _require(input.dim() == 2, "swiglu: input must be 2-D [total_tokens, 2*intermediate_size].")
+    _require(input.shape[1] % 2 == 0, "swiglu: input inner dimension must be even.")
+    rows, two_i = input.shape
+    inter = two_i // 2
+    out = torch.empty((rows, inter), dtype=torch.bfloat16, device=input.device)
+    if rows == 0:
+        return out
+    with _on_device(input):
+        _check(_lib.ds_swiglu(_ptr(input), _ptr(out), rows, inter, _stream(input)), "swiglu")
+    return out
+
+
+def _gemm_checks(a: torch.Tensor, w: torch.Tensor, off: torch.Tensor, tag: str,
+                 a_doc: str, w_doc: str) -> None:
+    _require(a.is_cuda and a.is_contiguous(), f"{tag}: {a_doc} must be a contiguous CUDA tensor.")
+    _require(a.dtype == torch.bfloat16, f"{tag}: {a_doc} must be bfloat16.")
+    _require(a.dim() == 2, f"{tag}: {a_doc} must be 2-D [total_slots, hidden_size].")
+    _require(w.is_cuda and w.is_contiguous(), f"{tag}: {w_doc} must be a contiguous CUDA tensor.")
+    _require(w.dtype == torch.bfloat16, f"{tag}: {w_doc} must be bfloat16.")
+    _require(w.dim() == 3, f"{tag}: {w_doc} must be 3-D.")
+    _require(off.is_cuda and off.is_contiguous(),
+             f"{tag}: expert_offsets must be a contiguous CUDA tensor.")
+    _require(off.dtype == torch.int32, f"{tag}: expert_offsets must be int32.")
+    _require(off.dim() == 1, f"{tag}: expert_offsets must be 1-D [num_experts + 1].")
+    _require(off.shape[0] == w.shape[0] + 1, f"{tag}: expert_offsets size must be num_experts + 1.")
+
+
+def _moe_gemm1(dispatched, packed_w1, expert_offsets, fused: bool) -> torch.Tensor:
+    _gemm_checks(dispatched, packed_w1, expert_offsets, "gemm1", "dispatched", "packed_w1")
+    total, hidden = dispatched.shape
+    num_experts, two_i, _ = packed_w1.shape
+    _require(packed_w1.shape[2] == hidden,
+             "gemm1: packed_w1 hidden_size dim does not match dispatched.")
+    cols = two_i // 2 if fused else two_i
+    out = torch.empty((total, cols), dtype=torch.bfloat16, device=dispatched.device)
+    if total == 0:
+        return out
+    fn = _lib.ds_moe_gemm1_swiglu if fused else _lib.ds_moe_gemm1
+    with _on_device(dispatched):
+        _check(fn(_ptr(dispatched), _ptr(packed_w1), _ptr(expert_offsets), _ptr(out), total,
+                  num_experts, hidden, two_i, _stream(dispatched)),
+               "moe_gemm1_swiglu" if fused else "moe_gemm1")
+    return out
+
+
+def moe_gemm1(dispatched: torch.Tensor, packed_w1: torch.Tensor,
+              expert_offsets: torch.Tensor) -> torch.Tensor:
+    """Batched gate+up projection for all active experts (tcgen05 grouped GEMM).
+
+    Mirrors moe_gemm1_forward (src/kernels/moe/gemm1.cu:167-227); offsets stay on device.
+    """
+    return _moe_gemm1(dispatched, packed_w1, expert_offsets, fused=False)
+
+
+def moe_gemm1_swiglu(dispatched: torch.Tensor, packed_w1: torch.Tensor,
+                     expert_offsets: torch.Tensor) -> torch.Tensor:
+    """GEMM1 with the SwiGLU epilogue fused: [S, H] -> [S, I] (new, additive op)."""
+    return _moe_gemm1(dispatched, packed_w1, expert_offsets, fused=True)
+
+
+def moe_gemm2(swiglu_out: torch.Tensor, w2: torch.Tensor,
+              expert_offsets: torch.Tensor) -> torch.Tensor:
+    """Batched down_proj for all active experts (tcgen05 grouped GEMM).
+
+    Mirrors moe_gemm2_forward (src/kernels/moe/gemm2.cu:136-195).
+    """
+    _gemm_checks(swiglu_out, w2, expert_offsets, "gemm2", "swiglu_out", "w2")
+    total, inter = swiglu_out.shape
+    num_experts, hidden, _ = w2.shape
+    _require(w2.shape[2] == inter, "gemm2: w2 intermediate dim does not match swiglu_out.")
+    out = torch.empty((total, hidden), dtype=torch.bfloat16, device=swiglu_out.device)
+    if total == 0:
+        return out
+    with _on_device(swiglu_out):
+        _check(_lib.ds_moe_gemm2(_ptr(swiglu_out), _ptr(w2), _ptr(expert_offsets), _ptr(out),
+                                 total, num_experts, inter, hidden, _stream(swiglu_out)),
+               "moe_gemm2")
+    return out
+
+
+def rms_norm(input: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """RMSNorm over the last dimension of a BF16 tensor (f32 weight).
+
+    Mirrors rms_norm_forward (src/kernels/mla/rms_norm.cu:158-192).
+    """
+    _require(input.is_cuda, "rms_norm: input must be a CUDA tensor.")
+    _require(weight.is_cuda, "rms_norm: weight must be a CUDA tensor.")
+    _require(input.is_contiguous(), "rms_norm: input must be contiguous.")
+    _require(input.dtype == torch.bfloat16, "rms_norm: input must be bfloat16.")
+    _require(weight.dtype == torch.float32,
+             "rms_norm: weight must be float32 (default nn.Parameter dtype).")
+    _require(input.dim() >= 2, "rms_norm: input must have at least 2 dimensions.")
+    hidden = input.shape[-1]
+    _require(weight.numel() == hidden,
+             f"rms_norm: weight size {weight.numel()} does not match input hidden_size {hidden}.")
+    _require(hidden % 2 == 0, "rms_norm: hidden_size must be even for bfloat162 vectorisation.")
+    weight = weight.contiguous()
+    rows = input.numel() // hidden if hidden else 0
+    out = torch.empty_like(input)
+    if rows == 0:
+        return out
+    with _on_device(input):
+        _check(_lib.ds_rms_norm(_ptr(input), _ptr(weight), _ptr(out), rows, hidden, float(eps),
+                                _stream(input)), "rms_norm")
+    return out
+
+
+def kv_upproj(normed_kv: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """KV up-projection: normed_kv @ kv_b_proj.weight.T (tcgen05 GEMM), keeps leading dims.
+
+    Mirrors kv_upproj_forward (src/kernels/mla/kv_upproj.cu:133-178).
+    """
+    _require(normed_kv.is_cuda and normed_kv.is_contiguous(),
+             "kv_upproj: normed_kv must be a contiguous CUDA tensor.")
+    _require(normed_kv.dtype == torch.bfloat16, "kv_upproj: normed_kv must be bfloat16.")
+    _require(normed_kv.dim() >= 2, "kv_upproj: normed_kv must have at least 2 dimensions.")
+    _require(weight.is_cuda and weight.is_contiguous(),
+             "kv_upproj: weight must be a contiguous CUDA tensor.")
+    _require(weight.dtype == torch.bfloat16, "kv_upproj: weight must be bfloat16.")
+    _require(weight.dim() == 2, "kv_upproj: weight must be 2-D [out_dim, kv_lora_rank].")
+    rank = normed_kv.shape[-1]
+    out_dim = weight.shape[0]
+    _require(weight.shape[1] == rank,
+             f"kv_upproj: weight inner dim {weight.shape[1]} must match normed_kv last dim {rank}.")
+    rows = normed_kv.numel() // rank if rank else 0
+    out = torch.empty((*normed_kv.shape[:-1], out_dim), dtype=torch.bfloat16,
+                      device=normed_kv.device)
+    if rows == 0:
+        return out
+    with _on_device(normed_kv):
+        _check(_lib.ds_kv_upproj(_ptr(normed_kv), _ptr(weight), _ptr(out), rows, rank, out_dim,
+                                 _stream(normed_kv)), "kv_upproj")
+    return out
+
+
+def rope(q_pe: torch.Tensor, k_pe: torch.Tensor, cos: torch.Tensor,
+         sin: torch.Tensor) -> List[torch.Tensor]:
+    """YaRN RoPE applied to q_pe and k_pe (interleave->half transform + rotation).
+
+    Mirrors rope_forward (src/kernels/mla/rope.cu:139-207) in a single launch; cos/sin are
+    broadcast over heads by index instead of being expanded.  Returns [q_rot, k_rot].
+    """
+    for t in (q_pe, k_pe, cos, sin):
+        _require(t.is_cuda and t.is_contiguous(), "rope: all inputs must be contiguous CUDA tensors.")
+        _require(t.dtype == torch.bfloat16, "rope: all inputs must be bfloat16.")
+    _require(q_pe.dim() == 4, "rope: q_pe must be 4-D [bsz, heads, seq, rope_dim].")
+    _require(k_pe.dim() == 4, "rope: k_pe must be 4-D [bsz, 1, seq, rope_dim].")
+    _require(cos.dim() == 4, "rope: cos must be 4-D [bsz, 1, seq, rope_dim].")
+    _require(sin.dim() == 4, "rope: sin must be 4-D [bsz, 1, seq, rope_dim].")
+    bsz, heads, seq, rope_dim = q_pe.shape
+    _require(k_pe.shape[0] == bsz and k_pe.shape[1] == 1 and k_pe.shape[2] == seq
+             and k_pe.shape[3] == rope_dim,
+             f"rope: k_pe shape {list(k_pe.shape)} incompatible with q_pe.")
+    _require(cos.shape[0] == bsz and cos.shape[1] == 1 and cos.shape[2] == seq
+             and cos.shape[3] == rope_dim, "rope: cos shape incompatible.")
+    _require(sin.shape[0] == bsz and sin.shape[1] == 1 and sin.shape[2] == seq
+             and sin.shape[3] == rope_dim, "rope: sin shape incompatible.")
+    _require(rope_dim % 2 == 0, "rope: rope_dim must be even.")
+    q_rot = torch.empty_like(q_pe)
+    k_rot = torch.empty_like(k_pe)
+    if q_pe.numel() + k_pe.numel() == 0:
+        return [q_rot, k_rot]
+    with _on_device(q_pe):
+        _check(_lib.ds_rope(_ptr(q_pe), _ptr(k_pe), _ptr(cos), _ptr(sin), _ptr(q_rot),
+                            _ptr(k_rot), bsz, heads, seq, rope_dim, _stream(q_pe)), "rope")
+    return [q_rot, k_rot]
+
+
+def moe_layer_workspace_size(num_tokens: int, hidden_size: int, num_experts: int, top_k: int,
+                             intermediate_size: int, shared_intermediate_size: int) -> int:
+    return int(_lib.ds_moe_layer_workspace_size(num_tokens, hidden_size, num_experts, top_k,
+                                                intermediate_size, shared_intermediate_size))
+
+
+def moe_layer_forward(router_logits: torch.Tensor, x: torch.Tensor, packed_w1: torch.Tensor,
+                      w2: torch.Tensor, shared_w1: Optional[torch.Tensor] = None,
+                      shared_w2: Optional[torch.Tensor] = None, top_k: int = 6,
+                      out: Optional[torch.Tensor] = None,
+                      workspace: Optional[torch.Tensor] = None,
+                      events: Optional[Sequence[torch.cuda.Event]] = None) -> torch.Tensor:
+    """Whole MoE layer in one C call (new, additive): routing -> dispatch -> grouped GEMMs
+    (+ shared expert) -> combine.  router_logits f32 [T, E], x bf16 [T, H], packed_w1 bf16
+    [E, 2I, H], w2 bf16 [E, H, I], shared_w1 bf16 [2Is, H] (gate rows then up rows),
+    shared_w2 bf16 [H, Is].  `events` (9 torch.cuda.Event) are recorded between phases.
+    """
+    _check_tensor(router_logits, "router_logits", torch.float32, "float32", 2, "[T, E]")
+    _check_tensor(x, "x", torch.bfloat16, "bfloat16", 2, "[T, H]")
+    _require(packed_w1.is_contiguous() and packed_w1.dtype == torch.bfloat16 and packed_w1.dim() == 3,
+             "packed_w1 must be a contiguous bf16 [E, 2I, H] tensor.")
+    _require(w2.is_contiguous() and w2.dtype == torch.bfloat16 and w2.dim() == 3,
+             "w2 must be a contiguous bf16 [E, H, I] tensor.")
+    T, H = x.shape
+    E = packed_w1.shape[0]
+    I = packed_w1.shape[1] // 2
+    _require(router_logits.shape == (T, E), "router_logits must be [T, num_experts].")
+    _require(w2.shape == (E, H, I), "w2 must be [E, H, I].")
+    Is = 0
+    if shared_w1 is not None or shared_w2 is not None:
+        _require(shared_w1 is not None and shared_w2 is not None,
+                 "give both shared expert weights or neither")
+        _require(shared_w1.is_contiguous() and shared_w1.dtype == torch.bfloat16
+                 and shared_w1.dim() == 2 and shared_w1.shape[1] == H,
+                 "shared_w1 must be a contiguous bf16 [2Is, H] tensor.")
+        Is = shared_w1.shape[0] // 2
+        _require(shared_w2.is_contiguous() and shared_w2.dtype == torch.bfloat16
+                 and tuple(shared_w2.shape) == (H, Is),
+                 "shared_w2 must be a contiguous bf16 [H, Is] tensor.")
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    if T == 0:
+        return out
+    need = moe_layer_workspace_size(T, H, E, top_k, I, Is)
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(need, x.device)
+    ev = None
+    if events is not None:
+        _require(len(events) == LAYER_NUM_EVENTS, f"events must hold {LAYER_NUM_EVENTS} events")
+        ev = (ctypes.c_void_p * LAYER_NUM_EVENTS)(*[e.cuda_event for e in events])
+    with _on_device(x):
+        _check(_lib.ds_moe_layer_forward(_ptr(router_logits), _ptr(x), _ptr(packed_w1), _ptr(w2),
+                                         _ptr(shared_w1), _ptr(shared_w2), _ptr(out), T, H, E,
+                                         top_k, I, Is, _ptr(workspace), workspace.numel(), ev,
+                                         _stream(x)), "moe_layer_forward")
+    return out
+
+
+def device_status() -> int:
+    """DS_OK or DS_ERR_TIMEOUT (set when an on-device bounded wait ran out). Synchronises."""
+    v = ctypes.c_int(0)
+    _check(_lib.ds_get_device_status(ctypes.byref(v)), "device_status")
+    return v.value
+
+
+def clear_device_status() -> None:
+    _check(_lib.ds_clear_device_status(), "clear_device_status")
+
+
+def debug_wait_probe(timeout_cycles: int) -> None:
+    """Launch the bounded-wait probe (a wait nothing completes); see include/ds_kernels.h."""
+    _check(_lib.ds_debug_wait_probe(int(timeout_cycles), torch.cuda.current_stream().cuda_stream),
+           "debug_wait_probe")

@@ -1,0 +1,126 @@
+"""Fused MoE forward (drop-in for src/kernels/moe_fused.py).
+
+Public API kept from the reference:
+  FusedMoELayer(moe_module)                      (moe_fused.py:161-216)
+  fused_moe_forward(hidden_states, gate_weight, experts, top_k=6, packed_w1=None, w2=None)
+                                                 (moe_fused.py:227-272)
+
+Per call: the router GEMM in f32 (F.linear(x.float(), W.float()), as moe_fused.py:131),
+then ONE C-ABI call (ds_moe_layer_forward) that runs routing -> plan -> dispatch ->
+tcgen05 grouped GEMM1 with fused SwiGLU -> grouped GEMM2 -> (shared expert) -> combine on
+the current stream, with no host synchronisation and no Python loop over experts.
+
+Difference from the reference: FusedMoELayer also runs the module's shared experts
+(src/reference/moe.py:72-74,106-107), which the reference pipeline drops, so its output
+equals DeepSeekMoE.forward for any n_shared_experts.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import ds_kernels
+from expert_prepack import prepack_experts, prepack_shared
+
+
+class _Workspace:
+    """Grow-only device workspace reused across calls on one device/stream."""
+
+    def __init__(self):
+        self.buf: Optional[torch.Tensor] = None
+
+    def get(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+        return self.buf
+
+
+def _layer(hidden_states, gate_weight, packed_w1, w2, shared_w1, shared_w2, top_k, ws,
+           events=None):
+    T, H = hidden_states.shape
+    logits = F.linear(hidden_states.float(), gate_weight.float(), None)
+    E, twoI, _ = packed_w1.shape
+    Is = 0 if shared_w1 is None else shared_w1.shape[0] // 2
+    need = ds_kernels.moe_layer_workspace_size(T, H, E, top_k, twoI // 2, Is)
+    return ds_kernels.moe_layer_forward(logits, hidden_states, packed_w1, w2, shared_w1,
+                                        shared_w2, top_k=top_k,
+                                        workspace=ws.get(need, hidden_states.device),
+                                        events=events)
+
+
+class FusedMoELayer(nn.Module):
+    """Drop-in replacement for DeepSeekMoE running the fused sm_100a pipeline.
+
+    Reads `gate.weight`, `num_experts_per_tok`, `experts` and (if present and not None)
+    `shared_experts` from `moe_module`; expert weights are pre-packed once.
+    """
+
+    def __init__(self, moe_module: nn.Module, verbose: bool = False):
+        super().__init__()
+        if not hasattr(moe_module, "gate") or not hasattr(moe_module, "experts"):
+            raise ValueError(
+                "FusedMoELayer: moe_module must have 'gate' and 'experts' attributes.")
+        self.gate_weight = moe_module.gate.weight.detach()
+        self.top_k = moe_module.num_experts_per_tok
+        self.num_experts = len(moe_module.experts)
+        self.packed_w1, self.w2 = prepack_experts(list(moe_module.experts))
+        shared = getattr(moe_module, "shared_experts", None)
+        if shared is not None:
+            self.shared_w1, self.shared_w2 = prepack_shared(shared, self.packed_w1.device)
+        else:
+            self.shared_w1 = self.shared_w2 = None
+        self._ws = _Workspace()
+        if verbose:
+            print(f"[FusedMoELayer] packed_w1 {tuple(self.packed_w1.shape)} "
+                  f"w2 {tuple(self.w2.shape)} shared={'yes' if shared is not None else 'no'}")
+
+    @classmethod
+    def from_packed(cls, gate_weight: torch.Tensor, packed_w1: torch.Tensor, w2: torch.Tensor,
+                    shared_w1: Optional[torch.Tensor] = None,
+                    shared_w2: Optional[torch.Tensor] = None, top_k: int = 6) -> "FusedMoELayer":
+        """Build from weights already in the packed layout (expert_prepack.py contract):
+        gate [E, H], packed_w1 bf16 [E, 2I, H], w2 bf16 [E, H, I], shared_w1 bf16 [2Is, H],
+        shared_w2 bf16 [H, Is]."""
+        self = cls.__new__(cls)
+        nn.Module.__init__(self)
+        self.gate_weight = gate_weight.detach()
+        self.top_k = top_k
+        self.num_experts = packed_w1.shape[0]
+        self.packed_w1, self.w2 = packed_w1.contiguous(), w2.contiguous()
+        self.shared_w1 = None if shared_w1 is None else shared_w1.contiguous()
+        self.shared_w2 = None if shared_w2 is None else shared_w2.contiguous()
+        self._ws = _Workspace()
+        return self
+
+    def forward(self, hidden_states: torch.Tensor, events=None) -> torch.Tensor:
+        assert hidden_states.is_cuda, "hidden_states must be on CUDA."
+        assert hidden_states.dtype == torch.bfloat16, "hidden_states must be BF16."
+        assert hidden_states.dim() == 2, "hidden_states must be 2-D [T, H]."
+        return _layer(hidden_states.contiguous(), self.gate_weight, self.packed_w1, self.w2,
+                      self.shared_w1, self.shared_w2, self.top_k, self._ws, events)
+
+
+_WEIGHT_CACHE: dict = {}
+_FN_WS = _Workspace()
+
+
+def fused_moe_forward(hidden_states: torch.Tensor, gate_weight: torch.Tensor, experts: list,
+                      top_k: int = 6, packed_w1: Optional[torch.Tensor] = None,
+                      w2: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Functional fused MoE forward (routed experts only, as the reference function).
+
+    Pre-packs `experts` on first use and caches the result keyed by id(experts).
+    """
+    assert hidden_states.is_cuda, "hidden_states must be on CUDA."
+    assert hidden_states.dim() == 2, "hidden_states must be [num_tokens, hidden_size]."
+    assert hidden_states.dtype == torch.bfloat16, "hidden_states must be BF16."
+    if packed_w1 is None or w2 is None:
+        key = id(experts)
+        if key not in _WEIGHT_CACHE:
+            _WEIGHT_CACHE[key] = prepack_experts(experts)
+        packed_w1, w2 = _WEIGHT_CACHE[key]
+    return _layer(hidden_states.contiguous(), gate_weight, packed_w1, w2, None, None, top_k,
+                  _FN_WS)

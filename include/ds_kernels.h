@@ -1,0 +1,206 @@
+/*
+ * ds_kernels.h — C ABI of libds_kernels_sm100.so, the B200 (sm_100a) implementation of
+ * DeepSeek-V2-Lite's MoE layer and MLA projection hot path.
+ *
+ * Every entry point takes raw device pointers, plain sizes and a CUDA stream passed as
+ * `void*` (a cudaStream_t; NULL = legacy default stream).  No entry point allocates device
+ * memory: scratch is passed in by the caller as (workspace, workspace_bytes), sized by the
+ * matching *_workspace_size() query.  All launches are asynchronous on `stream`; nothing
+ * synchronises with the host, so every entry point can be captured in a CUDA graph.
+ *
+ * Return value: DS_OK (0) or a DS_ERR_* code.  ds_last_error() returns a message for the
+ * last failure on the calling host thread.  Device-side failures (a bounded wait that ran
+ * out) are recorded in a per-device status word read by ds_get_device_status().
+ *
+ * Each declaration cites the reference interface it replaces (paths inside the reference
+ * project sahan974/DeepSeek-V2-Lite-CUDA).  Differences from the reference launchers:
+ *   - int status instead of `throw std::runtime_error`;
+ *   - expert offsets are DEVICE pointers (the reference GEMMs take a host array);
+ *   - scratch is caller-provided (the reference scan cudaMalloc's per call);
+ *   - routing/dispatch are deterministic: experts per token in descending logit order
+ *     (ties -> lower expert index); slots within an expert in ascending token order.
+ */
+#ifndef DS_KERNELS_H
+#define DS_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DS_API __attribute__((visibility("default")))
+#else
+#define DS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DS_OK 0
+#define DS_ERR_INVALID_ARG 1   /* bad shape / null pointer / misaligned pointer          */
+#define DS_ERR_UNSUPPORTED 2   /* valid arguments this build does not handle              */
+#define DS_ERR_CUDA 3          /* a CUDA runtime call failed                              */
+#define DS_ERR_TIMEOUT 4       /* device status: a bounded on-device wait ran out         */
+#define DS_ERR_WORKSPACE 5     /* workspace pointer null or smaller than required         */
+
+/* Message for the last failing call on this host thread ("" if none). */
+DS_API const char* ds_last_error(void);
+
+/* Library / build identification, e.g. "ds_kernels sm_100a 0.1". */
+DS_API const char* ds_version(void);
+
+/* Device status word: *status receives DS_OK or DS_ERR_TIMEOUT (set by a kernel whose
+ * bounded wait ran out).  Synchronises the device.  ds_clear_device_status() resets it. */
+DS_API int ds_get_device_status(int* status);
+DS_API int ds_clear_device_status(void);
+
+/* Replaces run_hello (src/kernels/hello.cu:11-21, bindings.cu:187-189): prints one line
+ * from a kernel; toolchain smoke test only. */
+DS_API int ds_run_hello(void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K1 routing.  Replaces launch_moe_routing (src/kernels/include/moe/routing.h:27-36,
+ * src/kernels/moe/routing.cu:230-260) and moe_routing_forward (routing.cu:266-301).
+ * logits f32 [num_tokens, num_experts] -> topk_indices i32 [num_tokens, top_k] (descending
+ * logit, ties -> lower index), topk_weights f32 [num_tokens, top_k] (softmax values, no
+ * renormalisation), expert_counts i32 [num_experts] (zeroed and filled here).
+ * num_experts <= 64, 1 <= top_k <= min(8, num_experts). */
+DS_API int ds_moe_routing(const float* logits, int32_t* topk_indices, float* topk_weights,
+                   int32_t* expert_counts, int num_tokens, int num_experts, int top_k,
+                   void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K2 scan.  Replaces launch_moe_scan (src/kernels/include/moe/scan.h:31-36,
+ * src/kernels/moe/scan.cu:33-75) and moe_scan_forward (scan.cu:86-130).
+ * expert_offsets[i] = sum(expert_counts[0..i-1]); expert_offsets[num_experts] = total.
+ * No host synchronisation, no allocation.  num_experts >= 1. */
+DS_API int ds_moe_scan(const int32_t* expert_counts, int32_t* expert_offsets, int num_experts,
+                void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K3 dispatch.  Replaces launch_moe_dispatch (src/kernels/include/moe/dispatch.h:44-57,
+ * src/kernels/moe/dispatch.cu:106-139) and moe_dispatch_forward (dispatch.cu:156-218).
+ * Row for (token t, pick j) with expert e = topk_indices[t, j]:
+ *   slot = expert_offsets[e] + #{t' < t routed to e}
+ * dispatched[slot] = input[t]; token_map[slot] = t; dispatched_weights[slot] = w[t, j].
+ * Deterministic (the reference claims slots with atomics).  hidden_size % 8 == 0.
+ * The reference's expert_cursor scratch is replaced by `workspace`. */
+DS_API size_t ds_moe_dispatch_workspace_size(int num_tokens, int num_experts, int top_k);
+DS_API int ds_moe_dispatch(const void* input_bf16, const int32_t* topk_indices,
+                    const float* topk_weights, const int32_t* expert_offsets,
+                    void* dispatched_bf16, int32_t* token_map, float* dispatched_weights,
+                    int num_tokens, int hidden_size, int num_experts, int top_k,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K7 combine.  Replaces launch_moe_combine (src/kernels/include/moe/combine.h:41-49; a
+ * throwing stub at combine.cu:80-93) and moe_combine_forward (combine.cu:107-176).
+ * final[t] = bf16( sum over slots s with token_map[s] == t, in ascending s, of
+ *                  f32(expert_output[s]) * dispatched_weights[s] ),   0 for tokens with
+ * no slot.  token_map may hold any multiplicity; entries outside [0, num_tokens) are
+ * ignored.  Deterministic (the reference accumulates with f32 atomics). */
+DS_API size_t ds_moe_combine_workspace_size(int total_slots, int num_tokens);
+DS_API int ds_moe_combine(const void* expert_output_bf16, const int32_t* token_map,
+                   const float* dispatched_weights, void* final_output_bf16,
+                   int total_slots, int hidden_size, int num_tokens,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K5 swiglu.  Replaces launch_swiglu (src/kernels/include/moe/swiglu.h:26-32,
+ * src/kernels/moe/swiglu.cu:114-130) and swiglu_forward (swiglu.cu:142-170).
+ * out[r, j] = bf16( silu(f32 in[r, j]) * f32 in[r, j + I] ).  I even. */
+DS_API int ds_swiglu(const void* input_bf16, void* output_bf16, int total_tokens,
+              int intermediate_size, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K4 grouped GEMM1.  Replaces launch_moe_gemm1 (src/kernels/include/moe/gemm1.h:25-34,
+ * src/kernels/moe/gemm1.cu:84-155) and moe_gemm1_forward (gemm1.cu:167-227).
+ * For each expert e: out[off[e]:off[e+1]] = dispatched[off[e]:off[e+1]] @ packed_w1[e]^T.
+ * packed_w1 bf16 [num_experts, 2I, H] (gate rows then up rows), out bf16 [S, 2I].
+ * expert_offsets is a DEVICE pointer [num_experts+1].  Rows outside [off[0], off[E]) are
+ * zeroed.  tcgen05/TMEM tensor cores.  H % 8 == 0, I % 128 == 0. */
+DS_API int ds_moe_gemm1(const void* dispatched_bf16, const void* packed_w1_bf16,
+                 const int32_t* expert_offsets, void* gemm1_out_bf16, int total_slots,
+                 int num_experts, int hidden_size, int double_intermed, void* stream);
+
+/* New (additive) op: GEMM1 with the SwiGLU epilogue fused: out bf16 [S, I] equals
+ * ds_swiglu(ds_moe_gemm1(...)) except that the gate/up values are not rounded to bf16
+ * before the activation. */
+DS_API int ds_moe_gemm1_swiglu(const void* dispatched_bf16, const void* packed_w1_bf16,
+                        const int32_t* expert_offsets, void* swiglu_out_bf16,
+                        int total_slots, int num_experts, int hidden_size,
+                        int double_intermed, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K6 grouped GEMM2.  Replaces launch_moe_gemm2 (src/kernels/include/moe/gemm2.h:25-34,
+ * src/kernels/moe/gemm2.cu:75-124) and moe_gemm2_forward (gemm2.cu:136-195).
+ * For each expert e: out[off[e]:off[e+1]] = swiglu_out[...] @ w2[e]^T.
+ * w2 bf16 [num_experts, H, I], out bf16 [S, H].  I % 8 == 0, H % 256 == 0. */
+DS_API int ds_moe_gemm2(const void* swiglu_out_bf16, const void* w2_bf16,
+                 const int32_t* expert_offsets, void* gemm2_out_bf16, int total_slots,
+                 int num_experts, int intermediate_size, int hidden_size, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K8 RMSNorm.  Replaces launch_rms_norm (src/kernels/include/mla/rms_norm.h:27-35,
+ * src/kernels/mla/rms_norm.cu:126-144) and rms_norm_forward (rms_norm.cu:158-192).
+ * out[r] = bf16( weight * x[r] * rsqrt(mean(x[r]^2) + eps) ), f32 weight.  hidden even.
+ * in_stride / out_stride are row strides in elements (hidden_size for contiguous rows). */
+DS_API int ds_rms_norm(const void* input_bf16, const float* weight, void* output_bf16, int rows,
+                int hidden_size, float eps, void* stream);
+DS_API int ds_rms_norm_strided(const void* input_bf16, int64_t in_stride, const float* weight,
+                        void* output_bf16, int64_t out_stride, int rows, int hidden_size,
+                        float eps, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K9 kv up-projection.  Replaces launch_kv_upproj (src/kernels/include/mla/kv_upproj.h:
+ * 30-38, src/kernels/mla/kv_upproj.cu:77-119) and kv_upproj_forward (kv_upproj.cu:
+ * 133-178): out bf16 [rows, out_dim] = normed bf16 [rows, K] @ weight bf16 [out_dim, K]^T.
+ * tcgen05/TMEM tensor cores.  K % 8 == 0, out_dim % 256 == 0. */
+DS_API int ds_kv_upproj(const void* normed_kv_bf16, const void* weight_bf16, void* kv_up_bf16,
+                 int rows, int kv_lora_rank, int out_dim, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * K10 RoPE.  Replaces launch_rope (src/kernels/include/mla/rope.h:33-41,
+ * src/kernels/mla/rope.cu:101-119) and rope_forward (rope.cu:139-207), in one launch for
+ * q and k.  q_pe [bsz, heads, seq, D], k_pe [bsz, 1, seq, D], cos/sin [bsz, 1, seq, D]
+ * (pre-indexed by position; broadcast over heads by index, not copied).  For k < D/2:
+ *   out[k]       = x[2k]   * cos[k]       - x[2k+1] * sin[k]
+ *   out[k + D/2] = x[2k+1] * cos[k + D/2] + x[2k]   * sin[k + D/2]      (f32, one rounding)
+ * D even. */
+DS_API int ds_rope(const void* q_pe_bf16, const void* k_pe_bf16, const void* cos_bf16,
+            const void* sin_bf16, void* q_out_bf16, void* k_out_bf16, int bsz, int heads,
+            int seq, int rope_dim, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Fused MoE layer (new, additive; the pipeline of src/kernels/moe_fused.py:118-154 plus the
+ * shared expert of src/reference/moe.py:72-74,106-107 that the reference pipeline drops).
+ * router_logits f32 [T, E] (x @ gate^T in f32), x bf16 [T, H], packed_w1 bf16 [E, 2I, H],
+ * w2 bf16 [E, H, I], shared_w1 bf16 [2*Is, H] (gate rows then up rows) and shared_w2 bf16
+ * [H, Is] or both NULL (no shared expert), out bf16 [T, H].
+ * `events`: NULL, or DS_LAYER_NUM_EVENTS cudaEvent_t handles recorded on `stream` before
+ * the first kernel and after each phase (routing, plan, dispatch, gemm1, gemm2, shared1,
+ * shared2, combine) for per-kernel timing. */
+#define DS_LAYER_NUM_EVENTS 9
+DS_API size_t ds_moe_layer_workspace_size(int num_tokens, int hidden_size, int num_experts,
+                                   int top_k, int intermediate_size,
+                                   int shared_intermediate_size);
+DS_API int ds_moe_layer_forward(const float* router_logits, const void* x_bf16,
+                         const void* packed_w1_bf16, const void* w2_bf16,
+                         const void* shared_w1_bf16, const void* shared_w2_bf16,
+                         void* out_bf16, int num_tokens, int hidden_size, int num_experts,
+                         int top_k, int intermediate_size, int shared_intermediate_size,
+                         void* workspace, size_t workspace_bytes, void** events,
+                         void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Failure-detection probe (no reference counterpart): launches one CTA that waits on an
+ * mbarrier nothing arrives on, through the same bounded-wait routine the GEMM pipeline
+ * uses, with a limit of `timeout_cycles` SM clock cycles.  The wait runs out, the kernel
+ * sets the device status to DS_ERR_TIMEOUT and returns; the context stays usable. */
+DS_API int ds_debug_wait_probe(long long timeout_cycles, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DS_KERNELS_H */
