@@ -233,8 +233,10 @@ def run_ours(args, rank, world, local_rank):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
+    torch.cuda.nvtx.range_push("ds_timed")
     for s in range(args.steps):
         step(ev[s])
+    torch.cuda.nvtx.range_pop()
     t1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -365,6 +367,73 @@ def op_report(path, dev):
                             "frac_bf16": round(fl / t / 1e12 / pk["bf16"], 3)}) + "\n")
 
 
+def kernel_case(name, reps=2):
+    """Run one kernel at its BASELINE size `reps` times with few launches before it (for
+    `ncu -k ... -s 1 -c 1`).  Inputs come from the real pipeline where the kernel consumes
+    pipeline outputs (routing -> dispatch -> GEMMs)."""
+    import ds_kernels
+    import synthetic
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if name in ("gemm1", "gemm2", "dispatch"):
+        T = T_GLOBAL
+        g = torch.Generator(device=dev).manual_seed(5)
+        x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        gate = (torch.randn(E, H, generator=g, device=dev) * 0.02)
+        logits = F.linear(x.float(), gate)
+        idx, w, counts = ds_kernels.moe_routing(logits, K)
+        off = ds_kernels.moe_scan(counts)
+        if name == "dispatch":
+            for _ in range(reps):
+                ds_kernels.moe_dispatch(x, idx, w, off)
+        else:
+            disp, tm, dw = ds_kernels.moe_dispatch(x, idx, w, off)
+            if name == "gemm1":
+                w1 = (torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                for _ in range(reps):
+                    ds_kernels.moe_gemm1_swiglu(disp, w1, off)
+            else:
+                h = torch.randn(T * K, I, generator=g, device=dev).to(torch.bfloat16)
+                w2 = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+                for _ in range(reps):
+                    ds_kernels.moe_gemm2(h, w2, off)
+    elif name in ("routing", "combine"):
+        T = 16384
+        logits = synthetic.zipf_logits(T, E, 11, dev)
+        if name == "routing":
+            for _ in range(reps):
+                ds_kernels.moe_routing(logits, K)
+        else:
+            idx, w, counts = ds_kernels.moe_routing(logits, K)
+            off = ds_kernels.moe_scan(counts)
+            x = torch.randn(T, H, device=dev).to(torch.bfloat16)
+            disp, tm, dw = ds_kernels.moe_dispatch(x, idx, w, off)
+            for _ in range(reps):
+                ds_kernels.moe_combine(disp, tm, dw, T)
+    elif name in ("rms_norm", "rope", "kv_upproj"):
+        M = 4 * 4096
+        lat = torch.randn(M, 512, device=dev).to(torch.bfloat16)
+        if name == "rms_norm":
+            wn = torch.rand(512, device=dev) + 0.5
+            for _ in range(reps):
+                ds_kernels.rms_norm(lat, wn)
+        elif name == "rope":
+            q = torch.randn(4, 16, 4096, 64, device=dev).to(torch.bfloat16)
+            k = torch.randn(4, 1, 4096, 64, device=dev).to(torch.bfloat16)
+            cs = torch.randn(4, 1, 4096, 64, device=dev).to(torch.bfloat16)
+            for _ in range(reps):
+                ds_kernels.rope(q, k, cs, cs)
+        else:
+            wkv = (torch.randn(4096, 512, device=dev) * 0.02).to(torch.bfloat16)
+            for _ in range(reps):
+                ds_kernels.kv_upproj(lat, wkv)
+    else:
+        raise SystemExit(f"unknown kernel case {name}")
+    torch.cuda.synchronize()
+    assert ds_kernels.device_status() == ds_kernels.DS_OK
+    print(f"kernel case {name}: ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -373,7 +442,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--op-report", default=None)
+    ap.add_argument("--kernel-case", default=None,
+                    choices=["gemm1", "gemm2", "dispatch", "routing", "combine",
+                             "rms_norm", "rope", "kv_upproj"],
+                    help="run one kernel at its BASELINE size twice (profiling) and exit")
     args = ap.parse_args()
+    if args.kernel_case:
+        kernel_case(args.kernel_case)
+        return
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -470,6 +470,9 @@ def moe_layer_forward(router_logits: torch.Tensor, x: torch.Tensor, packed_w1: t
     ev = None
     if events is not None:
         _require(len(events) == LAYER_NUM_EVENTS, f"events must hold {LAYER_NUM_EVENTS} events")
+        st = torch.cuda.current_stream(x.device)
+        for e in events:  # torch creates events lazily; a record makes the handle valid
+            e.record(st)
         ev = (ctypes.c_void_p * LAYER_NUM_EVENTS)(*[e.cuda_event for e in events])
     with _on_device(x):
         _check(_lib.ds_moe_layer_forward(_ptr(router_logits), _ptr(x), _ptr(packed_w1), _ptr(w2),

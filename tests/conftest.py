@@ -42,3 +42,18 @@ def pytest_collection_modifyitems(config, items):
 @pytest.fixture(scope="session")
 def golden_dir():
     return GOLDEN
+
+
+def assert_bf16_close(out, ref, atol, rel_l2_max=1e-2):
+    """bf16 output vs f32 reference: |out - ref| <= atol + 2^-8 |ref| elementwise (2^-8 is the
+    relative half-ulp of bf16 round-to-nearest, so large outputs are held to their own
+    precision) and relative L2 error <= rel_l2_max."""
+    import torch
+    o = out.float().cpu()
+    r = ref.float().cpu()
+    err = (o - r).abs()
+    bound = atol + (2.0 ** -8) * r.abs()
+    worst = (err - bound).max().item()
+    rel = (torch.linalg.vector_norm(o - r) / torch.linalg.vector_norm(r).clamp_min(1e-30)).item()
+    assert worst <= 0 and rel <= rel_l2_max, (
+        f"max excess over atol+2^-8|ref|: {worst:.3e}, max-abs {err.max().item():.3e}, rel-L2 {rel:.3e}")

@@ -5,8 +5,9 @@ tests/test_moe_combine_kernel.py and tests/test_swiglu_kernel.py of the referenc
 bit-exact checks where the reference only compared sets.
 
 Tolerances: integer outputs bit-exact; routing weights atol 1e-6 (f32 softmax, 1 ulp of
-exp/divide); bf16 outputs max-abs <= 2e-2 and rel-L2 <= 1e-2 against the f32 oracle
-(BASELINE), plus the reference's own atol where it is tighter.
+exp/divide); bf16 outputs |out - ref| <= atol + 2^-8 |ref| (atol = the reference test's:
+2e-2 single-slot combine, 5e-2 multi-slot combine, 1e-2 swiglu; 2^-8 = bf16 relative
+half-ulp) and rel-L2 <= 1e-2 against the f32 oracle.
 """
 import os
 
@@ -14,6 +15,7 @@ import pytest
 import torch
 
 import oracle
+from conftest import assert_bf16_close
 
 pytestmark = pytest.mark.gpu
 
@@ -159,9 +161,7 @@ def _check_combine(eo, tm, dw, T, atol):
     out = ds().moe_combine(eo.cuda(), tm.cuda(), dw.cuda(), T)
     ref = oracle.combine(eo, tm, dw, T)
     assert out.shape == (T, eo.shape[1]) and out.dtype == torch.bfloat16
-    d = (out.float().cpu() - ref).abs().max().item()
-    assert d <= atol, d
-    assert rel_l2(out, ref) <= 1e-2
+    assert_bf16_close(out, ref, atol)
     return out
 
 
@@ -177,7 +177,7 @@ def test_combine_multi_slot(T):
     g = torch.Generator().manual_seed(1)
     eo = torch.randn(T * K, H, generator=g).to(torch.bfloat16)
     tm = torch.repeat_interleave(torch.arange(T, dtype=torch.int32), K)
-    _check_combine(eo, tm, torch.rand(T * K, generator=g), T, 2e-2)
+    _check_combine(eo, tm, torch.rand(T * K, generator=g), T, 5e-2)
 
 
 @pytest.mark.parametrize("T", [1, 32, 128])
@@ -186,7 +186,7 @@ def test_combine_arbitrary_multiplicity(T):
     S = T * K
     eo = torch.randn(S, H, generator=g).to(torch.bfloat16)
     tm = torch.randint(0, T, (S,), generator=g, dtype=torch.int32)
-    _check_combine(eo, tm, torch.rand(S, generator=g), T, 2e-2)
+    _check_combine(eo, tm, torch.rand(S, generator=g), T, 5e-2)
 
 
 def test_combine_heavy_token_and_empty_tokens():
@@ -203,7 +203,7 @@ def test_combine_known_answer(golden_dir):
     c = torch.load(os.path.join(golden_dir, "known_answers.pt"), weights_only=False)["combine"]
     # H=64 in the fixture
     out = ds().moe_combine(c["eo"].cuda(), c["token_map"].cuda(), c["dw"].cuda(), c["T"])
-    assert (out.float().cpu() - c["out"]).abs().max().item() <= 2e-2
+    assert_bf16_close(out, c["out"], 2e-2)
 
 
 @pytest.mark.parametrize("T", [1, 32, 128])
@@ -234,8 +234,7 @@ def test_route_dispatch_combine_end_to_end(T):
     logits, x, idx, w, counts, offsets, disp, tmap, dw = _pipeline(T, seed=7)
     out = ds().moe_combine(disp, tmap, dw, T)
     ref = x.float() * w.cpu().sum(1, keepdim=True)
-    assert (out.float().cpu() - ref).abs().max().item() <= 5e-2
-    assert rel_l2(out, ref) <= 1e-2
+    assert_bf16_close(out, ref, 2e-2)
 
 
 # ------------------------------------------------------------------------------ swiglu
@@ -246,13 +245,12 @@ def test_swiglu(rows):
     out = ds().swiglu(x.cuda())
     ref = oracle.swiglu(x)
     assert out.shape == (rows, 1408)
-    assert (out.float().cpu() - ref).abs().max().item() <= 1e-2
-    assert rel_l2(out, ref) <= 1e-2
+    assert_bf16_close(out, ref, 1e-2)
 
 
 def test_swiglu_odd_width_and_empty():
     x = (torch.rand(5, 2 * 6) * 4 - 2).to(torch.bfloat16)
     out = ds().swiglu(x.cuda())
-    assert (out.float().cpu() - oracle.swiglu(x)).abs().max().item() <= 1e-2
+    assert_bf16_close(out, oracle.swiglu(x), 1e-2)
     e = ds().swiglu(torch.empty(0, 2816, dtype=torch.bfloat16).cuda())
     assert e.shape == (0, 1408)
