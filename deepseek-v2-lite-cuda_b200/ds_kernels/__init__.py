@@ -47,6 +47,7 @@ SIGNATURES = {
     "ds_moe_scan": (_i, [_vp, _vp, _i, _vp]),
     "ds_moe_dispatch_workspace_size": (_sz, [_i, _i, _i]),
     "ds_moe_dispatch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "ds_moe_dispatch_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "ds_moe_combine_workspace_size": (_sz, [_i, _i]),
     "ds_moe_combine": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "ds_swiglu": (_i, [_vp, _vp, _i, _i, _vp]),

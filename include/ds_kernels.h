@@ -92,6 +92,24 @@ DS_API int ds_moe_dispatch(const void* input_bf16, const int32_t* topk_indices,
                     int num_tokens, int hidden_size, int num_experts, int top_k,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free dispatch (no counterpart in the reference).  Same arguments, outputs and
+ * ordering as ds_moe_dispatch, minus the workspace: for callers that cannot allocate device
+ * memory where they call this (a serving loop that keeps the CUDA allocator off its hot
+ * path, a binding that only holds plain pointers, code running while other work is being
+ * captured into a CUDA graph).  Its scratch is one fixed 2.5 MiB array in this library's
+ * device memory, reserved on every GPU that loads the library until the process exits.
+ * Limit: num_tokens <= DS_NOALLOC_MAX_TOKENS (else DS_ERR_UNSUPPORTED, nothing launched),
+ * num_experts <= 64, top_k <= 8.  All calls on a device share that array: calls that may
+ * overlap on the GPU (unordered streams, several host threads) race and corrupt each
+ * other's results, so order them on one stream.  The first call on each device looks up
+ * the array's address (one-time set-up); make it before any stream capture begins. */
+#define DS_NOALLOC_MAX_TOKENS 65536
+DS_API int ds_moe_dispatch_noalloc(const void* input_bf16, const int32_t* topk_indices,
+                                   const float* topk_weights, const int32_t* expert_offsets,
+                                   void* dispatched_bf16, int32_t* token_map,
+                                   float* dispatched_weights, int num_tokens, int hidden_size,
+                                   int num_experts, int top_k, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * K7 combine.  Replaces launch_moe_combine (src/kernels/include/moe/combine.h:41-49; a
  * throwing stub at combine.cu:80-93) and moe_combine_forward (combine.cu:107-176).
