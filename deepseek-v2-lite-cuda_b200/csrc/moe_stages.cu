@@ -1,0 +1,270 @@
+// Composable stages of the MoE layer, exported so that a caller can put a collective between
+// them (expert parallelism: dispatch -> all-to-all -> expert MLP -> all-to-all -> combine).
+// Each stage is one or more launches on the caller's stream, with no host synchronisation.
+#include "kernels.cuh"
+
+namespace ds {
+namespace {
+
+// Receive-side plan for expert parallelism.  counts[s * El + e] = rows that source rank s
+// sends for local expert e; received rows arrive source-major (all of source 0's rows,
+// expert-major inside, then source 1's, ...).  Produces expert-major offsets [El+1] and, for
+// every expert-major row i, the source-major row it comes from (row_map[i]).
+__global__ void __launch_bounds__(1024)
+    ep_offsets_kernel(const int32_t* __restrict__ counts, int N, int El,
+                      int32_t* __restrict__ exp_offsets, int32_t* __restrict__ seg_src,
+                      int32_t* __restrict__ seg_exp) {
+  // seg_src[s*El+e]: source-major start of segment (s, e); seg_exp[s*El+e]: expert-major start
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int s = 0; s < N; ++s)
+      for (int e = 0; e < El; ++e) {
+        seg_src[s * El + e] = run;
+        run += counts[s * El + e];
+      }
+    run = 0;
+    for (int e = 0; e < El; ++e) {
+      exp_offsets[e] = run;
+      for (int s = 0; s < N; ++s) {
+        seg_exp[s * El + e] = run;
+        run += counts[s * El + e];
+      }
+    }
+    exp_offsets[El] = run;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    ep_rowmap_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ seg_src,
+                     const int32_t* __restrict__ seg_exp, int segs, int R,
+                     int32_t* __restrict__ row_map) {
+  extern __shared__ int32_t sm[];
+  int32_t* ssrc = sm;
+  int32_t* sexp = sm + segs + 1;
+  for (int i = threadIdx.x; i < segs; i += blockDim.x) {
+    ssrc[i] = seg_src[i];
+    sexp[i] = seg_exp[i];
+  }
+  if (threadIdx.x == 0) ssrc[segs] = R;
+  __syncthreads();
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < R; r += gridDim.x * blockDim.x) {
+    // segment containing source-major row r: last seg with ssrc[seg] <= r and nonempty
+    int lo = 0, hi = segs;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (ssrc[mid] <= r) lo = mid;
+      else hi = mid;
+    }
+    row_map[sexp[lo] + (r - ssrc[lo])] = r;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    gather_rows_kernel(const uint4* __restrict__ src, const int32_t* __restrict__ map, int R,
+                       int H8, uint4* __restrict__ dst) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
+    const uint4* s = src + static_cast<int64_t>(__ldg(map + r)) * H8;
+    uint4* d = dst + static_cast<int64_t>(r) * H8;
+    for (int c = lane; c < H8; c += 32) d[c] = __ldg(s + c);
+  }
+}
+
+int grid_cap(int64_t items, int per_block, int num_sms) {
+  const int64_t need = (items + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(num_sms) * 8;
+  return static_cast<int>(need < cap ? (need > 0 ? need : 1) : cap);
+}
+
+gemm::Problem mlp_gemm1(const void* A, int64_t rows, int H, const void* w1, int64_t w1_rows,
+                        const int32_t* offsets, int groups, int I, void* h) {
+  gemm::Problem p{};
+  p.A = A;
+  p.a_rows = rows;
+  p.K = H;
+  p.B = w1;
+  p.b_rows = w1_rows;
+  p.offsets = offsets;
+  p.groups = groups;
+  p.n_tiles = I / 128;
+  p.b_rows_per_group = 2 * I;
+  p.b_tile_stride = 128;
+  p.b_half1_off = I;
+  p.weight_group_mod = groups;
+  p.out = h;
+  p.ldo = I;
+  p.epilogue = gemm::kSwiGLU;
+  p.out_row_map = nullptr;
+  return p;
+}
+
+gemm::Problem mlp_gemm2(const void* h, int64_t rows, int I, const void* w2, int64_t w2_rows,
+                        const int32_t* offsets, int groups, int H, void* out,
+                        const int32_t* row_map) {
+  gemm::Problem p{};
+  p.A = h;
+  p.a_rows = rows;
+  p.K = I;
+  p.B = w2;
+  p.b_rows = w2_rows;
+  p.offsets = offsets;
+  p.groups = groups;
+  p.n_tiles = H / 256;
+  p.b_rows_per_group = H;
+  p.b_tile_stride = 256;
+  p.b_half1_off = 128;
+  p.weight_group_mod = groups;
+  p.out = out;
+  p.ldo = H;
+  p.epilogue = gemm::kPlain;
+  p.out_row_map = row_map;
+  return p;
+}
+
+}  // namespace
+}  // namespace ds
+
+using ds::fail;
+
+extern "C" {
+
+size_t ds_moe_route_dispatch_workspace_size(int num_tokens, int num_experts, int top_k) {
+  ds::Carve c(nullptr, 0);
+  const size_t nblk = static_cast<size_t>(ds::route_blocks(num_tokens));
+  c.take<int32_t>(nblk * num_experts);                       // hist
+  c.take<int32_t>(nblk * num_experts);                       // base
+  c.take<int32_t>(static_cast<size_t>(num_tokens) * top_k);  // rank
+  return ds::align_up(c.used, 256);
+}
+
+int ds_moe_route_dispatch(const float* router_logits, const void* x_bf16, int num_tokens,
+                          int hidden_size, int num_experts, int top_k, int32_t* topk_indices,
+                          float* topk_weights, int32_t* expert_offsets, int32_t* slot_of,
+                          int32_t* token_map, void* dispatched_bf16, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  const int T = num_tokens, H = hidden_size, E = num_experts, K = top_k;
+  DS_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, "route_dispatch: bad shape");
+  DS_REQUIRE(E >= 1 && E <= ds::kMaxExperts, "route_dispatch: num_experts must be in [1, 64]");
+  DS_REQUIRE(K >= 1 && K <= ds::kMaxTopK && K <= E, "route_dispatch: bad top_k");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 0) {
+    if (expert_offsets) DS_CUDA(cudaMemsetAsync(expert_offsets, 0, sizeof(int32_t) * (E + 1), s));
+    return DS_OK;
+  }
+  DS_REQUIRE(router_logits && x_bf16 && topk_indices && topk_weights && expert_offsets && slot_of &&
+                 token_map && dispatched_bf16,
+             "route_dispatch: null pointer");
+  DS_REQUIRE(ds::aligned16(x_bf16) && ds::aligned16(dispatched_bf16),
+             "route_dispatch: x/dispatched must be 16-byte aligned");
+  const int nblk = ds::route_blocks(T);
+  ds::Carve c(workspace, workspace_bytes);
+  int32_t* hist = c.take<int32_t>(static_cast<size_t>(nblk) * E);
+  int32_t* base = c.take<int32_t>(static_cast<size_t>(nblk) * E);
+  int32_t* rank = c.take<int32_t>(static_cast<size_t>(T) * K);
+  if (!c.ok()) return fail(DS_ERR_WORKSPACE, "route_dispatch: workspace needs %zu bytes", c.used);
+  DS_TRY(ds::launch_route(router_logits, T, E, K, topk_indices, topk_weights, nullptr, hist, rank, s));
+  DS_TRY(ds::launch_plan(hist, nblk, E, nullptr, nullptr, expert_offsets, base, s));
+  return ds::launch_scatter(x_bf16, T, H, E, K, topk_indices, topk_weights, base, rank,
+                            dispatched_bf16, token_map, nullptr, slot_of, T * K, s);
+}
+
+int ds_moe_expert_mlp(const void* rows_bf16, int num_rows, const int32_t* group_offsets,
+                      int num_groups, const void* packed_w1_bf16, const void* w2_bf16,
+                      int hidden_size, int intermediate_size, void* h_bf16, void* out_bf16,
+                      const int32_t* out_row_map, void* stream) {
+  const int H = hidden_size, I = intermediate_size;
+  DS_REQUIRE(num_rows >= 0 && num_groups >= 1, "expert_mlp: bad shape");
+  DS_REQUIRE(H % 256 == 0 && I % 128 == 0,
+             "expert_mlp: hidden_size %% 256 and intermediate_size %% 128 must be 0");
+  if (num_rows == 0) return DS_OK;
+  DS_REQUIRE(rows_bf16 && group_offsets && packed_w1_bf16 && w2_bf16 && h_bf16 && out_bf16,
+             "expert_mlp: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DS_TRY(ds::gemm::launch(ds::mlp_gemm1(rows_bf16, num_rows, H, packed_w1_bf16,
+                                        static_cast<int64_t>(num_groups) * 2 * I, group_offsets,
+                                        num_groups, I, h_bf16),
+                          s));
+  return ds::gemm::launch(ds::mlp_gemm2(h_bf16, num_rows, I, w2_bf16,
+                                        static_cast<int64_t>(num_groups) * H, group_offsets,
+                                        num_groups, H, out_bf16, out_row_map),
+                          s);
+}
+
+int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16, const void* w2_bf16,
+                 int hidden_size, int intermediate_size, void* h_bf16, void* out_bf16,
+                 void* stream) {
+  const int H = hidden_size, I = intermediate_size;
+  DS_REQUIRE(num_rows >= 0, "dense_mlp: bad shape");
+  DS_REQUIRE(H % 256 == 0 && I % 128 == 0,
+             "dense_mlp: hidden_size %% 256 and intermediate_size %% 128 must be 0");
+  if (num_rows == 0) return DS_OK;
+  DS_REQUIRE(x_bf16 && w1_bf16 && w2_bf16 && h_bf16 && out_bf16, "dense_mlp: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DS_TRY(ds::gemm::launch(ds::mlp_gemm1(x_bf16, num_rows, H, w1_bf16, 2 * static_cast<int64_t>(I),
+                                        nullptr, 1, I, h_bf16),
+                          s));
+  return ds::gemm::launch(ds::mlp_gemm2(h_bf16, num_rows, I, w2_bf16, H, nullptr, 1, H, out_bf16,
+                                        nullptr),
+                          s);
+}
+
+int ds_moe_combine_slots(const void* expert_out_bf16, const int32_t* slot_of,
+                         const float* topk_weights, int top_k, const void* shared_out_bf16,
+                         void* out_bf16, int num_tokens, int hidden_size, void* stream) {
+  DS_REQUIRE(num_tokens >= 0 && hidden_size > 0 && hidden_size % 8 == 0,
+             "combine_slots: bad shape");
+  DS_REQUIRE(top_k >= 1 && top_k <= ds::kMaxTopK, "combine_slots: bad top_k");
+  if (num_tokens == 0) return DS_OK;
+  DS_REQUIRE(expert_out_bf16 && slot_of && topk_weights && out_bf16, "combine_slots: null pointer");
+  return ds::launch_combine_gather(expert_out_bf16, slot_of, topk_weights, top_k, shared_out_bf16,
+                                   out_bf16, num_tokens, hidden_size,
+                                   static_cast<cudaStream_t>(stream));
+}
+
+size_t ds_ep_plan_workspace_size(int num_ranks, int local_experts) {
+  return ds::align_up(2 * sizeof(int32_t) * static_cast<size_t>(num_ranks) * local_experts, 256);
+}
+
+int ds_ep_plan(const int32_t* recv_counts, int num_ranks, int local_experts, int recv_rows,
+               int32_t* expert_offsets, int32_t* row_map, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  const int N = num_ranks, El = local_experts;
+  DS_REQUIRE(N >= 1 && El >= 1 && N * El <= 4096 && recv_rows >= 0, "ep_plan: bad shape");
+  DS_REQUIRE(recv_counts && expert_offsets, "ep_plan: null pointer");
+  ds::Carve c(workspace, workspace_bytes);
+  int32_t* seg_src = c.take<int32_t>(static_cast<size_t>(N) * El);
+  int32_t* seg_exp = c.take<int32_t>(static_cast<size_t>(N) * El);
+  if (!c.ok()) return fail(DS_ERR_WORKSPACE, "ep_plan: workspace needs %zu bytes", c.used);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ds::ep_offsets_kernel<<<1, 32, 0, s>>>(recv_counts, N, El, expert_offsets, seg_src, seg_exp);
+  DS_LAUNCH_CHECK("ep_offsets_kernel");
+  if (recv_rows == 0) return DS_OK;
+  DS_REQUIRE(row_map != nullptr, "ep_plan: null row_map");
+  ds::DeviceInfo di;
+  DS_TRY(ds::device_info(&di));
+  const int segs = N * El;
+  ds::ep_rowmap_kernel<<<ds::grid_cap(recv_rows, 256, di.num_sms), 256,
+                         2 * (segs + 1) * sizeof(int32_t), s>>>(recv_counts, seg_src, seg_exp, segs,
+                                                                recv_rows, row_map);
+  DS_LAUNCH_CHECK("ep_rowmap_kernel");
+  return DS_OK;
+}
+
+int ds_gather_rows(const void* src_bf16, const int32_t* row_map, int num_rows, int hidden_size,
+                   void* dst_bf16, void* stream) {
+  DS_REQUIRE(num_rows >= 0 && hidden_size > 0 && hidden_size % 8 == 0, "gather_rows: bad shape");
+  if (num_rows == 0) return DS_OK;
+  DS_REQUIRE(src_bf16 && row_map && dst_bf16, "gather_rows: null pointer");
+  DS_REQUIRE(ds::aligned16(src_bf16) && ds::aligned16(dst_bf16), "gather_rows: misaligned");
+  ds::DeviceInfo di;
+  DS_TRY(ds::device_info(&di));
+  ds::gather_rows_kernel<<<ds::grid_cap(num_rows, 8, di.num_sms), 256, 0,
+                           static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src_bf16), row_map, num_rows, hidden_size / 8,
+      static_cast<uint4*>(dst_bf16));
+  DS_LAUNCH_CHECK("gather_rows_kernel");
+  return DS_OK;
+}
+
+}  // extern "C"

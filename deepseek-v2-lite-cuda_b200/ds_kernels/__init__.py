@@ -62,6 +62,15 @@ SIGNATURES = {
     "ds_moe_layer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
                                   _vp, _sz, _vp, _vp]),
     "ds_debug_wait_probe": (_i, [ctypes.c_longlong, _vp]),
+    "ds_moe_route_dispatch_workspace_size": (_sz, [_i, _i, _i]),
+    "ds_moe_route_dispatch": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                   _sz, _vp]),
+    "ds_moe_expert_mlp": (_i, [_vp, _i, _vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "ds_dense_mlp": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "ds_moe_combine_slots": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _vp]),
+    "ds_ep_plan_workspace_size": (_sz, [_i, _i]),
+    "ds_ep_plan": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _sz, _vp]),
+    "ds_gather_rows": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
 }
 
 
@@ -498,3 +507,110 @@ def debug_wait_probe(timeout_cycles: int) -> None:
     """Launch the bounded-wait probe (a wait nothing completes); see include/ds_kernels.h."""
     _check(_lib.ds_debug_wait_probe(int(timeout_cycles), torch.cuda.current_stream().cuda_stream),
            "debug_wait_probe")
+
+
+# ---------------------------------------------------------------------------------- stages
+def moe_route_dispatch(router_logits: torch.Tensor, x: torch.Tensor, top_k: int = 6):
+    """Routing + offsets + deterministic dispatch in one call.
+
+    Returns (topk_indices [T,k] i32, topk_weights [T,k] f32, expert_offsets [E+1] i32,
+    slot_of [T,k] i32, token_map [T*k] i32, dispatched [T*k, H] bf16)."""
+    _check_tensor(router_logits, "router_logits", torch.float32, "float32", 2, "[T, E]")
+    _check_tensor(x, "x", torch.bfloat16, "bfloat16", 2, "[T, H]")
+    T, H = x.shape
+    E = router_logits.shape[1]
+    dev = x.device
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+    off = torch.empty((E + 1,), dtype=torch.int32, device=dev)
+    slot_of = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    tmap = torch.empty((T * top_k,), dtype=torch.int32, device=dev)
+    disp = torch.empty((T * top_k, H), dtype=torch.bfloat16, device=dev)
+    need = _lib.ds_moe_route_dispatch_workspace_size(T, E, top_k)
+    ws = _workspace(need, dev)
+    with _on_device(x):
+        _check(_lib.ds_moe_route_dispatch(_ptr(router_logits), _ptr(x), T, H, E, top_k, _ptr(idx),
+                                          _ptr(w), _ptr(off), _ptr(slot_of), _ptr(tmap), _ptr(disp),
+                                          _ptr(ws), need, _stream(x)), "moe_route_dispatch")
+    return idx, w, off, slot_of, tmap, disp
+
+
+def moe_expert_mlp(rows: torch.Tensor, group_offsets: torch.Tensor, packed_w1: torch.Tensor,
+                   w2: torch.Tensor, out: Optional[torch.Tensor] = None,
+                   out_row_map: Optional[torch.Tensor] = None,
+                   h: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Grouped SwiGLU expert MLP over expert-major rows (GEMM1+SwiGLU, GEMM2)."""
+    R, H = rows.shape
+    G, two_i, _ = packed_w1.shape
+    I = two_i // 2
+    if out is None:
+        out = torch.empty((R, H), dtype=torch.bfloat16, device=rows.device)
+    if h is None:
+        h = torch.empty((R, I), dtype=torch.bfloat16, device=rows.device)
+    if R == 0:
+        return out
+    with _on_device(rows):
+        _check(_lib.ds_moe_expert_mlp(_ptr(rows), R, _ptr(group_offsets), G, _ptr(packed_w1),
+                                      _ptr(w2), H, I, _ptr(h), _ptr(out), _ptr(out_row_map),
+                                      _stream(rows)), "moe_expert_mlp")
+    return out
+
+
+def dense_mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One SwiGLU MLP over all rows (the shared expert): w1 [2I, H], w2 [H, I]."""
+    R, H = x.shape
+    I = w1.shape[0] // 2
+    if out is None:
+        out = torch.empty((R, H), dtype=torch.bfloat16, device=x.device)
+    if R == 0:
+        return out
+    h = torch.empty((R, I), dtype=torch.bfloat16, device=x.device)
+    with _on_device(x):
+        _check(_lib.ds_dense_mlp(_ptr(x), R, _ptr(w1), _ptr(w2), H, I, _ptr(h), _ptr(out),
+                                 _stream(x)), "dense_mlp")
+    return out
+
+
+def moe_combine_slots(expert_out: torch.Tensor, slot_of: torch.Tensor, topk_weights: torch.Tensor,
+                      shared_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[t] = sum_j w[t,j] * expert_out[slot_of[t,j]] (+ shared_out[t]), one bf16 rounding."""
+    T, k = slot_of.shape
+    H = expert_out.shape[1]
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=expert_out.device)
+    if T == 0:
+        return out
+    with _on_device(expert_out):
+        _check(_lib.ds_moe_combine_slots(_ptr(expert_out), _ptr(slot_of), _ptr(topk_weights), k,
+                                         _ptr(shared_out), _ptr(out), T, H, _stream(expert_out)),
+               "moe_combine_slots")
+    return out
+
+
+def ep_plan(recv_counts: torch.Tensor, recv_rows: int):
+    """Receive-side plan of the expert-parallel all-to-all: recv_counts int32 [N, El] ->
+    (expert_offsets [El+1], row_map [recv_rows])."""
+    N, El = recv_counts.shape
+    dev = recv_counts.device
+    off = torch.empty((El + 1,), dtype=torch.int32, device=dev)
+    row_map = torch.empty((max(recv_rows, 1),), dtype=torch.int32, device=dev)
+    need = _lib.ds_ep_plan_workspace_size(N, El)
+    ws = _workspace(need, dev)
+    with _on_device(recv_counts):
+        _check(_lib.ds_ep_plan(_ptr(recv_counts.contiguous()), N, El, recv_rows, _ptr(off),
+                               _ptr(row_map), _ptr(ws), need, _stream(recv_counts)), "ep_plan")
+    return off, row_map[:recv_rows]
+
+
+def gather_rows(src: torch.Tensor, row_map: torch.Tensor,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    R = row_map.shape[0]
+    H = src.shape[1]
+    if out is None:
+        out = torch.empty((R, H), dtype=src.dtype, device=src.device)
+    if R == 0:
+        return out
+    with _on_device(src):
+        _check(_lib.ds_gather_rows(_ptr(src), _ptr(row_map), R, H, _ptr(out), _stream(src)),
+               "gather_rows")
+    return out

@@ -211,6 +211,58 @@ DS_API int ds_moe_layer_forward(const float* router_logits, const void* x_bf16,
                          void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Layer stages (new, additive).  The fused layer above is these stages back to back; they
+ * are exported so a caller can put a collective between them (expert parallelism:
+ * route_dispatch -> all-to-all -> ep_plan + gather_rows -> expert_mlp -> all-to-all ->
+ * combine_slots).  Pipeline of src/kernels/moe_fused.py:118-154 split at its data exchanges.
+ *
+ * ds_moe_route_dispatch: routing (as ds_moe_routing) + expert offsets [E+1] + deterministic
+ *   dispatch (as ds_moe_dispatch) of x into expert-major `dispatched` [T*k, H]; slot_of[t, j]
+ *   is the dispatched row of (token t, pick j). */
+DS_API size_t ds_moe_route_dispatch_workspace_size(int num_tokens, int num_experts, int top_k);
+DS_API int ds_moe_route_dispatch(const float* router_logits, const void* x_bf16, int num_tokens,
+                                 int hidden_size, int num_experts, int top_k,
+                                 int32_t* topk_indices, float* topk_weights,
+                                 int32_t* expert_offsets, int32_t* slot_of, int32_t* token_map,
+                                 void* dispatched_bf16, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/* ds_moe_expert_mlp: for each group g (rows [off[g], off[g+1]) of `rows`), down(silu(gate x)
+ *   * up x) with the group's weights (packed_w1 [G, 2I, H], w2 [G, H, I]); h [R, I] is
+ *   scratch; output row i goes to out[out_row_map ? out_row_map[i] : i]. */
+DS_API int ds_moe_expert_mlp(const void* rows_bf16, int num_rows, const int32_t* group_offsets,
+                             int num_groups, const void* packed_w1_bf16, const void* w2_bf16,
+                             int hidden_size, int intermediate_size, void* h_bf16,
+                             void* out_bf16, const int32_t* out_row_map, void* stream);
+
+/* ds_dense_mlp: one SwiGLU MLP over all rows (the shared expert, src/reference/moe.py:72-74):
+ *   w1 [2I, H] (gate rows then up rows), w2 [H, I], h [R, I] scratch. */
+DS_API int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16,
+                        const void* w2_bf16, int hidden_size, int intermediate_size,
+                        void* h_bf16, void* out_bf16, void* stream);
+
+/* ds_moe_combine_slots: out[t] = bf16( sum_j w[t,j] * expert_out[slot_of[t,j]] (ascending
+ *   slot) + shared_out[t] ) ; shared_out may be NULL. */
+DS_API int ds_moe_combine_slots(const void* expert_out_bf16, const int32_t* slot_of,
+                                const float* topk_weights, int top_k,
+                                const void* shared_out_bf16, void* out_bf16, int num_tokens,
+                                int hidden_size, void* stream);
+
+/* ds_ep_plan: receive side of the expert-parallel all-to-all.  recv_counts[s*El + e] = rows
+ *   source rank s sent for local expert e; received rows are source-major.  Writes
+ *   expert_offsets [El+1] of the expert-major order and row_map [recv_rows]: expert-major
+ *   row i is source-major row row_map[i] (use it to gather the GEMM input and as the GEMM2
+ *   out_row_map so results land back in source-major order). */
+DS_API size_t ds_ep_plan_workspace_size(int num_ranks, int local_experts);
+DS_API int ds_ep_plan(const int32_t* recv_counts, int num_ranks, int local_experts,
+                      int recv_rows, int32_t* expert_offsets, int32_t* row_map,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ds_gather_rows: dst[i] = src[row_map[i]] for bf16 rows of hidden_size. */
+DS_API int ds_gather_rows(const void* src_bf16, const int32_t* row_map, int num_rows,
+                          int hidden_size, void* dst_bf16, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Failure-detection probe (no reference counterpart): launches one CTA that waits on an
  * mbarrier nothing arrives on, through the same bounded-wait routine the GEMM pipeline
  * uses, with a limit of `timeout_cycles` SM clock cycles.  The wait runs out, the kernel
