@@ -60,6 +60,12 @@ struct Params {
   const int32_t* out_row_map;
   int* status;
   long long timeout_cycles;
+  // router epilogue
+  int router_E;
+  int router_K;
+  int32_t* idx_out;
+  float* w_out;
+  float* logits_out;
 };
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
@@ -93,6 +99,125 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const Params& p, const in
   return ti;
 }
 
+// ---- epilogues: one accumulator row per thread, all lanes execute the TMEM loads ----------
+// SwiGLU: accumulator columns [0,128) gate, [128,256) up of the same 128 intermediate units.
+__device__ __forceinline__ void epilogue_swiglu(uint32_t tb, bool valid, __nv_bfloat16* dst) {
+#pragma unroll 1
+  for (int cc = 0; cc < 4; ++cc) {
+    uint32_t g[32], u[32];
+    ptx::tmem_ld32(tb + cc * 32, g);
+    ptx::tmem_ld32(tb + 128 + cc * 32, u);
+    ptx::tmem_wait_ld2(g, u);
+    if (valid) {
+      uint32_t o[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        o[i] = pack2(silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
+                     silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1])));
+      uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    }
+  }
+}
+
+// Plain: 256 accumulator columns -> bf16, half h of the tile to column base + h*half1_off.
+__device__ __forceinline__ void epilogue_plain(uint32_t tb, bool valid, __nv_bfloat16* row,
+                                               int col0, int half1_off) {
+#pragma unroll 1
+  for (int cc = 0; cc < 8; ++cc) {
+    uint32_t v[32];
+    ptx::tmem_ld32(tb + cc * 32, v);
+    ptx::tmem_wait_ld(v);
+    if (valid) {
+      const int col = col0 + (cc >> 2) * half1_off + (cc & 3) * 32;
+      uint4* d4 = reinterpret_cast<uint4*>(row + col);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        d4[i] = make_uint4(pack2(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
+                           pack2(__uint_as_float(v[8 * i + 2]), __uint_as_float(v[8 * i + 3])),
+                           pack2(__uint_as_float(v[8 * i + 4]), __uint_as_float(v[8 * i + 5])),
+                           pack2(__uint_as_float(v[8 * i + 6]), __uint_as_float(v[8 * i + 7])));
+    }
+  }
+}
+
+// Router: the B operand is the f32 gate split exactly into three bf16 parts (rows [0,64) hi,
+// [64,128) mid, [128,192) lo, zero above), so accumulator columns c, 64+c, 128+c hold
+// x.hi, x.mid, x.lo for expert c and logit = (hi + mid) + lo keeps f32 accuracy.  Then
+// top-K by logit (ties -> lower expert index) and the softmax weight of each pick, written
+// from registers (src/reference/moe.py:33-43 semantics, canonical tie-break).
+__device__ __forceinline__ bool router_above(float v, int c, float a, int i) {
+  return v > a || (v == a && c < i);
+}
+
+__device__ __forceinline__ void epilogue_router(uint32_t tb, bool valid, int64_t row,
+                                                const Params& p) {
+  float lg[64];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t v[32];
+    ptx::tmem_ld32(tb + h * 32, v);
+    ptx::tmem_wait_ld(v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) lg[h * 32 + i] = __uint_as_float(v[i]);
+    ptx::tmem_ld32(tb + 64 + h * 32, v);
+    ptx::tmem_wait_ld(v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) lg[h * 32 + i] += __uint_as_float(v[i]);
+    ptx::tmem_ld32(tb + 128 + h * 32, v);
+    ptx::tmem_wait_ld(v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) lg[h * 32 + i] += __uint_as_float(v[i]);
+  }
+  if (!valid) return;
+  const int E = p.router_E, K = p.router_K;
+  float tv[8];
+  int ti[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    tv[j] = -INFINITY;
+    ti[j] = 0x7fffffff;
+  }
+#pragma unroll
+  for (int e = 0; e < 64; ++e) {
+    if (e < E && router_above(lg[e], e, tv[7], ti[7])) {
+      tv[7] = lg[e];
+      ti[7] = e;
+#pragma unroll
+      for (int j = 7; j > 0; --j) {
+        if (router_above(tv[j], ti[j], tv[j - 1], ti[j - 1])) {
+          const float a = tv[j];
+          tv[j] = tv[j - 1];
+          tv[j - 1] = a;
+          const int b = ti[j];
+          ti[j] = ti[j - 1];
+          ti[j - 1] = b;
+        }
+      }
+    }
+  }
+  const float mx = tv[0];
+  float sum = 0.f;
+#pragma unroll
+  for (int e = 0; e < 64; ++e)
+    if (e < E) sum += expf(lg[e] - mx);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (j < K) {
+      p.idx_out[row * K + j] = ti[j];
+      p.w_out[row * K + j] = expf(tv[j] - mx) / sum;
+    }
+  }
+  if (p.logits_out != nullptr) {
+#pragma unroll
+    for (int e = 0; e < 64; ++e)
+      if (e < E) p.logits_out[row * E + e] = lg[e];
+  }
+}
+
+template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const Params p) {
@@ -263,43 +388,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = r < ti.rows;
       int64_t orow = ti.row0 + r;
       if (valid && p.out_row_map != nullptr) orow = __ldg(p.out_row_map + orow);
-      if (p.epilogue == kSwiGLU) {
-        __nv_bfloat16* dst = p.out + orow * p.ldo + ti.nt * 128;
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t g[32], u[32];
-          ptx::tmem_ld32(tb + cc * 32, g);
-          ptx::tmem_ld32(tb + 128 + cc * 32, u);
-          ptx::tmem_wait_ld2(g, u);
-          if (valid) {
-            uint32_t o[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              o[i] = pack2(silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
-                           silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1])));
-            uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-          }
-        }
+      if constexpr (EPI == kSwiGLU) {
+        epilogue_swiglu(tb, valid, p.out + orow * p.ldo + ti.nt * 128);
+      } else if constexpr (EPI == kRouter) {
+        epilogue_router(tb, valid, orow, p);
       } else {
-#pragma unroll 1
-        for (int cc = 0; cc < 8; ++cc) {
-          uint32_t v[32];
-          ptx::tmem_ld32(tb + cc * 32, v);
-          ptx::tmem_wait_ld(v);
-          if (valid) {
-            const int col = ti.nt * p.b_tile_stride + (cc >> 2) * p.b_half1_off + (cc & 3) * 32;
-            uint4* d4 = reinterpret_cast<uint4*>(p.out + orow * p.ldo + col);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i] = make_uint4(pack2(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
-                                 pack2(__uint_as_float(v[8 * i + 2]), __uint_as_float(v[8 * i + 3])),
-                                 pack2(__uint_as_float(v[8 * i + 4]), __uint_as_float(v[8 * i + 5])),
-                                 pack2(__uint_as_float(v[8 * i + 6]), __uint_as_float(v[8 * i + 7])));
-          }
-        }
+        epilogue_plain(tb, valid, p.out + orow * p.ldo, ti.nt * p.b_tile_stride, p.b_half1_off);
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -338,7 +432,7 @@ __global__ void zero_uncovered_kernel(uint4* __restrict__ out, int64_t S, int ld
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 cudaError_t g_encode_err = cudaSuccess;
-bool g_attr_set[64] = {};
+bool g_attr_set[3][64] = {};
 std::mutex g_attr_mutex;
 
 int get_encode(PFN_cuTensorMapEncodeTiled_v12000* fn) {
@@ -379,9 +473,14 @@ int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int cols) {
 
 int launch(const Problem& pr, cudaStream_t s) {
   if (pr.a_rows <= 0) return DS_OK;
-  DS_REQUIRE(pr.A && pr.B && pr.out, "gemm: null pointer");
-  DS_REQUIRE(aligned16(pr.A) && aligned16(pr.B) && aligned16(pr.out),
+  const bool router = pr.epilogue == kRouter;
+  DS_REQUIRE(pr.A && pr.B && (router || pr.out), "gemm: null pointer");
+  DS_REQUIRE(aligned16(pr.A) && aligned16(pr.B) && (router || aligned16(pr.out)),
              "gemm: A, B and out must be 16-byte aligned");
+  DS_REQUIRE(!router || (pr.idx_out && pr.w_out && pr.router_E >= 1 && pr.router_E <= 64 &&
+                         pr.router_K >= 1 && pr.router_K <= 8 && pr.router_K <= pr.router_E &&
+                         pr.n_tiles == 1 && pr.b_rows == 256 && pr.offsets == nullptr),
+             "gemm: bad router problem");
   DS_REQUIRE(pr.K > 0 && pr.K % 8 == 0, "gemm: K=%d must be a positive multiple of 8", pr.K);
   DS_REQUIRE(pr.ldo % 8 == 0, "gemm: output leading dimension must be a multiple of 8");
   DS_REQUIRE(pr.groups >= 1 && pr.groups <= kMaxGroups, "gemm: groups=%d outside [1, %d]",
@@ -390,12 +489,17 @@ int launch(const Problem& pr, cudaStream_t s) {
   DS_REQUIRE(pr.a_rows < (1LL << 31) && pr.b_rows < (1LL << 31), "gemm: too many rows");
   DeviceInfo di;
   DS_TRY(device_info(&di));
+  DS_REQUIRE(pr.epilogue == kPlain || pr.epilogue == kSwiGLU || pr.epilogue == kRouter,
+             "gemm: unknown epilogue %d", pr.epilogue);
   {
     std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (!g_attr_set[di.device]) {
-      DS_CUDA(cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (!g_attr_set[pr.epilogue][di.device]) {
+      const void* fn = pr.epilogue == kSwiGLU  ? reinterpret_cast<const void*>(grouped_gemm_kernel<kSwiGLU>)
+                       : pr.epilogue == kRouter ? reinterpret_cast<const void*>(grouped_gemm_kernel<kRouter>)
+                                                : reinterpret_cast<const void*>(grouped_gemm_kernel<kPlain>);
+      DS_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(kSmemBytes)));
-      g_attr_set[di.device] = true;
+      g_attr_set[pr.epilogue][di.device] = true;
     }
   }
   CUtensorMap tmA, tmB;
@@ -417,11 +521,23 @@ int launch(const Problem& pr, cudaStream_t s) {
   p.out_row_map = pr.out_row_map;
   p.status = device_status_ptr();
   p.timeout_cycles = kDefaultTimeoutCycles;
+  p.router_E = pr.router_E;
+  p.router_K = pr.router_K;
+  p.idx_out = pr.idx_out;
+  p.w_out = pr.w_out;
+  p.logits_out = pr.logits_out;
   if (p.status == nullptr) return fail(DS_ERR_CUDA, "device status word unavailable");
   const int64_t max_mtiles = (pr.a_rows + BM - 1) / BM + (pr.offsets ? p.groups : 0);
   const int64_t max_tiles = max_mtiles * pr.n_tiles;
-  const int grid = static_cast<int>(max_tiles < di.num_sms ? max_tiles : di.num_sms);
-  grouped_gemm_kernel<<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, p);
+  int cap = di.num_sms;
+  if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
+  const int grid = static_cast<int>(max_tiles < cap ? max_tiles : cap);
+  if (pr.epilogue == kSwiGLU)
+    grouped_gemm_kernel<kSwiGLU><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, p);
+  else if (pr.epilogue == kRouter)
+    grouped_gemm_kernel<kRouter><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, p);
+  else
+    grouped_gemm_kernel<kPlain><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, p);
   DS_LAUNCH_CHECK("grouped_gemm_kernel");
   return DS_OK;
 }

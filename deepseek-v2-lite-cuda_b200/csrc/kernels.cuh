@@ -44,7 +44,7 @@ int launch_swiglu(const void* in, void* out, int64_t rows, int I, cudaStream_t s
 
 namespace gemm {
 
-enum Epilogue : int { kPlain = 0, kSwiGLU = 1 };
+enum Epilogue : int { kPlain = 0, kSwiGLU = 1, kRouter = 2 };
 
 // Grouped / dense bf16 GEMM on tcgen05: for each row group g (rows [off[g], off[g+1]) of A)
 // out[rows, cols] = A[rows, :] @ B_w[...]^T with w = g % weight_group_mod.  B rows for
@@ -67,6 +67,13 @@ struct Problem {
   int ldo;
   int epilogue;
   const int32_t* out_row_map;  // optional: destination row for each A row
+  int max_ctas = 0;            // grid cap (0 = one CTA per SM), leaves SMs to concurrent work
+  // router epilogue (epilogue == kRouter): B = split gate [256, K]; writes top-k per row
+  int router_E = 0;
+  int router_K = 0;
+  int32_t* idx_out = nullptr;
+  float* w_out = nullptr;
+  float* logits_out = nullptr;
 };
 
 int launch(const Problem& pr, cudaStream_t s);

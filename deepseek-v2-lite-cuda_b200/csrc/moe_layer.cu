@@ -49,23 +49,24 @@ size_t carve_layer(Carve& c, LayerBuffers* b, int T, int H, int E, int K, int I,
 
 using ds::fail;
 
-extern "C" {
-
-size_t ds_moe_layer_workspace_size(int num_tokens, int hidden_size, int num_experts,
-                                   int top_k, int intermediate_size,
-                                   int shared_intermediate_size) {
+extern "C" size_t ds_moe_layer_workspace_size(int num_tokens, int hidden_size, int num_experts,
+                                              int top_k, int intermediate_size,
+                                              int shared_intermediate_size) {
   ds::Carve c(nullptr, 0);
   return ds::carve_layer(c, nullptr, num_tokens, hidden_size, num_experts, top_k,
                          intermediate_size, shared_intermediate_size);
 }
 
-int ds_moe_layer_forward(const float* router_logits, const void* x_bf16,
-                         const void* packed_w1_bf16, const void* w2_bf16,
-                         const void* shared_w1_bf16, const void* shared_w2_bf16,
-                         void* out_bf16, int num_tokens, int hidden_size, int num_experts,
-                         int top_k, int intermediate_size, int shared_intermediate_size,
-                         void* workspace, size_t workspace_bytes, void** events,
-                         void* stream) {
+namespace {
+
+// One implementation for both entry points: routing from given f32 logits, or from x via the
+// router GEMM (tcgen05, split f32 gate) whose epilogue does the top-k.
+int layer_impl(const float* router_logits, const void* router_w_split, float* logits_out,
+               const void* x_bf16, const void* packed_w1_bf16, const void* w2_bf16,
+               const void* shared_w1_bf16, const void* shared_w2_bf16, void* out_bf16,
+               int num_tokens, int hidden_size, int num_experts, int top_k,
+               int intermediate_size, int shared_intermediate_size, void* workspace,
+               size_t workspace_bytes, void** events, void* stream) {
   const int T = num_tokens, H = hidden_size, E = num_experts, K = top_k;
   const int I = intermediate_size;
   const bool has_shared = shared_w1_bf16 != nullptr && shared_w2_bf16 != nullptr;
@@ -86,7 +87,7 @@ int ds_moe_layer_forward(const float* router_logits, const void* x_bf16,
     return DS_OK;
   };
   if (T == 0) return DS_OK;
-  DS_REQUIRE(router_logits && x_bf16 && packed_w1_bf16 && w2_bf16 && out_bf16,
+  DS_REQUIRE((router_logits || router_w_split) && x_bf16 && packed_w1_bf16 && w2_bf16 && out_bf16,
              "moe_layer: null pointer");
   ds::Carve c(workspace, workspace_bytes);
   ds::LayerBuffers b;
@@ -96,7 +97,33 @@ int ds_moe_layer_forward(const float* router_logits, const void* x_bf16,
   const int nblk = ds::route_blocks(T);
 
   DS_TRY(mark(0));
-  DS_TRY(ds::launch_route(router_logits, T, E, K, b.idx, b.w, nullptr, b.blk_hist, b.local_rank, s));
+  if (router_w_split != nullptr) {
+    ds::gemm::Problem r{};
+    r.A = x_bf16;
+    r.a_rows = T;
+    r.K = H;
+    r.B = router_w_split;
+    r.b_rows = 256;
+    r.offsets = nullptr;
+    r.groups = 1;
+    r.n_tiles = 1;
+    r.b_rows_per_group = 256;
+    r.b_tile_stride = 256;
+    r.b_half1_off = 128;
+    r.weight_group_mod = 1;
+    r.out = nullptr;
+    r.ldo = 8;
+    r.epilogue = ds::gemm::kRouter;
+    r.router_E = E;
+    r.router_K = K;
+    r.idx_out = b.idx;
+    r.w_out = b.w;
+    r.logits_out = logits_out;
+    DS_TRY(ds::gemm::launch(r, s));
+    DS_TRY(ds::launch_rank(b.idx, T, E, K, b.blk_hist, b.local_rank, s));
+  } else {
+    DS_TRY(ds::launch_route(router_logits, T, E, K, b.idx, b.w, nullptr, b.blk_hist, b.local_rank, s));
+  }
   DS_TRY(mark(1));
   DS_TRY(ds::launch_plan(b.blk_hist, nblk, E, nullptr, nullptr, b.offsets, b.blk_base, s));
   DS_TRY(mark(2));
@@ -186,6 +213,39 @@ int ds_moe_layer_forward(const float* router_logits, const void* x_bf16,
                                    T, H, s));
   DS_TRY(mark(8));
   return DS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ds_moe_layer_forward(const float* router_logits, const void* x_bf16,
+                         const void* packed_w1_bf16, const void* w2_bf16,
+                         const void* shared_w1_bf16, const void* shared_w2_bf16,
+                         void* out_bf16, int num_tokens, int hidden_size, int num_experts,
+                         int top_k, int intermediate_size, int shared_intermediate_size,
+                         void* workspace, size_t workspace_bytes, void** events,
+                         void* stream) {
+  return layer_impl(router_logits, nullptr, nullptr, x_bf16, packed_w1_bf16, w2_bf16,
+                    shared_w1_bf16, shared_w2_bf16, out_bf16, num_tokens, hidden_size,
+                    num_experts, top_k, intermediate_size, shared_intermediate_size, workspace,
+                    workspace_bytes, events, stream);
+}
+
+int ds_moe_layer_forward_from_x(const void* x_bf16, const void* router_w_split_bf16,
+                                float* logits_out, const void* packed_w1_bf16,
+                                const void* w2_bf16, const void* shared_w1_bf16,
+                                const void* shared_w2_bf16, void* out_bf16, int num_tokens,
+                                int hidden_size, int num_experts, int top_k,
+                                int intermediate_size, int shared_intermediate_size,
+                                void* workspace, size_t workspace_bytes, void** events,
+                                void* stream) {
+  if (router_w_split_bf16 == nullptr)
+    return fail(DS_ERR_INVALID_ARG, "moe_layer_from_x: router_w_split is null");
+  return layer_impl(nullptr, router_w_split_bf16, logits_out, x_bf16, packed_w1_bf16, w2_bf16,
+                    shared_w1_bf16, shared_w2_bf16, out_bf16, num_tokens, hidden_size,
+                    num_experts, top_k, intermediate_size, shared_intermediate_size, workspace,
+                    workspace_bytes, events, stream);
 }
 
 }  // extern "C"

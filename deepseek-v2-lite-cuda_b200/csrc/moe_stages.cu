@@ -71,6 +71,29 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// gate f32 [E, H] -> split [256, H] bf16: rows e, 64+e, 128+e = hi, mid, lo with
+// gate = hi + mid + lo (each residual is exact in f32); all other rows zero.
+__global__ void router_split_kernel(const float* __restrict__ gate, int E, int H,
+                                    __nv_bfloat16* __restrict__ out) {
+  const int64_t total = 256LL * H;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / H);
+    const int c = static_cast<int>(i - static_cast<int64_t>(r) * H);
+    const int part = r >> 6, e = r & 63;
+    float v = 0.f;
+    if (part < 3 && e < E) {
+      const float g = gate[static_cast<int64_t>(e) * H + c];
+      const float hi = __bfloat162float(__float2bfloat16_rn(g));
+      const float r1 = g - hi;
+      const float mid = __bfloat162float(__float2bfloat16_rn(r1));
+      const float r2 = r1 - mid;
+      v = part == 0 ? hi : (part == 1 ? mid : r2);
+    }
+    out[i] = __float2bfloat16_rn(v);
+  }
+}
+
 int grid_cap(int64_t items, int per_block, int num_sms) {
   const int64_t need = (items + per_block - 1) / per_block;
   const int64_t cap = static_cast<int64_t>(num_sms) * 8;
@@ -172,7 +195,7 @@ int ds_moe_route_dispatch(const float* router_logits, const void* x_bf16, int nu
 int ds_moe_expert_mlp(const void* rows_bf16, int num_rows, const int32_t* group_offsets,
                       int num_groups, const void* packed_w1_bf16, const void* w2_bf16,
                       int hidden_size, int intermediate_size, void* h_bf16, void* out_bf16,
-                      const int32_t* out_row_map, void* stream) {
+                      const int32_t* out_row_map, int max_ctas, void* stream) {
   const int H = hidden_size, I = intermediate_size;
   DS_REQUIRE(num_rows >= 0 && num_groups >= 1, "expert_mlp: bad shape");
   DS_REQUIRE(H % 256 == 0 && I % 128 == 0,
@@ -181,19 +204,20 @@ int ds_moe_expert_mlp(const void* rows_bf16, int num_rows, const int32_t* group_
   DS_REQUIRE(rows_bf16 && group_offsets && packed_w1_bf16 && w2_bf16 && h_bf16 && out_bf16,
              "expert_mlp: null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  DS_TRY(ds::gemm::launch(ds::mlp_gemm1(rows_bf16, num_rows, H, packed_w1_bf16,
-                                        static_cast<int64_t>(num_groups) * 2 * I, group_offsets,
-                                        num_groups, I, h_bf16),
-                          s));
-  return ds::gemm::launch(ds::mlp_gemm2(h_bf16, num_rows, I, w2_bf16,
-                                        static_cast<int64_t>(num_groups) * H, group_offsets,
-                                        num_groups, H, out_bf16, out_row_map),
-                          s);
+  ds::gemm::Problem g1 = ds::mlp_gemm1(rows_bf16, num_rows, H, packed_w1_bf16,
+                                       static_cast<int64_t>(num_groups) * 2 * I, group_offsets,
+                                       num_groups, I, h_bf16);
+  ds::gemm::Problem g2 = ds::mlp_gemm2(h_bf16, num_rows, I, w2_bf16,
+                                       static_cast<int64_t>(num_groups) * H, group_offsets,
+                                       num_groups, H, out_bf16, out_row_map);
+  g1.max_ctas = g2.max_ctas = max_ctas;
+  DS_TRY(ds::gemm::launch(g1, s));
+  return ds::gemm::launch(g2, s);
 }
 
 int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16, const void* w2_bf16,
                  int hidden_size, int intermediate_size, void* h_bf16, void* out_bf16,
-                 void* stream) {
+                 int max_ctas, void* stream) {
   const int H = hidden_size, I = intermediate_size;
   DS_REQUIRE(num_rows >= 0, "dense_mlp: bad shape");
   DS_REQUIRE(H % 256 == 0 && I % 128 == 0,
@@ -201,12 +225,13 @@ int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16, const vo
   if (num_rows == 0) return DS_OK;
   DS_REQUIRE(x_bf16 && w1_bf16 && w2_bf16 && h_bf16 && out_bf16, "dense_mlp: null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  DS_TRY(ds::gemm::launch(ds::mlp_gemm1(x_bf16, num_rows, H, w1_bf16, 2 * static_cast<int64_t>(I),
-                                        nullptr, 1, I, h_bf16),
-                          s));
-  return ds::gemm::launch(ds::mlp_gemm2(h_bf16, num_rows, I, w2_bf16, H, nullptr, 1, H, out_bf16,
-                                        nullptr),
-                          s);
+  ds::gemm::Problem g1 = ds::mlp_gemm1(x_bf16, num_rows, H, w1_bf16, 2 * static_cast<int64_t>(I),
+                                       nullptr, 1, I, h_bf16);
+  ds::gemm::Problem g2 = ds::mlp_gemm2(h_bf16, num_rows, I, w2_bf16, H, nullptr, 1, H, out_bf16,
+                                       nullptr);
+  g1.max_ctas = g2.max_ctas = max_ctas;
+  DS_TRY(ds::gemm::launch(g1, s));
+  return ds::gemm::launch(g2, s);
 }
 
 int ds_moe_combine_slots(const void* expert_out_bf16, const int32_t* slot_of,
@@ -220,6 +245,83 @@ int ds_moe_combine_slots(const void* expert_out_bf16, const int32_t* slot_of,
   return ds::launch_combine_gather(expert_out_bf16, slot_of, topk_weights, top_k, shared_out_bf16,
                                    out_bf16, num_tokens, hidden_size,
                                    static_cast<cudaStream_t>(stream));
+}
+
+int ds_router_weight_split(const float* gate_weight, int num_experts, int hidden_size,
+                           void* w_split_bf16, void* stream) {
+  DS_REQUIRE(num_experts >= 1 && num_experts <= 64 && hidden_size > 0 && hidden_size % 8 == 0,
+             "router_weight_split: num_experts in [1, 64], hidden_size %% 8 == 0");
+  DS_REQUIRE(gate_weight && w_split_bf16, "router_weight_split: null pointer");
+  ds::DeviceInfo di;
+  DS_TRY(ds::device_info(&di));
+  ds::router_split_kernel<<<ds::grid_cap(256LL * hidden_size, 256, di.num_sms), 256, 0,
+                            static_cast<cudaStream_t>(stream)>>>(
+      gate_weight, num_experts, hidden_size, static_cast<__nv_bfloat16*>(w_split_bf16));
+  DS_LAUNCH_CHECK("router_split_kernel");
+  return DS_OK;
+}
+
+int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens, int hidden_size,
+                  int num_experts, int top_k, int32_t* topk_indices, float* topk_weights,
+                  float* logits_out, void* stream) {
+  DS_REQUIRE(num_tokens >= 0 && hidden_size > 0 && hidden_size % 8 == 0, "moe_router: bad shape");
+  DS_REQUIRE(num_experts >= 1 && num_experts <= 64, "moe_router: num_experts must be in [1, 64]");
+  DS_REQUIRE(top_k >= 1 && top_k <= 8 && top_k <= num_experts, "moe_router: bad top_k");
+  if (num_tokens == 0) return DS_OK;
+  DS_REQUIRE(x_bf16 && w_split_bf16 && topk_indices && topk_weights, "moe_router: null pointer");
+  ds::gemm::Problem p{};
+  p.A = x_bf16;
+  p.a_rows = num_tokens;
+  p.K = hidden_size;
+  p.B = w_split_bf16;
+  p.b_rows = 256;
+  p.offsets = nullptr;
+  p.groups = 1;
+  p.n_tiles = 1;
+  p.b_rows_per_group = 256;
+  p.b_tile_stride = 256;
+  p.b_half1_off = 128;
+  p.weight_group_mod = 1;
+  p.out = nullptr;
+  p.ldo = 8;
+  p.epilogue = ds::gemm::kRouter;
+  p.router_E = num_experts;
+  p.router_K = top_k;
+  p.idx_out = topk_indices;
+  p.w_out = topk_weights;
+  p.logits_out = logits_out;
+  return ds::gemm::launch(p, static_cast<cudaStream_t>(stream));
+}
+
+int ds_moe_dispatch_routed(const int32_t* topk_indices, const float* topk_weights,
+                           const void* x_bf16, int num_tokens, int hidden_size, int num_experts,
+                           int top_k, int32_t* expert_offsets, int32_t* slot_of,
+                           int32_t* token_map, void* dispatched_bf16, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  const int T = num_tokens, H = hidden_size, E = num_experts, K = top_k;
+  DS_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, "dispatch_routed: bad shape");
+  DS_REQUIRE(E >= 1 && E <= ds::kMaxExperts, "dispatch_routed: num_experts must be in [1, 64]");
+  DS_REQUIRE(K >= 1 && K <= ds::kMaxTopK && K <= E, "dispatch_routed: bad top_k");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T == 0) {
+    if (expert_offsets) DS_CUDA(cudaMemsetAsync(expert_offsets, 0, sizeof(int32_t) * (E + 1), s));
+    return DS_OK;
+  }
+  DS_REQUIRE(topk_indices && topk_weights && x_bf16 && expert_offsets && slot_of && token_map &&
+                 dispatched_bf16,
+             "dispatch_routed: null pointer");
+  DS_REQUIRE(ds::aligned16(x_bf16) && ds::aligned16(dispatched_bf16),
+             "dispatch_routed: x/dispatched must be 16-byte aligned");
+  const int nblk = ds::route_blocks(T);
+  ds::Carve c(workspace, workspace_bytes);
+  int32_t* hist = c.take<int32_t>(static_cast<size_t>(nblk) * E);
+  int32_t* base = c.take<int32_t>(static_cast<size_t>(nblk) * E);
+  int32_t* rank = c.take<int32_t>(static_cast<size_t>(T) * K);
+  if (!c.ok()) return fail(DS_ERR_WORKSPACE, "dispatch_routed: workspace needs %zu bytes", c.used);
+  DS_TRY(ds::launch_rank(topk_indices, T, E, K, hist, rank, s));
+  DS_TRY(ds::launch_plan(hist, nblk, E, nullptr, nullptr, expert_offsets, base, s));
+  return ds::launch_scatter(x_bf16, T, H, E, K, topk_indices, topk_weights, base, rank,
+                            dispatched_bf16, token_map, nullptr, slot_of, T * K, s);
 }
 
 size_t ds_ep_plan_workspace_size(int num_ranks, int local_experts) {

@@ -65,8 +65,14 @@ SIGNATURES = {
     "ds_moe_route_dispatch_workspace_size": (_sz, [_i, _i, _i]),
     "ds_moe_route_dispatch": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                    _sz, _vp]),
-    "ds_moe_expert_mlp": (_i, [_vp, _i, _vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp]),
-    "ds_dense_mlp": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "ds_moe_expert_mlp": (_i, [_vp, _i, _vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
+    "ds_dense_mlp": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _vp]),
+    "ds_router_weight_split": (_i, [_vp, _i, _i, _vp, _vp]),
+    "ds_moe_router": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "ds_moe_dispatch_routed": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz,
+                                    _vp]),
+    "ds_moe_layer_forward_from_x": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
+                                         _i, _i, _vp, _sz, _vp, _vp]),
     "ds_moe_combine_slots": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _vp]),
     "ds_ep_plan_workspace_size": (_sz, [_i, _i]),
     "ds_ep_plan": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _sz, _vp]),
@@ -538,7 +544,7 @@ def moe_route_dispatch(router_logits: torch.Tensor, x: torch.Tensor, top_k: int 
 def moe_expert_mlp(rows: torch.Tensor, group_offsets: torch.Tensor, packed_w1: torch.Tensor,
                    w2: torch.Tensor, out: Optional[torch.Tensor] = None,
                    out_row_map: Optional[torch.Tensor] = None,
-                   h: Optional[torch.Tensor] = None) -> torch.Tensor:
+                   h: Optional[torch.Tensor] = None, max_ctas: int = 0) -> torch.Tensor:
     """Grouped SwiGLU expert MLP over expert-major rows (GEMM1+SwiGLU, GEMM2)."""
     R, H = rows.shape
     G, two_i, _ = packed_w1.shape
@@ -552,12 +558,12 @@ def moe_expert_mlp(rows: torch.Tensor, group_offsets: torch.Tensor, packed_w1: t
     with _on_device(rows):
         _check(_lib.ds_moe_expert_mlp(_ptr(rows), R, _ptr(group_offsets), G, _ptr(packed_w1),
                                       _ptr(w2), H, I, _ptr(h), _ptr(out), _ptr(out_row_map),
-                                      _stream(rows)), "moe_expert_mlp")
+                                      int(max_ctas), _stream(rows)), "moe_expert_mlp")
     return out
 
 
 def dense_mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
-              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, max_ctas: int = 0) -> torch.Tensor:
     """One SwiGLU MLP over all rows (the shared expert): w1 [2I, H], w2 [H, I]."""
     R, H = x.shape
     I = w1.shape[0] // 2
@@ -568,7 +574,7 @@ def dense_mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     h = torch.empty((R, I), dtype=torch.bfloat16, device=x.device)
     with _on_device(x):
         _check(_lib.ds_dense_mlp(_ptr(x), R, _ptr(w1), _ptr(w2), H, I, _ptr(h), _ptr(out),
-                                 _stream(x)), "dense_mlp")
+                                 int(max_ctas), _stream(x)), "dense_mlp")
     return out
 
 
@@ -613,4 +619,87 @@ def gather_rows(src: torch.Tensor, row_map: torch.Tensor,
     with _on_device(src):
         _check(_lib.ds_gather_rows(_ptr(src), _ptr(row_map), R, H, _ptr(out), _stream(src)),
                "gather_rows")
+    return out
+
+
+def router_weight_split(gate_weight: torch.Tensor) -> torch.Tensor:
+    """f32 gate [E, H] -> bf16 [256, H]: hi/mid/lo parts (rows e, 64+e, 128+e) summing to it."""
+    g = gate_weight.detach().float().contiguous()
+    E, H = g.shape
+    out = torch.empty((256, H), dtype=torch.bfloat16, device=g.device)
+    with _on_device(g):
+        _check(_lib.ds_router_weight_split(_ptr(g), E, H, _ptr(out), _stream(g)),
+               "router_weight_split")
+    return out
+
+
+def moe_router(x: torch.Tensor, w_split: torch.Tensor, num_experts: int, top_k: int = 6,
+               logits_out: Optional[torch.Tensor] = None):
+    """Router GEMM (f32-accurate, tensor cores) + top-k: -> (idx [T,k] i32, w [T,k] f32)."""
+    _check_tensor(x, "x", torch.bfloat16, "bfloat16", 2, "[T, H]")
+    T, H = x.shape
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
+    if T == 0:
+        return idx, w
+    with _on_device(x):
+        _check(_lib.ds_moe_router(_ptr(x), _ptr(w_split), T, H, num_experts, top_k, _ptr(idx),
+                                  _ptr(w), _ptr(logits_out), _stream(x)), "moe_router")
+    return idx, w
+
+
+def moe_dispatch_routed(idx: torch.Tensor, w: torch.Tensor, x: torch.Tensor, num_experts: int):
+    """Offsets + deterministic dispatch from given routing -> (offsets, slot_of, token_map,
+    dispatched)."""
+    T, H = x.shape
+    k = idx.shape[1]
+    dev = x.device
+    off = torch.empty((num_experts + 1,), dtype=torch.int32, device=dev)
+    slot_of = torch.empty((T, k), dtype=torch.int32, device=dev)
+    tmap = torch.empty((T * k,), dtype=torch.int32, device=dev)
+    disp = torch.empty((T * k, H), dtype=torch.bfloat16, device=dev)
+    need = _lib.ds_moe_route_dispatch_workspace_size(T, num_experts, k)
+    ws = _workspace(need, dev)
+    with _on_device(x):
+        _check(_lib.ds_moe_dispatch_routed(_ptr(idx), _ptr(w), _ptr(x), T, H, num_experts, k,
+                                           _ptr(off), _ptr(slot_of), _ptr(tmap), _ptr(disp),
+                                           _ptr(ws), need, _stream(x)), "moe_dispatch_routed")
+    return off, slot_of, tmap, disp
+
+
+def moe_layer_forward_from_x(x: torch.Tensor, router_w_split: torch.Tensor, num_experts: int,
+                             packed_w1: torch.Tensor, w2: torch.Tensor,
+                             shared_w1: Optional[torch.Tensor] = None,
+                             shared_w2: Optional[torch.Tensor] = None, top_k: int = 6,
+                             out: Optional[torch.Tensor] = None,
+                             workspace: Optional[torch.Tensor] = None,
+                             events: Optional[Sequence[torch.cuda.Event]] = None,
+                             logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Whole MoE layer from the tokens in one C call, router included (f32-accurate tensor-core
+    router + top-k epilogue).  `logits_out` (f32 [T, E]) receives the router logits."""
+    _check_tensor(x, "x", torch.bfloat16, "bfloat16", 2, "[T, H]")
+    T, H = x.shape
+    E = num_experts
+    I = packed_w1.shape[1] // 2
+    _require(packed_w1.shape[0] == E and tuple(w2.shape) == (E, H, I), "expert weight shapes")
+    Is = 0 if shared_w1 is None else shared_w1.shape[0] // 2
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    if T == 0:
+        return out
+    need = moe_layer_workspace_size(T, H, E, top_k, I, Is)
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(need, x.device)
+    ev = None
+    if events is not None:
+        _require(len(events) == LAYER_NUM_EVENTS, f"events must hold {LAYER_NUM_EVENTS} events")
+        st = torch.cuda.current_stream(x.device)
+        for e in events:
+            e.record(st)
+        ev = (ctypes.c_void_p * LAYER_NUM_EVENTS)(*[e.cuda_event for e in events])
+    with _on_device(x):
+        _check(_lib.ds_moe_layer_forward_from_x(
+            _ptr(x), _ptr(router_w_split), _ptr(logits_out), _ptr(packed_w1), _ptr(w2),
+            _ptr(shared_w1), _ptr(shared_w2), _ptr(out), T, H, E, top_k, I, Is, _ptr(workspace),
+            workspace.numel(), ev, _stream(x)), "moe_layer_forward_from_x")
     return out

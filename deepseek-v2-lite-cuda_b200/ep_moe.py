@@ -26,7 +26,6 @@ from typing import Optional
 
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
 
 
 class CudaOps:
@@ -36,11 +35,16 @@ class CudaOps:
         import ds_kernels
         self.k = ds_kernels
 
-    def router(self, x, gate_weight):
-        return F.linear(x.float(), gate_weight.float())
+    def prepare_router(self, gate_weight):
+        return self.k.router_weight_split(gate_weight)
 
-    def route_dispatch(self, logits, x, top_k):
-        return self.k.moe_route_dispatch(logits, x, top_k)
+    def route(self, x, router_state, num_experts, top_k):
+        """-> (topk_indices, topk_weights): tensor-core router with f32-accurate logits."""
+        return self.k.moe_router(x, router_state, num_experts, top_k)
+
+    def dispatch(self, idx, w, x, num_experts):
+        """-> (expert_offsets, slot_of, token_map, dispatched)."""
+        return self.k.moe_dispatch_routed(idx, w, x, num_experts)
 
     def ep_plan(self, recv_counts, recv_rows):
         return self.k.ep_plan(recv_counts, recv_rows)
@@ -51,8 +55,8 @@ class CudaOps:
     def expert_mlp(self, rows, offsets, w1, w2, out, out_row_map):
         return self.k.moe_expert_mlp(rows, offsets, w1, w2, out=out, out_row_map=out_row_map)
 
-    def dense_mlp(self, x, w1, w2):
-        return self.k.dense_mlp(x, w1, w2)
+    def dense_mlp(self, x, w1, w2, max_ctas=0):
+        return self.k.dense_mlp(x, w1, w2, max_ctas=max_ctas)
 
     def combine_slots(self, back, slot_of, w, shared_out):
         return self.k.moe_combine_slots(back, slot_of, w, shared_out)
@@ -87,6 +91,7 @@ class EPMoELayer(torch.nn.Module):
         self.shared_w2 = shared_w2
         self.top_k = top_k
         self.ops = ops if ops is not None else CudaOps()
+        self.router_state = self.ops.prepare_router(gate_weight)
         self._side = torch.cuda.Stream(device=self.w1.device) if self.w1.is_cuda else None
 
     def _a2a(self, out, inp, out_splits=None, in_splits=None):
@@ -115,8 +120,8 @@ class EPMoELayer(torch.nn.Module):
             shared_out = ops.dense_mlp(x, self.shared_w1, self.shared_w2)
 
         mark(0)
-        logits = ops.router(x, self.gate_weight)
-        idx, w, offsets, slot_of, token_map, disp = ops.route_dispatch(logits, x, k)
+        idx, w = ops.route(x, self.router_state, self.num_experts, k)
+        offsets, slot_of, token_map, disp = ops.dispatch(idx, w, x, self.num_experts)
         mark(1)
         counts = (offsets[1:] - offsets[:-1]).to(torch.int32).view(N, El).contiguous()
         recv_counts = torch.empty_like(counts)

@@ -5,10 +5,12 @@ Public API kept from the reference:
   fused_moe_forward(hidden_states, gate_weight, experts, top_k=6, packed_w1=None, w2=None)
                                                  (moe_fused.py:227-272)
 
-Per call: the router GEMM in f32 (F.linear(x.float(), W.float()), as moe_fused.py:131),
-then ONE C-ABI call (ds_moe_layer_forward) that runs routing -> plan -> dispatch ->
-tcgen05 grouped GEMM1 with fused SwiGLU -> grouped GEMM2 -> (shared expert) -> combine on
-the current stream, with no host synchronisation and no Python loop over experts.
+Per call: ONE C-ABI call (ds_moe_layer_forward_from_x) that runs the router (x @ gate^T with
+f32 accuracy on the tensor cores: the f32 gate is pre-split into three bf16 parts that sum
+to it exactly; the GEMM epilogue does the top-k and softmax) -> plan -> dispatch -> tcgen05
+grouped GEMM1 with fused SwiGLU -> grouped GEMM2 -> (shared expert) -> combine on the
+current stream, with no host synchronisation and no Python loop over experts.  The
+reference computes the router as F.linear(x.float(), W.float()) (moe_fused.py:131).
 
 Difference from the reference: FusedMoELayer also runs the module's shared experts
 (src/reference/moe.py:72-74,106-107), which the reference pipeline drops, so its output
@@ -20,7 +22,6 @@ from typing import Optional
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 import ds_kernels
 from expert_prepack import prepack_experts, prepack_shared
@@ -38,17 +39,16 @@ class _Workspace:
         return self.buf
 
 
-def _layer(hidden_states, gate_weight, packed_w1, w2, shared_w1, shared_w2, top_k, ws,
-           events=None):
+def _layer(hidden_states, router_w_split, num_experts, packed_w1, w2, shared_w1, shared_w2,
+           top_k, ws, events=None, logits_out=None):
     T, H = hidden_states.shape
-    logits = F.linear(hidden_states.float(), gate_weight.float(), None)
     E, twoI, _ = packed_w1.shape
     Is = 0 if shared_w1 is None else shared_w1.shape[0] // 2
     need = ds_kernels.moe_layer_workspace_size(T, H, E, top_k, twoI // 2, Is)
-    return ds_kernels.moe_layer_forward(logits, hidden_states, packed_w1, w2, shared_w1,
-                                        shared_w2, top_k=top_k,
-                                        workspace=ws.get(need, hidden_states.device),
-                                        events=events)
+    return ds_kernels.moe_layer_forward_from_x(hidden_states, router_w_split, num_experts,
+                                               packed_w1, w2, shared_w1, shared_w2, top_k=top_k,
+                                               workspace=ws.get(need, hidden_states.device),
+                                               events=events, logits_out=logits_out)
 
 
 class FusedMoELayer(nn.Module):
@@ -67,6 +67,8 @@ class FusedMoELayer(nn.Module):
         self.top_k = moe_module.num_experts_per_tok
         self.num_experts = len(moe_module.experts)
         self.packed_w1, self.w2 = prepack_experts(list(moe_module.experts))
+        self.router_w_split = ds_kernels.router_weight_split(
+            self.gate_weight.to(self.packed_w1.device))
         shared = getattr(moe_module, "shared_experts", None)
         if shared is not None:
             self.shared_w1, self.shared_w2 = prepack_shared(shared, self.packed_w1.device)
@@ -92,15 +94,20 @@ class FusedMoELayer(nn.Module):
         self.packed_w1, self.w2 = packed_w1.contiguous(), w2.contiguous()
         self.shared_w1 = None if shared_w1 is None else shared_w1.contiguous()
         self.shared_w2 = None if shared_w2 is None else shared_w2.contiguous()
+        self.router_w_split = ds_kernels.router_weight_split(gate_weight.to(packed_w1.device))
         self._ws = _Workspace()
         return self
 
-    def forward(self, hidden_states: torch.Tensor, events=None) -> torch.Tensor:
+    def forward(self, hidden_states: torch.Tensor, events=None,
+                logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """hidden_states bf16 [T, H] -> bf16 [T, H].  `logits_out` (f32 [T, E]) receives the
+        router logits; `events` (9 CUDA events) are recorded between the phases."""
         assert hidden_states.is_cuda, "hidden_states must be on CUDA."
         assert hidden_states.dtype == torch.bfloat16, "hidden_states must be BF16."
         assert hidden_states.dim() == 2, "hidden_states must be 2-D [T, H]."
-        return _layer(hidden_states.contiguous(), self.gate_weight, self.packed_w1, self.w2,
-                      self.shared_w1, self.shared_w2, self.top_k, self._ws, events)
+        return _layer(hidden_states.contiguous(), self.router_w_split, self.num_experts,
+                      self.packed_w1, self.w2, self.shared_w1, self.shared_w2, self.top_k,
+                      self._ws, events, logits_out)
 
 
 _WEIGHT_CACHE: dict = {}
@@ -122,5 +129,6 @@ def fused_moe_forward(hidden_states: torch.Tensor, gate_weight: torch.Tensor, ex
         if key not in _WEIGHT_CACHE:
             _WEIGHT_CACHE[key] = prepack_experts(experts)
         packed_w1, w2 = _WEIGHT_CACHE[key]
-    return _layer(hidden_states.contiguous(), gate_weight, packed_w1, w2, None, None, top_k,
-                  _FN_WS)
+    split = ds_kernels.router_weight_split(gate_weight.to(hidden_states.device))
+    return _layer(hidden_states.contiguous(), split, gate_weight.shape[0], packed_w1, w2, None,
+                  None, top_k, _FN_WS)

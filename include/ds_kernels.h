@@ -227,19 +227,41 @@ DS_API int ds_moe_route_dispatch(const float* router_logits, const void* x_bf16,
                                  void* dispatched_bf16, void* workspace, size_t workspace_bytes,
                                  void* stream);
 
+/* ds_moe_router: router logits x @ gate^T with f32 accuracy on the tensor cores plus the
+ *   top-k of ds_moe_routing, in one launch (the f32 gate is pre-split by
+ *   ds_router_weight_split into bf16 hi/mid/lo parts that sum to it exactly; the GEMM
+ *   epilogue adds the three partial logits and selects).  Replaces the f32 F.linear +
+ *   moe_routing pair of src/kernels/moe_fused.py:131-137.  logits_out [T, E] may be NULL.
+ * ds_router_weight_split: gate f32 [E, H] -> w_split bf16 [256, H] (rows e, 64+e, 128+e). */
+DS_API int ds_router_weight_split(const float* gate_weight, int num_experts, int hidden_size,
+                                  void* w_split_bf16, void* stream);
+DS_API int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens,
+                         int hidden_size, int num_experts, int top_k, int32_t* topk_indices,
+                         float* topk_weights, float* logits_out, void* stream);
+
+/* ds_moe_dispatch_routed: ds_moe_route_dispatch for routing that is already computed
+ *   (topk_indices/weights [T, k]); workspace size as ds_moe_route_dispatch_workspace_size. */
+DS_API int ds_moe_dispatch_routed(const int32_t* topk_indices, const float* topk_weights,
+                                  const void* x_bf16, int num_tokens, int hidden_size,
+                                  int num_experts, int top_k, int32_t* expert_offsets,
+                                  int32_t* slot_of, int32_t* token_map, void* dispatched_bf16,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* ds_moe_expert_mlp: for each group g (rows [off[g], off[g+1]) of `rows`), down(silu(gate x)
  *   * up x) with the group's weights (packed_w1 [G, 2I, H], w2 [G, H, I]); h [R, I] is
- *   scratch; output row i goes to out[out_row_map ? out_row_map[i] : i]. */
+ *   scratch; output row i goes to out[out_row_map ? out_row_map[i] : i].  max_ctas caps the
+ *   GEMM grid (0 = one CTA per SM) to leave SMs to work that must run concurrently. */
 DS_API int ds_moe_expert_mlp(const void* rows_bf16, int num_rows, const int32_t* group_offsets,
                              int num_groups, const void* packed_w1_bf16, const void* w2_bf16,
                              int hidden_size, int intermediate_size, void* h_bf16,
-                             void* out_bf16, const int32_t* out_row_map, void* stream);
+                             void* out_bf16, const int32_t* out_row_map, int max_ctas,
+                             void* stream);
 
 /* ds_dense_mlp: one SwiGLU MLP over all rows (the shared expert, src/reference/moe.py:72-74):
- *   w1 [2I, H] (gate rows then up rows), w2 [H, I], h [R, I] scratch. */
+ *   w1 [2I, H] (gate rows then up rows), w2 [H, I], h [R, I] scratch; max_ctas as above. */
 DS_API int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16,
                         const void* w2_bf16, int hidden_size, int intermediate_size,
-                        void* h_bf16, void* out_bf16, void* stream);
+                        void* h_bf16, void* out_bf16, int max_ctas, void* stream);
 
 /* ds_moe_combine_slots: out[t] = bf16( sum_j w[t,j] * expert_out[slot_of[t,j]] (ascending
  *   slot) + shared_out[t] ) ; shared_out may be NULL. */
@@ -261,6 +283,19 @@ DS_API int ds_ep_plan(const int32_t* recv_counts, int num_ranks, int local_exper
 /* ds_gather_rows: dst[i] = src[row_map[i]] for bf16 rows of hidden_size. */
 DS_API int ds_gather_rows(const void* src_bf16, const int32_t* row_map, int num_rows,
                           int hidden_size, void* dst_bf16, void* stream);
+
+/* Fused layer from the tokens: ds_moe_router (f32-accurate tensor-core router + top-k)
+ * followed by the pipeline of ds_moe_layer_forward.  router_w_split from
+ * ds_router_weight_split; logits_out f32 [T, E] may be NULL; workspace size as
+ * ds_moe_layer_workspace_size; events as ds_moe_layer_forward (phase 0 = router + ranks). */
+DS_API int ds_moe_layer_forward_from_x(const void* x_bf16, const void* router_w_split_bf16,
+                                       float* logits_out, const void* packed_w1_bf16,
+                                       const void* w2_bf16, const void* shared_w1_bf16,
+                                       const void* shared_w2_bf16, void* out_bf16,
+                                       int num_tokens, int hidden_size, int num_experts,
+                                       int top_k, int intermediate_size,
+                                       int shared_intermediate_size, void* workspace,
+                                       size_t workspace_bytes, void** events, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Failure-detection probe (no reference counterpart): launches one CTA that waits on an

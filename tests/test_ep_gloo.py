@@ -28,14 +28,17 @@ def _free_port():
 class CpuOps:
     """f32 CPU stand-in for CudaOps, built on the oracle."""
 
-    def router(self, x, gate):
-        return x.float() @ gate.float().t()
+    def prepare_router(self, gate):
+        return gate.float()
 
-    def route_dispatch(self, logits, x, top_k):
+    def route(self, x, gate, num_experts, top_k):
         import oracle
-        idx, w = oracle.route(logits, top_k)
-        disp, tmap, dw, slot_of, off = oracle.dispatch(x, idx, w, logits.shape[1])
-        return idx, w, off, slot_of, tmap, disp.contiguous()
+        return oracle.route(x.float() @ gate.t(), top_k)
+
+    def dispatch(self, idx, w, x, num_experts):
+        import oracle
+        disp, tmap, dw, slot_of, off = oracle.dispatch(x, idx, w, num_experts)
+        return off, slot_of, tmap, disp.contiguous()
 
     def ep_plan(self, recv_counts, R):
         N, El = recv_counts.shape
@@ -65,7 +68,7 @@ class CpuOps:
                 out[out_row_map[a:b].long()] = _mlp(rows[a:b].float(), w1[e].float(), w2[e].float())
         return out
 
-    def dense_mlp(self, x, w1, w2):
+    def dense_mlp(self, x, w1, w2, max_ctas=0):
         from oracle.moe_oracle import _mlp
         return _mlp(x.float(), w1.float(), w2.float())
 

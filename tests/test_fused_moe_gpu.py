@@ -88,6 +88,7 @@ def test_cfg0_full():
 
 def test_fused_layer_module_api_and_functional_api():
     # reference e2e test shape: no shared experts, x = randn * 0.1
+    import ds_kernels
     W = weights(7, 0)
     mod = OracleMoE(W, top_k=K).to(torch.bfloat16).cuda()
     from moe_fused import FusedMoELayer, fused_moe_forward
@@ -95,13 +96,46 @@ def test_fused_layer_module_api_and_functional_api():
     for T in (1, 4, 16, 32, 128):
         g = torch.Generator().manual_seed(42 + T)
         x = (torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16)
-        out = fused(x.cuda())
-        logits = F.linear(x.cuda().float(), mod.gate.weight.float())
+        logits = torch.empty(T, E, device="cuda")
+        out = fused(x.cuda(), logits_out=logits)
         ref = oracle.moe_forward(x, W, K, logits=logits.cpu())
         assert out.shape == (T, H)
         check(out, ref, atol=2e-2)
+        # the device logits are the f32 router logits up to summation order
+        torch.testing.assert_close(logits.cpu(), x.float() @ W.gate.t(), atol=1e-4, rtol=1e-4)
         out2 = fused_moe_forward(x.cuda(), mod.gate.weight, list(mod.experts), top_k=K)
-        check(out2, ref, atol=2e-2)
+        assert torch.equal(out2, out)  # same router, same pipeline (no shared expert here)
+
+
+def run_layer_from_x(W, D, x):
+    import ds_kernels
+    xd = x.cuda()
+    split = ds_kernels.router_weight_split(D["gate"])
+    logits = torch.empty(x.shape[0], E, device="cuda")
+    out = ds_kernels.moe_layer_forward_from_x(xd, split, E, D["w1"], D["w2"], D["sw1"], D["sw2"],
+                                              top_k=K, logits_out=logits)
+    ref = oracle.moe_forward(x, W, K, logits=logits.cpu())
+    return out, ref, logits
+
+
+@pytest.mark.parametrize("T", [1, 3, 129, 1000])
+def test_layer_from_x(T):
+    W = weights(0, 2)
+    D = device_weights(W)
+    g = torch.Generator().manual_seed(500 + T)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    out, ref, logits = run_layer_from_x(W, D, x)
+    check(out, ref)
+    torch.testing.assert_close(logits.cpu(), x.float() @ W.gate.t(), atol=1e-4, rtol=1e-4)
+
+
+def test_cfg2_full_size_from_x():
+    W = weights(1, 2)
+    D = device_weights(W)
+    g = torch.Generator().manual_seed(1002)
+    x = torch.randn(8192, H, generator=g).to(torch.bfloat16)
+    out, ref, logits = run_layer_from_x(W, D, x)
+    check(out, ref)
 
 
 def test_layer_deterministic():

@@ -96,3 +96,42 @@ def test_combine_slots_matches_oracle():
     out = ds().moe_combine_slots(eo.cuda(), slot_of.cuda(), w.cuda(), sh.cuda())
     ref = oracle.combine(eo, tmap, dw, T) + sh.float()
     assert_bf16_close(out, ref, 2e-2)
+
+
+def test_router_weight_split_sums_to_gate():
+    g = torch.Generator().manual_seed(3)
+    gate = torch.randn(64, H, generator=g) * 0.02  # generic f32, not bf16-representable
+    split = ds().router_weight_split(gate.cuda()).float().cpu()
+    rec = (split[0:64].double() + split[64:128].double()) + split[128:192].double()
+    assert torch.all(split[192:] == 0)
+    err = (rec - gate.double()).abs() / gate.double().abs().clamp_min(1e-30)
+    assert err.max().item() <= 2.0 ** -24
+
+
+@pytest.mark.parametrize("T,E_", [(1, 64), (127, 64), (3000, 64), (77, 24)])
+def test_router_matches_f32_logits_and_routing(T, E_):
+    g = torch.Generator().manual_seed(T + E_)
+    gate = torch.randn(E_, H, generator=g) * 0.02
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    split = ds().router_weight_split(gate.cuda())
+    logits = torch.empty(T, E_, device="cuda")
+    idx, w = ds().moe_router(x.cuda(), split, E_, K, logits_out=logits)
+    ref_logits = x.double() @ gate.double().t()
+    torch.testing.assert_close(logits.cpu().double(), ref_logits, atol=2e-5, rtol=1e-5)
+    ridx, rw = oracle.route(logits.cpu(), K)   # routing defined on the device logits
+    assert torch.equal(idx.cpu(), ridx)
+    torch.testing.assert_close(w.cpu(), rw, atol=1e-6, rtol=0)
+
+
+def test_dispatch_routed_matches_oracle():
+    T = 2049
+    g = torch.Generator().manual_seed(8)
+    logits = torch.randn(T, E, generator=g)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    ridx, rw = oracle.route(logits, K)
+    off, slot_of, tmap, disp = ds().moe_dispatch_routed(ridx.cuda(), rw.cuda(), x.cuda(), E)
+    rdisp, rtmap, _, rslot, roff = oracle.dispatch(x, ridx, rw, E)
+    assert torch.equal(off.cpu(), roff)
+    assert torch.equal(slot_of.cpu(), rslot)
+    assert torch.equal(tmap.cpu(), rtmap)
+    assert torch.equal(disp.cpu(), rdisp)
