@@ -426,6 +426,14 @@ def kernel_case(name, reps=2):
                 w2 = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
                 for _ in range(reps):
                     ds_kernels.moe_gemm2(h, w2, off)
+    elif name == "router":
+        T = T_GLOBAL
+        g = torch.Generator(device=dev).manual_seed(5)
+        x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        gate = torch.randn(E, H, generator=g, device=dev) * 0.02
+        split = ds_kernels.router_weight_split(gate)
+        for _ in range(reps):
+            ds_kernels.moe_router(x, split, E, K)
     elif name in ("routing", "combine"):
         T = 16384
         logits = synthetic.zipf_logits(T, E, 11, dev)
@@ -472,7 +480,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--op-report", default=None)
     ap.add_argument("--kernel-case", default=None,
-                    choices=["gemm1", "gemm2", "dispatch", "routing", "combine",
+                    choices=["gemm1", "gemm2", "dispatch", "routing", "router", "combine",
                              "rms_norm", "rope", "kv_upproj"],
                     help="run one kernel at its BASELINE size twice (profiling) and exit")
     args = ap.parse_args()

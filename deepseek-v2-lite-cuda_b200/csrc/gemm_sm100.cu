@@ -562,7 +562,8 @@ using ds::fail;
 namespace {
 
 int moe_gemm1_impl(const void* dispatched, const void* packed_w1, const int32_t* offsets,
-                   void* out, int S, int E, int H, int twoI, int epilogue, void* stream) {
+                   void* out, int S, int E, int H, int twoI, int epilogue, void* stream,
+                   int max_ctas = 0) {
   DS_REQUIRE(S >= 0 && E >= 1 && H > 0 && twoI > 0, "gemm1: bad shape");
   DS_REQUIRE(twoI % 256 == 0, "gemm1: 2*intermediate_size=%d must be a multiple of 256", twoI);
   DS_REQUIRE(H % 8 == 0, "gemm1: hidden_size must be a multiple of 8");
@@ -587,7 +588,43 @@ int moe_gemm1_impl(const void* dispatched, const void* packed_w1, const int32_t*
   pr.ldo = epilogue == ds::gemm::kSwiGLU ? I : twoI;
   pr.epilogue = epilogue;
   pr.out_row_map = nullptr;
+  pr.max_ctas = max_ctas;
   DS_TRY(ds::gemm::launch_zero_uncovered(out, S, pr.ldo, offsets, E, s));
+  return ds::gemm::launch(pr, s);
+}
+
+int moe_gemm2_impl(const void* swiglu_out_bf16, const void* w2_bf16,
+                   const int32_t* expert_offsets, void* gemm2_out_bf16, int total_slots,
+                   int num_experts, int intermediate_size, int hidden_size, int max_ctas,
+                   void* stream) {
+  DS_REQUIRE(total_slots >= 0 && num_experts >= 1 && intermediate_size > 0 && hidden_size > 0,
+             "gemm2: bad shape");
+  DS_REQUIRE(hidden_size % 256 == 0, "gemm2: hidden_size=%d must be a multiple of 256",
+             hidden_size);
+  DS_REQUIRE(intermediate_size % 8 == 0, "gemm2: intermediate_size must be a multiple of 8");
+  if (total_slots == 0) return DS_OK;
+  DS_REQUIRE(expert_offsets != nullptr, "gemm2: expert_offsets is null");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ds::gemm::Problem pr{};
+  pr.A = swiglu_out_bf16;
+  pr.a_rows = total_slots;
+  pr.K = intermediate_size;
+  pr.B = w2_bf16;
+  pr.b_rows = static_cast<int64_t>(num_experts) * hidden_size;
+  pr.offsets = expert_offsets;
+  pr.groups = num_experts;
+  pr.n_tiles = hidden_size / 256;
+  pr.b_rows_per_group = hidden_size;
+  pr.b_tile_stride = 256;
+  pr.b_half1_off = 128;
+  pr.weight_group_mod = num_experts;
+  pr.out = gemm2_out_bf16;
+  pr.ldo = hidden_size;
+  pr.epilogue = ds::gemm::kPlain;
+  pr.out_row_map = nullptr;
+  pr.max_ctas = max_ctas;
+  DS_TRY(ds::gemm::launch_zero_uncovered(gemm2_out_bf16, total_slots, hidden_size, expert_offsets,
+                                         num_experts, s));
   return ds::gemm::launch(pr, s);
 }
 
@@ -615,34 +652,8 @@ int ds_moe_gemm1_swiglu(const void* dispatched_bf16, const void* packed_w1_bf16,
 int ds_moe_gemm2(const void* swiglu_out_bf16, const void* w2_bf16,
                  const int32_t* expert_offsets, void* gemm2_out_bf16, int total_slots,
                  int num_experts, int intermediate_size, int hidden_size, void* stream) {
-  DS_REQUIRE(total_slots >= 0 && num_experts >= 1 && intermediate_size > 0 && hidden_size > 0,
-             "gemm2: bad shape");
-  DS_REQUIRE(hidden_size % 256 == 0, "gemm2: hidden_size=%d must be a multiple of 256",
-             hidden_size);
-  DS_REQUIRE(intermediate_size % 8 == 0, "gemm2: intermediate_size must be a multiple of 8");
-  if (total_slots == 0) return DS_OK;
-  DS_REQUIRE(expert_offsets != nullptr, "gemm2: expert_offsets is null");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ds::gemm::Problem pr{};
-  pr.A = swiglu_out_bf16;
-  pr.a_rows = total_slots;
-  pr.K = intermediate_size;
-  pr.B = w2_bf16;
-  pr.b_rows = static_cast<int64_t>(num_experts) * hidden_size;
-  pr.offsets = expert_offsets;
-  pr.groups = num_experts;
-  pr.n_tiles = hidden_size / 256;
-  pr.b_rows_per_group = hidden_size;
-  pr.b_tile_stride = 256;
-  pr.b_half1_off = 128;
-  pr.weight_group_mod = num_experts;
-  pr.out = gemm2_out_bf16;
-  pr.ldo = hidden_size;
-  pr.epilogue = ds::gemm::kPlain;
-  pr.out_row_map = nullptr;
-  DS_TRY(ds::gemm::launch_zero_uncovered(gemm2_out_bf16, total_slots, hidden_size, expert_offsets,
-                                         num_experts, s));
-  return ds::gemm::launch(pr, s);
+  return moe_gemm2_impl(swiglu_out_bf16, w2_bf16, expert_offsets, gemm2_out_bf16, total_slots,
+                        num_experts, intermediate_size, hidden_size, 0, stream);
 }
 
 int ds_kv_upproj(const void* normed_kv_bf16, const void* weight_bf16, void* kv_up_bf16,

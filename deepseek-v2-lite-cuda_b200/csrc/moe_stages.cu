@@ -234,6 +234,34 @@ int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16, const vo
   return ds::gemm::launch(g2, s);
 }
 
+int ds_dense_gemm1_swiglu(const void* x_bf16, int num_rows, const void* w1_bf16,
+                          int hidden_size, int intermediate_size, void* h_bf16, int max_ctas,
+                          void* stream) {
+  DS_REQUIRE(num_rows >= 0 && hidden_size > 0 && hidden_size % 8 == 0 &&
+                 intermediate_size % 128 == 0 && intermediate_size > 0,
+             "dense_gemm1_swiglu: bad shape");
+  if (num_rows == 0) return DS_OK;
+  DS_REQUIRE(x_bf16 && w1_bf16 && h_bf16, "dense_gemm1_swiglu: null pointer");
+  ds::gemm::Problem g = ds::mlp_gemm1(x_bf16, num_rows, hidden_size, w1_bf16,
+                                      2 * static_cast<int64_t>(intermediate_size), nullptr, 1,
+                                      intermediate_size, h_bf16);
+  g.max_ctas = max_ctas;
+  return ds::gemm::launch(g, static_cast<cudaStream_t>(stream));
+}
+
+int ds_dense_gemm2(const void* h_bf16, int num_rows, const void* w2_bf16, int intermediate_size,
+                   int hidden_size, void* out_bf16, int max_ctas, void* stream) {
+  DS_REQUIRE(num_rows >= 0 && intermediate_size > 0 && intermediate_size % 8 == 0 &&
+                 hidden_size % 256 == 0 && hidden_size > 0,
+             "dense_gemm2: bad shape");
+  if (num_rows == 0) return DS_OK;
+  DS_REQUIRE(h_bf16 && w2_bf16 && out_bf16, "dense_gemm2: null pointer");
+  ds::gemm::Problem g = ds::mlp_gemm2(h_bf16, num_rows, intermediate_size, w2_bf16, hidden_size,
+                                      nullptr, 1, hidden_size, out_bf16, nullptr);
+  g.max_ctas = max_ctas;
+  return ds::gemm::launch(g, static_cast<cudaStream_t>(stream));
+}
+
 int ds_moe_combine_slots(const void* expert_out_bf16, const int32_t* slot_of,
                          const float* topk_weights, int top_k, const void* shared_out_bf16,
                          void* out_bf16, int num_tokens, int hidden_size, void* stream) {

@@ -68,6 +68,8 @@ SIGNATURES = {
     "ds_moe_expert_mlp": (_i, [_vp, _i, _vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
     "ds_dense_mlp": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _vp]),
     "ds_router_weight_split": (_i, [_vp, _i, _i, _vp, _vp]),
+    "ds_dense_gemm1_swiglu": (_i, [_vp, _i, _vp, _i, _i, _vp, _i, _vp]),
+    "ds_dense_gemm2": (_i, [_vp, _i, _vp, _i, _i, _vp, _i, _vp]),
     "ds_moe_router": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "ds_moe_dispatch_routed": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz,
                                     _vp]),
@@ -702,4 +704,30 @@ def moe_layer_forward_from_x(x: torch.Tensor, router_w_split: torch.Tensor, num_
             _ptr(x), _ptr(router_w_split), _ptr(logits_out), _ptr(packed_w1), _ptr(w2),
             _ptr(shared_w1), _ptr(shared_w2), _ptr(out), T, H, E, top_k, I, Is, _ptr(workspace),
             workspace.numel(), ev, _stream(x)), "moe_layer_forward_from_x")
+    return out
+
+
+def dense_gemm1_swiglu(x: torch.Tensor, w1: torch.Tensor, max_ctas: int = 0) -> torch.Tensor:
+    """h = silu(x @ gate^T) * (x @ up^T) with w1 = [gate; up] [2I, H] -> bf16 [R, I]."""
+    R, H = x.shape
+    I = w1.shape[0] // 2
+    h = torch.empty((R, I), dtype=torch.bfloat16, device=x.device)
+    if R == 0:
+        return h
+    with _on_device(x):
+        _check(_lib.ds_dense_gemm1_swiglu(_ptr(x), R, _ptr(w1), H, I, _ptr(h), int(max_ctas),
+                                          _stream(x)), "dense_gemm1_swiglu")
+    return h
+
+
+def dense_gemm2(h: torch.Tensor, w2: torch.Tensor, max_ctas: int = 0) -> torch.Tensor:
+    """out = h @ w2^T, w2 [H, I] -> bf16 [R, H]."""
+    R, I = h.shape
+    H = w2.shape[0]
+    out = torch.empty((R, H), dtype=torch.bfloat16, device=h.device)
+    if R == 0:
+        return out
+    with _on_device(h):
+        _check(_lib.ds_dense_gemm2(_ptr(h), R, _ptr(w2), I, H, _ptr(out), int(max_ctas),
+                                   _stream(h)), "dense_gemm2")
     return out

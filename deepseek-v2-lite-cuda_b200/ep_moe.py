@@ -12,8 +12,11 @@ Rank r of N owns experts [r*E/N, (r+1)*E/N) and its own tokens.  One forward:
      into expert-major order, grouped GEMM1+SwiGLU / GEMM2 on the local experts with the
      GEMM2 epilogue writing each result straight back to its source-major row;
   5. all-to-all of the expert outputs back to the token owners;
-  6. combine (k expert rows per token in ascending slot order + the shared expert, which
-     runs on a side stream while the exchanges are in flight).
+  6. combine (k expert rows per token in ascending slot order + the shared expert).
+
+The row exchanges are issued asynchronously and the shared expert's two GEMMs run on the
+compute stream while they are in flight (GEMM1 under the dispatch exchange, GEMM2 under the
+return exchange), with their grid capped so NCCL's kernels keep SMs.
 
 The reference has no multi-GPU code; this is the sharding BASELINE config 2 asks for.
 The compute steps go through an `ops` object: by default the CUDA kernels of
@@ -58,6 +61,16 @@ class CudaOps:
     def dense_mlp(self, x, w1, w2, max_ctas=0):
         return self.k.dense_mlp(x, w1, w2, max_ctas=max_ctas)
 
+    def shared_gemm1(self, x, w1, max_ctas=0):
+        """silu(x @ gate^T) * (x @ up^T) for the shared expert (GEMM1 + SwiGLU epilogue)."""
+        return self.k.dense_gemm1_swiglu(x, w1, max_ctas)
+
+    def shared_gemm2(self, h, w2, max_ctas=0):
+        return self.k.dense_gemm2(h, w2, max_ctas)
+
+    def num_sms(self, device):
+        return torch.cuda.get_device_properties(device).multi_processor_count
+
     def combine_slots(self, back, slot_of, w, shared_out):
         return self.k.moe_combine_slots(back, slot_of, w, shared_out)
 
@@ -92,10 +105,11 @@ class EPMoELayer(torch.nn.Module):
         self.top_k = top_k
         self.ops = ops if ops is not None else CudaOps()
         self.router_state = self.ops.prepare_router(gate_weight)
-        self._side = torch.cuda.Stream(device=self.w1.device) if self.w1.is_cuda else None
+        self.nccl_reserve_sms = 32
 
-    def _a2a(self, out, inp, out_splits=None, in_splits=None):
-        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+    def _a2a(self, out, inp, out_splits=None, in_splits=None, async_op=False):
+        return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group,
+                                      async_op=async_op)
 
     PHASES = ("route_dispatch", "exchange_counts", "exchange_rows", "expert_mlp",
               "exchange_back", "combine")
@@ -110,14 +124,8 @@ class EPMoELayer(torch.nn.Module):
                 events[i].record()
         T, H = x.shape
         has_shared = self.shared_w1 is not None
-        shared_out = None
-        if has_shared and self._side is not None:
-            cur = torch.cuda.current_stream(x.device)
-            self._side.wait_stream(cur)
-            with torch.cuda.stream(self._side):
-                shared_out = ops.dense_mlp(x, self.shared_w1, self.shared_w2)
-        elif has_shared:
-            shared_out = ops.dense_mlp(x, self.shared_w1, self.shared_w2)
+        # SMs left to NCCL while a capped GEMM overlaps an exchange
+        cap = max(1, ops.num_sms(x.device) - self.nccl_reserve_sms) if x.is_cuda else 0
 
         mark(0)
         idx, w = ops.route(x, self.router_state, self.num_experts, k)
@@ -131,7 +139,9 @@ class EPMoELayer(torch.nn.Module):
         R = int(sum(recv_splits))
         mark(2)
         recv = torch.empty((R, H), dtype=disp.dtype, device=disp.device)
-        self._a2a(recv, disp, recv_splits, send_splits)
+        work = self._a2a(recv, disp, recv_splits, send_splits, async_op=True)
+        sh = ops.shared_gemm1(x, self.shared_w1, cap) if has_shared else None
+        work.wait()
         mark(3)
 
         exp_off, row_map = ops.ep_plan(recv_counts, R)
@@ -142,12 +152,10 @@ class EPMoELayer(torch.nn.Module):
         self.last_recv_rows = R
         mark(4)
         back = torch.empty_like(disp)
-        self._a2a(back, ret, send_splits, recv_splits)
+        work = self._a2a(back, ret, send_splits, recv_splits, async_op=True)
+        shared_out = ops.shared_gemm2(sh, self.shared_w2, cap) if has_shared else None
+        work.wait()
         mark(5)
-
-        if has_shared and self._side is not None:
-            torch.cuda.current_stream(x.device).wait_stream(self._side)
-            shared_out.record_stream(torch.cuda.current_stream(x.device))
         out = ops.combine_slots(back, slot_of, w, shared_out)
         mark(6)
         return out

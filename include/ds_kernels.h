@@ -263,6 +263,16 @@ DS_API int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16,
                         const void* w2_bf16, int hidden_size, int intermediate_size,
                         void* h_bf16, void* out_bf16, int max_ctas, void* stream);
 
+/* ds_dense_gemm1_swiglu / ds_dense_gemm2: the two halves of ds_dense_mlp as separate
+ *   launches (h = silu(x gate^T) * (x up^T); out = h w2^T), so each can overlap a different
+ *   exchange; max_ctas as above. */
+DS_API int ds_dense_gemm1_swiglu(const void* x_bf16, int num_rows, const void* w1_bf16,
+                                 int hidden_size, int intermediate_size, void* h_bf16,
+                                 int max_ctas, void* stream);
+DS_API int ds_dense_gemm2(const void* h_bf16, int num_rows, const void* w2_bf16,
+                          int intermediate_size, int hidden_size, void* out_bf16, int max_ctas,
+                          void* stream);
+
 /* ds_moe_combine_slots: out[t] = bf16( sum_j w[t,j] * expert_out[slot_of[t,j]] (ascending
  *   slot) + shared_out[t] ) ; shared_out may be NULL. */
 DS_API int ds_moe_combine_slots(const void* expert_out_bf16, const int32_t* slot_of,

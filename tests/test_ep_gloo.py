@@ -72,6 +72,18 @@ class CpuOps:
         from oracle.moe_oracle import _mlp
         return _mlp(x.float(), w1.float(), w2.float())
 
+    def shared_gemm1(self, x, w1, max_ctas=0):
+        I = w1.shape[0] // 2
+        h = x.float() @ w1.float().t()
+        g, u = h[:, :I], h[:, I:]
+        return g / (1.0 + torch.exp(-g)) * u
+
+    def shared_gemm2(self, h, w2, max_ctas=0):
+        return h @ w2.float().t()
+
+    def num_sms(self, device):
+        return 0
+
     def combine_slots(self, back, slot_of, w, shared_out):
         T, k = slot_of.shape
         out = torch.zeros(T, back.shape[1])
