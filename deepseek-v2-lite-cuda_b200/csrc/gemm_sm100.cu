@@ -60,11 +60,8 @@ struct Params {
   const int32_t* out_row_map;
   int* status;
   long long timeout_cycles;
-  // router epilogue
+  // router-logits epilogue
   int router_E;
-  int router_K;
-  int32_t* idx_out;
-  float* w_out;
   float* logits_out;
 };
 
@@ -143,77 +140,40 @@ __device__ __forceinline__ void epilogue_plain(uint32_t tb, bool valid, __nv_bfl
   }
 }
 
-// Router: the B operand is the f32 gate split exactly into three bf16 parts (rows [0,64) hi,
-// [64,128) mid, [128,192) lo, zero above), so accumulator columns c, 64+c, 128+c hold
-// x.hi, x.mid, x.lo for expert c and logit = (hi + mid) + lo keeps f32 accuracy.  Then
-// top-K by logit (ties -> lower expert index) and the softmax weight of each pick, written
-// from registers (src/reference/moe.py:33-43 semantics, canonical tie-break).
-__device__ __forceinline__ bool router_above(float v, int c, float a, int i) {
-  return v > a || (v == a && c < i);
-}
-
-__device__ __forceinline__ void epilogue_router(uint32_t tb, bool valid, int64_t row,
-                                                const Params& p) {
-  float lg[64];
-#pragma unroll
+// Router logits: the B operand is the f32 gate split exactly into three bf16 parts (rows
+// [0,64) hi, [64,128) mid, [128,192) lo, zero above), so accumulator columns c, 64+c, 128+c
+// hold x.hi, x.mid, x.lo for expert c and logit = (hi + mid) + lo keeps f32 accuracy.
+// Written as f32 [rows, E] for the routing kernel.
+__device__ __forceinline__ void epilogue_router_logits(uint32_t tb, bool valid, int64_t row,
+                                                       const Params& p) {
+#pragma unroll 1
   for (int h = 0; h < 2; ++h) {
-    uint32_t v[32];
-    ptx::tmem_ld32(tb + h * 32, v);
-    ptx::tmem_wait_ld(v);
+    uint32_t a[32], b[32];
+    ptx::tmem_ld32(tb + h * 32, a);
+    ptx::tmem_ld32(tb + 64 + h * 32, b);
+    ptx::tmem_wait_ld2(a, b);
+    float lg[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) lg[h * 32 + i] = __uint_as_float(v[i]);
-    ptx::tmem_ld32(tb + 64 + h * 32, v);
-    ptx::tmem_wait_ld(v);
+    for (int i = 0; i < 32; ++i) lg[i] = __uint_as_float(a[i]) + __uint_as_float(b[i]);
+    ptx::tmem_ld32(tb + 128 + h * 32, a);
+    ptx::tmem_wait_ld(a);
+    if (valid) {
+      const int E = p.router_E;
+      float* dst = p.logits_out + row * E + h * 32;
+      if (E == 64) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) lg[h * 32 + i] += __uint_as_float(v[i]);
-    ptx::tmem_ld32(tb + 128 + h * 32, v);
-    ptx::tmem_wait_ld(v);
+        for (int i = 0; i < 8; ++i)
+          d4[i] = make_float4(lg[4 * i] + __uint_as_float(a[4 * i]),
+                              lg[4 * i + 1] + __uint_as_float(a[4 * i + 1]),
+                              lg[4 * i + 2] + __uint_as_float(a[4 * i + 2]),
+                              lg[4 * i + 3] + __uint_as_float(a[4 * i + 3]));
+      } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) lg[h * 32 + i] += __uint_as_float(v[i]);
-  }
-  if (!valid) return;
-  const int E = p.router_E, K = p.router_K;
-  float tv[8];
-  int ti[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    tv[j] = -INFINITY;
-    ti[j] = 0x7fffffff;
-  }
-#pragma unroll
-  for (int e = 0; e < 64; ++e) {
-    if (e < E && router_above(lg[e], e, tv[7], ti[7])) {
-      tv[7] = lg[e];
-      ti[7] = e;
-#pragma unroll
-      for (int j = 7; j > 0; --j) {
-        if (router_above(tv[j], ti[j], tv[j - 1], ti[j - 1])) {
-          const float a = tv[j];
-          tv[j] = tv[j - 1];
-          tv[j - 1] = a;
-          const int b = ti[j];
-          ti[j] = ti[j - 1];
-          ti[j - 1] = b;
-        }
+        for (int i = 0; i < 32; ++i)
+          if (h * 32 + i < E) dst[i] = lg[i] + __uint_as_float(a[i]);
       }
     }
-  }
-  const float mx = tv[0];
-  float sum = 0.f;
-#pragma unroll
-  for (int e = 0; e < 64; ++e)
-    if (e < E) sum += expf(lg[e] - mx);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    if (j < K) {
-      p.idx_out[row * K + j] = ti[j];
-      p.w_out[row * K + j] = expf(tv[j] - mx) / sum;
-    }
-  }
-  if (p.logits_out != nullptr) {
-#pragma unroll
-    for (int e = 0; e < 64; ++e)
-      if (e < E) p.logits_out[row * E + e] = lg[e];
   }
 }
 
@@ -391,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == kSwiGLU) {
         epilogue_swiglu(tb, valid, p.out + orow * p.ldo + ti.nt * 128);
       } else if constexpr (EPI == kRouter) {
-        epilogue_router(tb, valid, orow, p);
+        epilogue_router_logits(tb, valid, orow, p);
       } else {
         epilogue_plain(tb, valid, p.out + orow * p.ldo, ti.nt * p.b_tile_stride, p.b_half1_off);
       }
@@ -477,9 +437,9 @@ int launch(const Problem& pr, cudaStream_t s) {
   DS_REQUIRE(pr.A && pr.B && (router || pr.out), "gemm: null pointer");
   DS_REQUIRE(aligned16(pr.A) && aligned16(pr.B) && (router || aligned16(pr.out)),
              "gemm: A, B and out must be 16-byte aligned");
-  DS_REQUIRE(!router || (pr.idx_out && pr.w_out && pr.router_E >= 1 && pr.router_E <= 64 &&
-                         pr.router_K >= 1 && pr.router_K <= 8 && pr.router_K <= pr.router_E &&
-                         pr.n_tiles == 1 && pr.b_rows == 256 && pr.offsets == nullptr),
+  DS_REQUIRE(!router || (pr.logits_out && pr.router_E >= 1 && pr.router_E <= 64 &&
+                         pr.n_tiles == 1 && pr.b_rows == 256 && pr.offsets == nullptr &&
+                         aligned16(pr.logits_out)),
              "gemm: bad router problem");
   DS_REQUIRE(pr.K > 0 && pr.K % 8 == 0, "gemm: K=%d must be a positive multiple of 8", pr.K);
   DS_REQUIRE(pr.ldo % 8 == 0, "gemm: output leading dimension must be a multiple of 8");
@@ -522,9 +482,6 @@ int launch(const Problem& pr, cudaStream_t s) {
   p.status = device_status_ptr();
   p.timeout_cycles = kDefaultTimeoutCycles;
   p.router_E = pr.router_E;
-  p.router_K = pr.router_K;
-  p.idx_out = pr.idx_out;
-  p.w_out = pr.w_out;
   p.logits_out = pr.logits_out;
   if (p.status == nullptr) return fail(DS_ERR_CUDA, "device status word unavailable");
   const int64_t max_mtiles = (pr.a_rows + BM - 1) / BM + (pr.offsets ? p.groups : 0);

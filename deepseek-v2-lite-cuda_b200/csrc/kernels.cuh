@@ -68,11 +68,9 @@ struct Problem {
   int epilogue;
   const int32_t* out_row_map;  // optional: destination row for each A row
   int max_ctas = 0;            // grid cap (0 = one CTA per SM), leaves SMs to concurrent work
-  // router epilogue (epilogue == kRouter): B = split gate [256, K]; writes top-k per row
+  // router-logits epilogue (epilogue == kRouter): B = split gate [256, K]; writes the f32
+  // logits [a_rows, router_E] to logits_out
   int router_E = 0;
-  int router_K = 0;
-  int32_t* idx_out = nullptr;
-  float* w_out = nullptr;
   float* logits_out = nullptr;
 };
 

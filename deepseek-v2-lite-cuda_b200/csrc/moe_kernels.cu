@@ -21,30 +21,6 @@ __device__ __forceinline__ unsigned lanemask_lt() {
   return m;
 }
 
-// (v, c) ranks above (a, i): larger logit first, equal logits -> lower expert index.
-__device__ __forceinline__ bool ranks_above(float v, int c, float a, int i) {
-  return v > a || (v == a && c < i);
-}
-
-template <int K>
-__device__ __forceinline__ void topk_insert(float (&tv)[K], int (&ti)[K], float v, int c) {
-  if (ranks_above(v, c, tv[K - 1], ti[K - 1])) {
-    tv[K - 1] = v;
-    ti[K - 1] = c;
-#pragma unroll
-    for (int j = K - 1; j > 0; --j) {
-      if (ranks_above(tv[j], ti[j], tv[j - 1], ti[j - 1])) {
-        const float fv = tv[j];
-        tv[j] = tv[j - 1];
-        tv[j - 1] = fv;
-        const int fi = ti[j];
-        ti[j] = ti[j - 1];
-        ti[j - 1] = fi;
-      }
-    }
-  }
-}
-
 // Per-warp ballots give each pick's rank among the block's tokens routed to the same
 // expert (ascending token order), and the block histogram.  ti[j] < 0 marks "no pick".
 template <int K>
@@ -88,65 +64,108 @@ __device__ __forceinline__ void block_rank_hist(const int (&ti)[K], int E, int t
   }
 }
 
-// K1: one thread per token; the block's logits tile is staged in shared memory with
-// coalesced 16-byte loads and each thread walks its row starting at a rotated column so
-// a warp's reads fall in distinct banks.
+// 64-bit selection key: order-preserving bits of the f32 logit in the high word, the
+// inverted expert index in the low word, so the unsigned maximum is the largest logit and,
+// among equal logits, the lowest expert index.
+__device__ __forceinline__ unsigned long long route_key(float v, int e) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(e));
+}
+__device__ __forceinline__ float route_key_value(unsigned long long k) {
+  uint32_t b = static_cast<uint32_t>(k >> 32);
+  b = (b & 0x80000000u) ? (b & 0x7FFFFFFFu) : ~b;
+  return __uint_as_float(b);
+}
+__device__ __forceinline__ int route_key_index(unsigned long long k) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k));
+}
+
+constexpr int kRouteWarps = 8;  // 256 threads per routing block of kRouteTokens tokens
+
+// K1.  Phase 1, one warp per token: lane l holds experts l and l+32; softmax statistics by
+// warp reductions; the K picks by K rounds of a warp-wide 64-bit key maximum (the winner
+// clears its key).  Phase 2, the block's picks in shared memory: warp w takes experts
+// [8w, 8w+8) and, with two ballots per expert (tokens 0..31 and 32..63), produces the rank of
+// every (token, pick) among the block's tokens routed to that expert (ascending token order)
+// and the block histogram.
 template <int K>
-__global__ void __launch_bounds__(kRouteTokens)
-    route_kernel(const float* __restrict__ logits, int T, int E, int vec_ok,
+__global__ void __launch_bounds__(kRouteWarps * 32)
+    route_kernel(const float* __restrict__ logits, int T, int E,
                  int32_t* __restrict__ idx_out, float* __restrict__ w_out,
                  int32_t* __restrict__ counts, int32_t* __restrict__ blk_hist,
                  int32_t* __restrict__ local_rank) {
-  __shared__ __align__(16) float tile[kRouteTokens * kMaxExperts];
-  __shared__ int warp_cnt[kRouteTokens / 32][kMaxExperts];
-  const int tid = threadIdx.x;
+  __shared__ int sel[kRouteTokens][K];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRouteTokens;
-  const int nrows = min(kRouteTokens, T - t0);
-  const int64_t base = static_cast<int64_t>(t0) * E;
-  const int n = nrows * E;
-  if (vec_ok) {
-    const float4* src = reinterpret_cast<const float4*>(logits + base);
-    float4* dst = reinterpret_cast<float4*>(tile);
-    for (int i = tid; i < (n >> 2); i += kRouteTokens) dst[i] = __ldg(src + i);
-  } else {
-    for (int i = tid; i < n; i += kRouteTokens) tile[i] = __ldg(logits + base + i);
-  }
-  __syncthreads();
-
-  const bool valid = tid < nrows;
-  float tv[K];
-  int ti[K];
+  for (int i = warp; i < kRouteTokens; i += kRouteWarps) {
+    const int t = t0 + i;
+    if (t >= T) {
+      if (lane < K) sel[i][lane] = -1;
+      continue;
+    }
+    const float* row = logits + static_cast<int64_t>(t) * E;
+    const float v0 = lane < E ? __ldg(row + lane) : -INFINITY;
+    const float v1 = lane + 32 < E ? __ldg(row + lane + 32) : -INFINITY;
+    unsigned long long k0 = lane < E ? route_key(v0, lane) : 0ull;
+    unsigned long long k1 = lane + 32 < E ? route_key(v1, lane + 32) : 0ull;
+    float mx = fmaxf(v0, v1);
 #pragma unroll
-  for (int j = 0; j < K; ++j) {
-    tv[j] = -INFINITY;
-    ti[j] = INT_MAX;
-  }
-  const int t = t0 + tid;
-  if (valid) {
-    const float* row = tile + tid * E;
-    const int start = tid % E;
-    int c = start;
-    for (int i = 0; i < E; ++i) {
-      topk_insert<K>(tv, ti, row[c], c);
-      if (++c == E) c = 0;
-    }
-    const float mx = tv[0];
-    float sum = 0.f;
-    c = start;
-    for (int i = 0; i < E; ++i) {
-      sum += expf(row[c] - mx);
-      if (++c == E) c = 0;
-    }
+    for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+    float sum = (lane < E ? expf(v0 - mx) : 0.f) + (lane + 32 < E ? expf(v1 - mx) : 0.f);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+    unsigned long long mine = 0ull;
 #pragma unroll
     for (int j = 0; j < K; ++j) {
-      idx_out[static_cast<int64_t>(t) * K + j] = ti[j];
-      w_out[static_cast<int64_t>(t) * K + j] = expf(tv[j] - mx) / sum;
-    }
-  } else {
+      unsigned long long best = k0 > k1 ? k0 : k1;
 #pragma unroll
-    for (int j = 0; j < K; ++j) ti[j] = -1;
+      for (int d = 16; d > 0; d >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, d);
+        best = o > best ? o : best;
+      }
+      if (k0 == best) k0 = 0ull;
+      if (k1 == best) k1 = 0ull;
+      if (lane == j) mine = best;
+    }
+    if (lane < K) {
+      const int e = route_key_index(mine);
+      const int64_t o = static_cast<int64_t>(t) * K + lane;
+      idx_out[o] = e;
+      w_out[o] = expf(route_key_value(mine) - mx) / sum;
+      sel[i][lane] = e;
+    }
   }
-  block_rank_hist<K>(ti, E, t, blockIdx.x, blk_hist, local_rank, counts, warp_cnt);
+  __syncthreads();
+  // phase 2: ranks and histogram
+  int p0[K], p1[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    p0[j] = sel[lane][j];
+    p1[j] = sel[32 + lane][j];
+  }
+  const unsigned lt = lanemask_lt();
+  for (int e = warp * (kMaxExperts / kRouteWarps); e < (warp + 1) * (kMaxExperts / kRouteWarps) && e < E;
+       ++e) {
+    int j0 = -1, j1 = -1;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      if (p0[j] == e) j0 = j;
+      if (p1[j] == e) j1 = j;
+    }
+    const unsigned b0 = __ballot_sync(0xffffffffu, j0 >= 0);
+    const unsigned b1 = __ballot_sync(0xffffffffu, j1 >= 0);
+    const int n0 = __popc(b0);
+    if (local_rank != nullptr) {
+      if (j0 >= 0) local_rank[static_cast<int64_t>(t0 + lane) * K + j0] = __popc(b0 & lt);
+      if (j1 >= 0) local_rank[static_cast<int64_t>(t0 + 32 + lane) * K + j1] = n0 + __popc(b1 & lt);
+    }
+    if (lane == 0) {
+      const int h = n0 + __popc(b1);
+      if (blk_hist != nullptr) blk_hist[static_cast<int64_t>(blockIdx.x) * E + e] = h;
+      if (counts != nullptr && h != 0) atomicAdd(counts + e, h);
+    }
+  }
 }
 
 // Rank/histogram pass over given routing indices (standalone dispatch).
@@ -549,10 +568,9 @@ int grid_for(int64_t work_items, int per_block, int num_sms, int blocks_per_sm) 
 int launch_route(const float* logits, int T, int E, int K, int32_t* idx, float* w,
                  int32_t* counts, int32_t* blk_hist, int32_t* local_rank, cudaStream_t s) {
   if (T <= 0) return DS_OK;
-  const int vec_ok = ((E & 3) == 0 && aligned16(logits)) ? 1 : 0;
   const int grid = route_blocks(T);
-  DS_DISPATCH_K(K, route_kernel<KK><<<grid, kRouteTokens, 0, s>>>(
-                       logits, T, E, vec_ok, idx, w, counts, blk_hist, local_rank));
+  DS_DISPATCH_K(K, route_kernel<KK><<<grid, kRouteWarps * 32, 0, s>>>(
+                       logits, T, E, idx, w, counts, blk_hist, local_rank));
   DS_LAUNCH_CHECK("route_kernel");
   return DS_OK;
 }

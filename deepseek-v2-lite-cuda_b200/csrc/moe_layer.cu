@@ -21,6 +21,7 @@ struct LayerBuffers {
   void* eo;          // bf16 [S, H]
   void* sh;          // bf16 [T, Is]
   void* so;          // bf16 [T, H]
+  float* logits;     // f32 [T, E] (router output when the layer starts from x)
 };
 
 size_t carve_layer(Carve& c, LayerBuffers* b, int T, int H, int E, int K, int I, int Is) {
@@ -40,6 +41,7 @@ size_t carve_layer(Carve& c, LayerBuffers* b, int T, int H, int E, int K, int I,
   x.eo = c.take<__nv_bfloat16>(S * H);
   x.sh = c.take<__nv_bfloat16>(Is > 0 ? static_cast<size_t>(T) * Is : 0);
   x.so = c.take<__nv_bfloat16>(Is > 0 ? static_cast<size_t>(T) * H : 0);
+  x.logits = c.take<float>(static_cast<size_t>(T) * E);
   if (b) *b = x;
   return align_up(c.used, 256);
 }
@@ -115,12 +117,9 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
     r.ldo = 8;
     r.epilogue = ds::gemm::kRouter;
     r.router_E = E;
-    r.router_K = K;
-    r.idx_out = b.idx;
-    r.w_out = b.w;
-    r.logits_out = logits_out;
+    r.logits_out = logits_out != nullptr ? logits_out : b.logits;
     DS_TRY(ds::gemm::launch(r, s));
-    DS_TRY(ds::launch_rank(b.idx, T, E, K, b.blk_hist, b.local_rank, s));
+    DS_TRY(ds::launch_route(r.logits_out, T, E, K, b.idx, b.w, nullptr, b.blk_hist, b.local_rank, s));
   } else {
     DS_TRY(ds::launch_route(router_logits, T, E, K, b.idx, b.w, nullptr, b.blk_hist, b.local_rank, s));
   }

@@ -291,12 +291,14 @@ int ds_router_weight_split(const float* gate_weight, int num_experts, int hidden
 
 int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens, int hidden_size,
                   int num_experts, int top_k, int32_t* topk_indices, float* topk_weights,
-                  float* logits_out, void* stream) {
+                  float* logits, void* stream) {
   DS_REQUIRE(num_tokens >= 0 && hidden_size > 0 && hidden_size % 8 == 0, "moe_router: bad shape");
   DS_REQUIRE(num_experts >= 1 && num_experts <= 64, "moe_router: num_experts must be in [1, 64]");
   DS_REQUIRE(top_k >= 1 && top_k <= 8 && top_k <= num_experts, "moe_router: bad top_k");
   if (num_tokens == 0) return DS_OK;
-  DS_REQUIRE(x_bf16 && w_split_bf16 && topk_indices && topk_weights, "moe_router: null pointer");
+  DS_REQUIRE(x_bf16 && w_split_bf16 && topk_indices && topk_weights && logits,
+             "moe_router: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   ds::gemm::Problem p{};
   p.A = x_bf16;
   p.a_rows = num_tokens;
@@ -314,11 +316,10 @@ int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens, 
   p.ldo = 8;
   p.epilogue = ds::gemm::kRouter;
   p.router_E = num_experts;
-  p.router_K = top_k;
-  p.idx_out = topk_indices;
-  p.w_out = topk_weights;
-  p.logits_out = logits_out;
-  return ds::gemm::launch(p, static_cast<cudaStream_t>(stream));
+  p.logits_out = logits;
+  DS_TRY(ds::gemm::launch(p, s));
+  return ds::launch_route(logits, num_tokens, num_experts, top_k, topk_indices, topk_weights,
+                          nullptr, nullptr, nullptr, s);
 }
 
 int ds_moe_dispatch_routed(const int32_t* topk_indices, const float* topk_weights,

@@ -637,13 +637,16 @@ def router_weight_split(gate_weight: torch.Tensor) -> torch.Tensor:
 
 def moe_router(x: torch.Tensor, w_split: torch.Tensor, num_experts: int, top_k: int = 6,
                logits_out: Optional[torch.Tensor] = None):
-    """Router GEMM (f32-accurate, tensor cores) + top-k: -> (idx [T,k] i32, w [T,k] f32)."""
+    """Router GEMM (f32-accurate, tensor cores) + top-k: -> (idx [T,k] i32, w [T,k] f32).
+    `logits_out` (f32 [T, E]) receives the logits; a scratch buffer is used otherwise."""
     _check_tensor(x, "x", torch.bfloat16, "bfloat16", 2, "[T, H]")
     T, H = x.shape
     idx = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
     w = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
     if T == 0:
         return idx, w
+    if logits_out is None:
+        logits_out = torch.empty((T, num_experts), dtype=torch.float32, device=x.device)
     with _on_device(x):
         _check(_lib.ds_moe_router(_ptr(x), _ptr(w_split), T, H, num_experts, top_k, _ptr(idx),
                                   _ptr(w), _ptr(logits_out), _stream(x)), "moe_router")
