@@ -60,8 +60,8 @@ struct Params {
   const int32_t* out_row_map;
   int* status;
   long long timeout_cycles;
-  // router-logits epilogue
-  int router_E;
+  // router epilogue: K slice = n-tile index, kb_per_split k-blocks per slice
+  int kb_per_split;
   float* logits_out;
 };
 
@@ -140,39 +140,22 @@ __device__ __forceinline__ void epilogue_plain(uint32_t tb, bool valid, __nv_bfl
   }
 }
 
-// Router logits: the B operand is the f32 gate split exactly into three bf16 parts (rows
-// [0,64) hi, [64,128) mid, [128,192) lo, zero above), so accumulator columns c, 64+c, 128+c
-// hold x.hi, x.mid, x.lo for expert c and logit = (hi + mid) + lo keeps f32 accuracy.
-// Written as f32 [rows, E] for the routing kernel.
-__device__ __forceinline__ void epilogue_router_logits(uint32_t tb, bool valid, int64_t row,
-                                                       const Params& p) {
+// Router: the B operand is the f32 gate split exactly into three bf16 parts (rows [0,64) hi,
+// [64,128) mid, [128,192) lo, zero above), and each tile covers one K slice; the epilogue
+// stores the 192 raw accumulator columns of its row as f32 into the slice's partial buffer
+// (the routing kernel sums slices and parts).
+__device__ __forceinline__ void epilogue_router_partials(uint32_t tb, bool valid, float* dst) {
 #pragma unroll 1
-  for (int h = 0; h < 2; ++h) {
-    uint32_t a[32], b[32];
-    ptx::tmem_ld32(tb + h * 32, a);
-    ptx::tmem_ld32(tb + 64 + h * 32, b);
-    ptx::tmem_wait_ld2(a, b);
-    float lg[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) lg[i] = __uint_as_float(a[i]) + __uint_as_float(b[i]);
-    ptx::tmem_ld32(tb + 128 + h * 32, a);
+  for (int cc = 0; cc < 6; ++cc) {
+    uint32_t a[32];
+    ptx::tmem_ld32(tb + cc * 32, a);
     ptx::tmem_wait_ld(a);
     if (valid) {
-      const int E = p.router_E;
-      float* dst = p.logits_out + row * E + h * 32;
-      if (E == 64) {
-        float4* d4 = reinterpret_cast<float4*>(dst);
+      float4* d4 = reinterpret_cast<float4*>(dst + cc * 32);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          d4[i] = make_float4(lg[4 * i] + __uint_as_float(a[4 * i]),
-                              lg[4 * i + 1] + __uint_as_float(a[4 * i + 1]),
-                              lg[4 * i + 2] + __uint_as_float(a[4 * i + 2]),
-                              lg[4 * i + 3] + __uint_as_float(a[4 * i + 3]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (h * 32 + i < E) dst[i] = lg[i] + __uint_as_float(a[i]);
-      }
+      for (int i = 0; i < 8; ++i)
+        d4[i] = make_float4(__uint_as_float(a[4 * i]), __uint_as_float(a[4 * i + 1]),
+                            __uint_as_float(a[4 * i + 2]), __uint_as_float(a[4 * i + 3]));
     }
   }
 }
@@ -251,7 +234,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
         const TileInfo ti = decode_tile(t, p, goff, gtile);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        const int kb0 = EPI == kRouter ? ti.nt * p.kb_per_split : 0;
+        const int kb1 = EPI == kRouter ? min(p.k_blocks, kb0 + p.kb_per_split) : p.k_blocks;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag, p.status,
                               p.timeout_cycles, DS_ERR_TIMEOUT)) {
             ok = false;
@@ -294,7 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        int kb0 = 0, kb1 = p.k_blocks;
+        if constexpr (EPI == kRouter) {
+          const int nt = t % p.n_tiles;
+          kb0 = nt * p.kb_per_split;
+          kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        }
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(full0 + 8u * stage, phase, abort_flag, p.status, p.timeout_cycles,
                               DS_ERR_TIMEOUT)) {
             ok = false;
@@ -307,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             ptx::umma_f16(d, ptx::sw128_kmajor_desc(a0 + kk * 32u),
                           ptx::sw128_kmajor_desc(b0 + kk * 32u), idesc,
-                          (kb | kk) != 0 ? 1u : 0u);
+                          (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           ptx::umma_commit(empty0 + 8u * stage);
           if (++stage == STAGES) {
@@ -351,7 +342,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == kSwiGLU) {
         epilogue_swiglu(tb, valid, p.out + orow * p.ldo + ti.nt * 128);
       } else if constexpr (EPI == kRouter) {
-        epilogue_router_logits(tb, valid, orow, p);
+        epilogue_router_partials(
+            tb, valid, p.logits_out + (static_cast<int64_t>(ti.nt) * p.dense_rows + orow) * 192);
       } else {
         epilogue_plain(tb, valid, p.out + orow * p.ldo, ti.nt * p.b_tile_stride, p.b_half1_off);
       }
@@ -437,8 +429,8 @@ int launch(const Problem& pr, cudaStream_t s) {
   DS_REQUIRE(pr.A && pr.B && (router || pr.out), "gemm: null pointer");
   DS_REQUIRE(aligned16(pr.A) && aligned16(pr.B) && (router || aligned16(pr.out)),
              "gemm: A, B and out must be 16-byte aligned");
-  DS_REQUIRE(!router || (pr.logits_out && pr.router_E >= 1 && pr.router_E <= 64 &&
-                         pr.n_tiles == 1 && pr.b_rows == 256 && pr.offsets == nullptr &&
+  DS_REQUIRE(!router || (pr.logits_out && pr.n_tiles >= 1 && pr.b_rows == 256 &&
+                         pr.b_tile_stride == 0 && pr.offsets == nullptr &&
                          aligned16(pr.logits_out)),
              "gemm: bad router problem");
   DS_REQUIRE(pr.K > 0 && pr.K % 8 == 0, "gemm: K=%d must be a positive multiple of 8", pr.K);
@@ -481,7 +473,7 @@ int launch(const Problem& pr, cudaStream_t s) {
   p.out_row_map = pr.out_row_map;
   p.status = device_status_ptr();
   p.timeout_cycles = kDefaultTimeoutCycles;
-  p.router_E = pr.router_E;
+  p.kb_per_split = (p.k_blocks + pr.n_tiles - 1) / pr.n_tiles;
   p.logits_out = pr.logits_out;
   if (p.status == nullptr) return fail(DS_ERR_CUDA, "device status word unavailable");
   const int64_t max_mtiles = (pr.a_rows + BM - 1) / BM + (pr.offsets ? p.groups : 0);

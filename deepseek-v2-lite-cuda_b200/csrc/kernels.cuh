@@ -18,6 +18,16 @@ inline int route_blocks(int num_tokens) { return (num_tokens + kRouteTokens - 1)
 int launch_route(const float* logits, int T, int E, int K, int32_t* idx, float* w,
                  int32_t* counts, int32_t* blk_hist, int32_t* local_rank, cudaStream_t s);
 
+// Same from the router GEMM's raw partial accumulators (`nsplit` K slices of [T, 192] f32:
+// x.hi | x.mid | x.lo per expert); optionally writes the summed logits [T, E].
+int launch_route_partials(const float* partials, int nsplit, int T, int E, int K,
+                          float* logits_out, int32_t* idx, float* w, int32_t* counts,
+                          int32_t* blk_hist, int32_t* local_rank, cudaStream_t s);
+
+// Router GEMM: split K slices; partial buffer floats per token.
+constexpr int kRouterSplits = 2;
+constexpr int kRouterPartCols = 192;
+
 // idx [T, K] -> blk_hist [nblk, E], local_rank [T, K].
 int launch_rank(const int32_t* idx, int T, int E, int K, int32_t* blk_hist,
                 int32_t* local_rank, cudaStream_t s);
@@ -68,9 +78,9 @@ struct Problem {
   int epilogue;
   const int32_t* out_row_map;  // optional: destination row for each A row
   int max_ctas = 0;            // grid cap (0 = one CTA per SM), leaves SMs to concurrent work
-  // router-logits epilogue (epilogue == kRouter): B = split gate [256, K]; writes the f32
-  // logits [a_rows, router_E] to logits_out
-  int router_E = 0;
+  // router epilogue (epilogue == kRouter): B = split gate [256, K]; n_tiles = number of K
+  // slices; slice s writes its raw accumulator columns [0, 192) as f32 to
+  // logits_out + (s * a_rows + row) * 192
   float* logits_out = nullptr;
 };
 

@@ -64,77 +64,99 @@ __device__ __forceinline__ void block_rank_hist(const int (&ti)[K], int E, int t
   }
 }
 
-// 64-bit selection key: order-preserving bits of the f32 logit in the high word, the
-// inverted expert index in the low word, so the unsigned maximum is the largest logit and,
-// among equal logits, the lowest expert index.
-__device__ __forceinline__ unsigned long long route_key(float v, int e) {
-  uint32_t b = __float_as_uint(v);
-  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(e));
-}
-__device__ __forceinline__ float route_key_value(unsigned long long k) {
-  uint32_t b = static_cast<uint32_t>(k >> 32);
-  b = (b & 0x80000000u) ? (b & 0x7FFFFFFFu) : ~b;
-  return __uint_as_float(b);
-}
-__device__ __forceinline__ int route_key_index(unsigned long long k) {
-  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k));
+constexpr int kRouteWarps = 32;  // 1024 threads: two tokens per warp, one per half-warp
+
+// Logit of (token t, expert e).  PARTIALS: the router GEMM's raw accumulators, `nsplit` K
+// slices of [T, 192] f32 holding x.hi | x.mid | x.lo per expert; the logit is the sum over
+// slices of (hi + mid) + lo, in that order.  Otherwise a plain f32 [T, E] row.
+template <bool PARTIALS>
+__device__ __forceinline__ float load_logit(const float* __restrict__ src, int64_t t, int e,
+                                            int E, int T, int nsplit) {
+  if constexpr (PARTIALS) {
+    float acc = 0.f;
+    for (int k = 0; k < nsplit; ++k) {
+      const float* r = src + (static_cast<int64_t>(k) * T + t) * 192;
+      acc += (__ldg(r + e) + __ldg(r + 64 + e)) + __ldg(r + 128 + e);
+    }
+    return acc;
+  } else {
+    return __ldg(src + t * E + e);
+  }
 }
 
-constexpr int kRouteWarps = 8;  // 256 threads per routing block of kRouteTokens tokens
-
-// K1.  Phase 1, one warp per token: lane l holds experts l and l+32; softmax statistics by
-// warp reductions; the K picks by K rounds of a warp-wide 64-bit key maximum (the winner
-// clears its key).  Phase 2, the block's picks in shared memory: warp w takes experts
-// [8w, 8w+8) and, with two ballots per expert (tokens 0..31 and 32..63), produces the rank of
-// every (token, pick) among the block's tokens routed to that expert (ascending token order)
-// and the block histogram.
-template <int K>
+// K1.  Phase 1, one half-warp per token: lane l of the half holds experts l, l+16, l+32, l+48;
+// the softmax statistics come from half-warp reductions; each of the K picks is the half-warp
+// maximum of the remaining logits, and among equal maxima the lowest expert index (found with
+// one ballot per expert quarter).  Phase 2, the block's picks in shared memory: warp w takes
+// experts 2w and 2w+1 and, with two ballots per expert (tokens 0..31 and 32..63), produces
+// the rank of every (token, pick) among the block's tokens routed to that expert (ascending
+// token order) and the block histogram.
+template <int K, bool PARTIALS>
 __global__ void __launch_bounds__(kRouteWarps * 32)
-    route_kernel(const float* __restrict__ logits, int T, int E,
-                 int32_t* __restrict__ idx_out, float* __restrict__ w_out,
-                 int32_t* __restrict__ counts, int32_t* __restrict__ blk_hist,
-                 int32_t* __restrict__ local_rank) {
+    route_kernel(const float* __restrict__ src, int T, int E, int nsplit,
+                 float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
+                 float* __restrict__ w_out, int32_t* __restrict__ counts,
+                 int32_t* __restrict__ blk_hist, int32_t* __restrict__ local_rank) {
   __shared__ int sel[kRouteTokens][K];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, hl = lane & 15;
   const int t0 = blockIdx.x * kRouteTokens;
-  for (int i = warp; i < kRouteTokens; i += kRouteWarps) {
-    const int t = t0 + i;
-    if (t >= T) {
-      if (lane < K) sel[i][lane] = -1;
-      continue;
-    }
-    const float* row = logits + static_cast<int64_t>(t) * E;
-    const float v0 = lane < E ? __ldg(row + lane) : -INFINITY;
-    const float v1 = lane + 32 < E ? __ldg(row + lane + 32) : -INFINITY;
-    unsigned long long k0 = lane < E ? route_key(v0, lane) : 0ull;
-    unsigned long long k1 = lane + 32 < E ? route_key(v1, lane + 32) : 0ull;
-    float mx = fmaxf(v0, v1);
+  const int i = warp * 2 + half;  // token slot in the block
+  const int64_t t = t0 + i;
+  const bool valid = t < T;
+  float v[4];
+  unsigned alive = 0;
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
-    float sum = (lane < E ? expf(v0 - mx) : 0.f) + (lane + 32 < E ? expf(v1 - mx) : 0.f);
+  for (int q = 0; q < 4; ++q) {
+    const int e = hl + 16 * q;
+    const bool ok = valid && e < E;
+    v[q] = ok ? load_logit<PARTIALS>(src, t, e, E, T, nsplit) : -INFINITY;
+    if (ok) alive |= 1u << q;
+    if (ok && logits_out != nullptr) logits_out[t * E + e] = v[q];
+  }
+  float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
-    unsigned long long mine = 0ull;
+  for (int d = 8; d > 0; d >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+  float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      unsigned long long best = k0 > k1 ? k0 : k1;
+  for (int q = 0; q < 4; ++q)
+    if (alive & (1u << q)) sum += expf(v[q] - mx);
 #pragma unroll
-      for (int d = 16; d > 0; d >>= 1) {
-        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, d);
-        best = o > best ? o : best;
+  for (int d = 8; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+  int pick_e = -1;
+  float pick_v = 0.f;
+  const unsigned shift = half * 16;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    float best = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (alive & (1u << q)) best = fmaxf(best, v[q]);
+#pragma unroll
+    for (int d = 8; d > 0; d >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, d));
+    int win_q = -1, win_l = 0;
+#pragma unroll
+    for (int q = 3; q >= 0; --q) {
+      const unsigned b = (__ballot_sync(0xffffffffu, (alive & (1u << q)) && v[q] == best) >> shift) &
+                         0xFFFFu;
+      if (b != 0u) {
+        win_q = q;
+        win_l = __ffs(b) - 1;
       }
-      if (k0 == best) k0 = 0ull;
-      if (k1 == best) k1 = 0ull;
-      if (lane == j) mine = best;
     }
-    if (lane < K) {
-      const int e = route_key_index(mine);
-      const int64_t o = static_cast<int64_t>(t) * K + lane;
-      idx_out[o] = e;
-      w_out[o] = expf(route_key_value(mine) - mx) / sum;
-      sel[i][lane] = e;
+    if (win_q >= 0 && hl == win_l) alive &= ~(1u << win_q);
+    if (hl == j) {
+      pick_e = win_q >= 0 ? win_l + 16 * win_q : -1;
+      pick_v = best;
     }
+  }
+  if (hl < K) {
+    if (valid) {
+      const int64_t o = t * K + hl;
+      idx_out[o] = pick_e;
+      w_out[o] = expf(pick_v - mx) / sum;
+    }
+    sel[i][hl] = valid ? pick_e : -1;
   }
   __syncthreads();
   // phase 2: ranks and histogram
@@ -145,8 +167,10 @@ __global__ void __launch_bounds__(kRouteWarps * 32)
     p1[j] = sel[32 + lane][j];
   }
   const unsigned lt = lanemask_lt();
-  for (int e = warp * (kMaxExperts / kRouteWarps); e < (warp + 1) * (kMaxExperts / kRouteWarps) && e < E;
-       ++e) {
+#pragma unroll
+  for (int ee = 0; ee < kMaxExperts / kRouteWarps; ++ee) {
+    const int e = warp * (kMaxExperts / kRouteWarps) + ee;
+    if (e >= E) break;
     int j0 = -1, j1 = -1;
 #pragma unroll
     for (int j = 0; j < K; ++j) {
@@ -569,8 +593,19 @@ int launch_route(const float* logits, int T, int E, int K, int32_t* idx, float* 
                  int32_t* counts, int32_t* blk_hist, int32_t* local_rank, cudaStream_t s) {
   if (T <= 0) return DS_OK;
   const int grid = route_blocks(T);
-  DS_DISPATCH_K(K, route_kernel<KK><<<grid, kRouteWarps * 32, 0, s>>>(
-                       logits, T, E, idx, w, counts, blk_hist, local_rank));
+  DS_DISPATCH_K(K, route_kernel<KK, false><<<grid, kRouteWarps * 32, 0, s>>>(
+                       logits, T, E, 0, nullptr, idx, w, counts, blk_hist, local_rank));
+  DS_LAUNCH_CHECK("route_kernel");
+  return DS_OK;
+}
+
+int launch_route_partials(const float* partials, int nsplit, int T, int E, int K,
+                          float* logits_out, int32_t* idx, float* w, int32_t* counts,
+                          int32_t* blk_hist, int32_t* local_rank, cudaStream_t s) {
+  if (T <= 0) return DS_OK;
+  const int grid = route_blocks(T);
+  DS_DISPATCH_K(K, route_kernel<KK, true><<<grid, kRouteWarps * 32, 0, s>>>(
+                       partials, T, E, nsplit, logits_out, idx, w, counts, blk_hist, local_rank));
   DS_LAUNCH_CHECK("route_kernel");
   return DS_OK;
 }

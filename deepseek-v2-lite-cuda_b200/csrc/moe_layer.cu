@@ -21,7 +21,7 @@ struct LayerBuffers {
   void* eo;          // bf16 [S, H]
   void* sh;          // bf16 [T, Is]
   void* so;          // bf16 [T, H]
-  float* logits;     // f32 [T, E] (router output when the layer starts from x)
+  float* router_part;  // f32 [kRouterSplits, T, 192] router GEMM partials (layer from x)
 };
 
 size_t carve_layer(Carve& c, LayerBuffers* b, int T, int H, int E, int K, int I, int Is) {
@@ -41,7 +41,7 @@ size_t carve_layer(Carve& c, LayerBuffers* b, int T, int H, int E, int K, int I,
   x.eo = c.take<__nv_bfloat16>(S * H);
   x.sh = c.take<__nv_bfloat16>(Is > 0 ? static_cast<size_t>(T) * Is : 0);
   x.so = c.take<__nv_bfloat16>(Is > 0 ? static_cast<size_t>(T) * H : 0);
-  x.logits = c.take<float>(static_cast<size_t>(T) * E);
+  x.router_part = c.take<float>(static_cast<size_t>(kRouterSplits) * T * kRouterPartCols);
   if (b) *b = x;
   return align_up(c.used, 256);
 }
@@ -108,18 +108,18 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
     r.b_rows = 256;
     r.offsets = nullptr;
     r.groups = 1;
-    r.n_tiles = 1;
+    r.n_tiles = ds::kRouterSplits;
     r.b_rows_per_group = 256;
-    r.b_tile_stride = 256;
+    r.b_tile_stride = 0;
     r.b_half1_off = 128;
     r.weight_group_mod = 1;
     r.out = nullptr;
     r.ldo = 8;
     r.epilogue = ds::gemm::kRouter;
-    r.router_E = E;
-    r.logits_out = logits_out != nullptr ? logits_out : b.logits;
+    r.logits_out = b.router_part;
     DS_TRY(ds::gemm::launch(r, s));
-    DS_TRY(ds::launch_route(r.logits_out, T, E, K, b.idx, b.w, nullptr, b.blk_hist, b.local_rank, s));
+    DS_TRY(ds::launch_route_partials(b.router_part, ds::kRouterSplits, T, E, K, logits_out, b.idx,
+                                     b.w, nullptr, b.blk_hist, b.local_rank, s));
   } else {
     DS_TRY(ds::launch_route(router_logits, T, E, K, b.idx, b.w, nullptr, b.blk_hist, b.local_rank, s));
   }

@@ -289,16 +289,25 @@ int ds_router_weight_split(const float* gate_weight, int num_experts, int hidden
   return DS_OK;
 }
 
+size_t ds_moe_router_workspace_size(int num_tokens) {
+  return ds::align_up(sizeof(float) * ds::kRouterSplits * static_cast<size_t>(num_tokens) *
+                          ds::kRouterPartCols,
+                      256);
+}
+
 int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens, int hidden_size,
                   int num_experts, int top_k, int32_t* topk_indices, float* topk_weights,
-                  float* logits, void* stream) {
+                  float* logits_out, void* workspace, size_t workspace_bytes, void* stream) {
   DS_REQUIRE(num_tokens >= 0 && hidden_size > 0 && hidden_size % 8 == 0, "moe_router: bad shape");
   DS_REQUIRE(num_experts >= 1 && num_experts <= 64, "moe_router: num_experts must be in [1, 64]");
   DS_REQUIRE(top_k >= 1 && top_k <= 8 && top_k <= num_experts, "moe_router: bad top_k");
   if (num_tokens == 0) return DS_OK;
-  DS_REQUIRE(x_bf16 && w_split_bf16 && topk_indices && topk_weights && logits,
-             "moe_router: null pointer");
+  DS_REQUIRE(x_bf16 && w_split_bf16 && topk_indices && topk_weights, "moe_router: null pointer");
+  if (workspace == nullptr || workspace_bytes < ds_moe_router_workspace_size(num_tokens))
+    return fail(DS_ERR_WORKSPACE, "moe_router: workspace needs %zu bytes",
+                ds_moe_router_workspace_size(num_tokens));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
   ds::gemm::Problem p{};
   p.A = x_bf16;
   p.a_rows = num_tokens;
@@ -307,19 +316,19 @@ int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens, 
   p.b_rows = 256;
   p.offsets = nullptr;
   p.groups = 1;
-  p.n_tiles = 1;
+  p.n_tiles = ds::kRouterSplits;
   p.b_rows_per_group = 256;
-  p.b_tile_stride = 256;
+  p.b_tile_stride = 0;
   p.b_half1_off = 128;
   p.weight_group_mod = 1;
   p.out = nullptr;
   p.ldo = 8;
   p.epilogue = ds::gemm::kRouter;
-  p.router_E = num_experts;
-  p.logits_out = logits;
+  p.logits_out = part;
   DS_TRY(ds::gemm::launch(p, s));
-  return ds::launch_route(logits, num_tokens, num_experts, top_k, topk_indices, topk_weights,
-                          nullptr, nullptr, nullptr, s);
+  return ds::launch_route_partials(part, ds::kRouterSplits, num_tokens, num_experts, top_k,
+                                   logits_out, topk_indices, topk_weights, nullptr, nullptr,
+                                   nullptr, s);
 }
 
 int ds_moe_dispatch_routed(const int32_t* topk_indices, const float* topk_weights,

@@ -70,7 +70,8 @@ SIGNATURES = {
     "ds_router_weight_split": (_i, [_vp, _i, _i, _vp, _vp]),
     "ds_dense_gemm1_swiglu": (_i, [_vp, _i, _vp, _i, _i, _vp, _i, _vp]),
     "ds_dense_gemm2": (_i, [_vp, _i, _vp, _i, _i, _vp, _i, _vp]),
-    "ds_moe_router": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "ds_moe_router_workspace_size": (_sz, [_i]),
+    "ds_moe_router": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ds_moe_dispatch_routed": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz,
                                     _vp]),
     "ds_moe_layer_forward_from_x": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i,
@@ -638,18 +639,19 @@ def router_weight_split(gate_weight: torch.Tensor) -> torch.Tensor:
 def moe_router(x: torch.Tensor, w_split: torch.Tensor, num_experts: int, top_k: int = 6,
                logits_out: Optional[torch.Tensor] = None):
     """Router GEMM (f32-accurate, tensor cores) + top-k: -> (idx [T,k] i32, w [T,k] f32).
-    `logits_out` (f32 [T, E]) receives the logits; a scratch buffer is used otherwise."""
+    `logits_out` (f32 [T, E]) optionally receives the summed logits."""
     _check_tensor(x, "x", torch.bfloat16, "bfloat16", 2, "[T, H]")
     T, H = x.shape
     idx = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
     w = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
     if T == 0:
         return idx, w
-    if logits_out is None:
-        logits_out = torch.empty((T, num_experts), dtype=torch.float32, device=x.device)
+    need = _lib.ds_moe_router_workspace_size(T)
+    ws = _workspace(need, x.device)
     with _on_device(x):
         _check(_lib.ds_moe_router(_ptr(x), _ptr(w_split), T, H, num_experts, top_k, _ptr(idx),
-                                  _ptr(w), _ptr(logits_out), _stream(x)), "moe_router")
+                                  _ptr(w), _ptr(logits_out), _ptr(ws), need, _stream(x)),
+               "moe_router")
     return idx, w
 
 

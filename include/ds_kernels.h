@@ -229,15 +229,17 @@ DS_API int ds_moe_route_dispatch(const float* router_logits, const void* x_bf16,
 
 /* ds_moe_router: router logits x @ gate^T with f32 accuracy on the tensor cores (the f32
  *   gate is pre-split by ds_router_weight_split into bf16 hi/mid/lo parts that sum to it;
- *   the GEMM epilogue adds the three partial logits) written to `logits` f32 [T, E], then
- *   the top-k of ds_moe_routing.  Replaces the f32 F.linear + moe_routing pair of
- *   src/kernels/moe_fused.py:131-137.
+ *   the GEMM writes per-K-slice partial accumulators into `workspace`, the routing kernel
+ *   sums them), then the top-k of ds_moe_routing.  Replaces the f32 F.linear + moe_routing
+ *   pair of src/kernels/moe_fused.py:131-137.  logits_out f32 [T, E] may be NULL.
  * ds_router_weight_split: gate f32 [E, H] -> w_split bf16 [256, H] (rows e, 64+e, 128+e). */
 DS_API int ds_router_weight_split(const float* gate_weight, int num_experts, int hidden_size,
                                   void* w_split_bf16, void* stream);
+DS_API size_t ds_moe_router_workspace_size(int num_tokens);
 DS_API int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens,
                          int hidden_size, int num_experts, int top_k, int32_t* topk_indices,
-                         float* topk_weights, float* logits, void* stream);
+                         float* topk_weights, float* logits_out, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /* ds_moe_dispatch_routed: ds_moe_route_dispatch for routing that is already computed
  *   (topk_indices/weights [T, k]); workspace size as ds_moe_route_dispatch_workspace_size. */
