@@ -262,20 +262,26 @@ def run_ours(args, rank, world, local_rank):
     phase_ms = {n: sum(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(args.steps)) / args.steps
                 for i, n in enumerate(names)}
 
-    # end to end through the public API: pinned host input -> device -> layer -> pinned host
+    # end to end through the public API (moe_fused.HostPipeline): every step copies its
+    # tokens from pinned host memory to the device and its output back to pinned host memory;
+    # copies of neighbouring steps overlap the compute on separate copy streams.
+    from moe_fused import HostPipeline
     xh = x_cpu.pin_memory()
-    oh = torch.empty(T_GLOBAL, H, dtype=torch.bfloat16).pin_memory()
-    for _ in range(max(1, args.warmup)):
-        oh.copy_(layer(xh.to(dev, non_blocking=True)), non_blocking=True)
+    oh = [torch.empty(T_GLOBAL, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(layer, T_GLOBAL, H, dev)
+    for i in range(max(1, args.warmup)):
+        pipe.submit(xh, oh[i % 2])
+    pipe.synchronize()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        oh.copy_(layer(xh.to(dev, non_blocking=True)), non_blocking=True)
-    e1.record()
+    e0.record(pipe.h2d)
+    for i in range(args.steps):
+        pipe.submit(xh, oh[i % 2])
+    e1.record(pipe.d2h)
+    pipe.synchronize()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
     clocks = sampler.stop()
@@ -335,23 +341,35 @@ def run_ours(args, rank, world, local_rank):
         op_report(args.op_report, dev)
 
 
-def _time(fn, iters=20, warm=3):
-    for _ in range(warm):
-        fn()
+def _time(fn, iters=20, warm=3, reps=5):
+    """Device seconds per call: `iters` calls captured in one CUDA graph (so host launch
+    overhead is not measured), replayed `reps` times between CUDA events."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
     torch.cuda.synchronize()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(iters):
-        fn()
+    for _ in range(reps):
+        g.replay()
     b.record()
     torch.cuda.synchronize()
-    return a.elapsed_time(b) / iters / 1000.0
+    return a.elapsed_time(b) / (iters * reps) / 1000.0
 
 
 def op_report(path, dev):
-    """Per-op timings and roofline fractions of the bandwidth kernels at their BASELINE
-    sizes (configs 1 and 3), appended as JSON lines to `path`."""
+    """Per-op device timings (CUDA-graph replay) and roofline fractions of the bandwidth
+    kernels at their BASELINE sizes (configs 1 and 3), appended as JSON lines to `path`."""
     import ds_kernels
     import synthetic
     pk = peaks()

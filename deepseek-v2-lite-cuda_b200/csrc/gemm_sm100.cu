@@ -38,13 +38,16 @@ constexpr uint32_t B_HALF_BYTES = 128 * BK * 2;  // 16 KiB
 constexpr uint32_t B_BYTES = BN * BK * 2;        // 32 KiB
 constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
 constexpr int kMaxGroups = 512;
+constexpr int kMaxProblems = 2;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTailBytes = 256;  // barriers + tmem holder + flags
+constexpr uint32_t kTailBytes = 256;  // barriers + tmem holder + flags + problem tile starts
+constexpr int kGroupStride = kMaxGroups + 1;
 constexpr size_t kSmemBytes = 1024 + STAGES * (A_BYTES + B_BYTES) + kTailBytes +
-                              2 * (kMaxGroups + 1) * sizeof(int);
+                              2 * kMaxProblems * kGroupStride * sizeof(int);
 constexpr long long kDefaultTimeoutCycles = 4000000000LL;  // ~2 s at 2 GHz
 
-struct Params {
+// One GEMM problem of a launch (fields as in Problem, kernels.cuh).
+struct ProbParams {
   const int32_t* offsets;
   int groups;
   int dense_rows;
@@ -56,13 +59,18 @@ struct Params {
   int weight_group_mod;
   __nv_bfloat16* out;
   int ldo;
-  int epilogue;
   const int32_t* out_row_map;
+  int kb_per_split;   // router: k-blocks per K slice (the n-tile index is the slice)
+  float* logits_out;  // router: partial accumulators
+};
+
+// A launch serves up to two problems with the same epilogue; their tiles are enumerated one
+// problem after the other.
+struct Params {
+  ProbParams pr[kMaxProblems];
+  int nprob;
   int* status;
   long long timeout_cycles;
-  // router epilogue: K slice = n-tile index, kb_per_split k-blocks per slice
-  int kb_per_split;
-  float* logits_out;
 };
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
@@ -73,26 +81,38 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 struct TileInfo {
+  int prob;
   int row0;
   int rows;
   int brow0;
   int nt;
 };
 
+__device__ __forceinline__ const ProbParams& prob_params(const Params& p, int pb) {
+  return pb ? p.pr[1] : p.pr[0];
+}
+
+// goff/gtile: per problem, kGroupStride row offsets and m-tile prefix; pstart[pb] = first
+// tile of problem pb.
 __device__ __forceinline__ TileInfo decode_tile(int t, const Params& p, const int* goff,
-                                                const int* gtile) {
+                                                const int* gtile, const int* pstart) {
   TileInfo ti;
-  const int mtg = t / p.n_tiles;
-  ti.nt = t - mtg * p.n_tiles;
-  int lo = 0, hi = p.groups;
+  ti.prob = (p.nprob > 1 && t >= pstart[1]) ? 1 : 0;
+  const ProbParams& q = prob_params(p, ti.prob);
+  const int* go = goff + ti.prob * kGroupStride;
+  const int* gt = gtile + ti.prob * kGroupStride;
+  const int tt = t - pstart[ti.prob];
+  const int mtg = tt / q.n_tiles;
+  ti.nt = tt - mtg * q.n_tiles;
+  int lo = 0, hi = q.groups;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (gtile[mid] <= mtg) lo = mid;
+    if (gt[mid] <= mtg) lo = mid;
     else hi = mid;
   }
-  ti.row0 = goff[lo] + (mtg - gtile[lo]) * BM;
-  ti.rows = min(BM, goff[lo + 1] - ti.row0);
-  ti.brow0 = (lo % p.weight_group_mod) * p.b_rows_per_group + ti.nt * p.b_tile_stride;
+  ti.row0 = go[lo] + (mtg - gt[lo]) * BM;
+  ti.rows = min(BM, go[lo + 1] - ti.row0);
+  ti.brow0 = (lo % q.weight_group_mod) * q.b_rows_per_group + ti.nt * q.b_tile_stride;
   return ti;
 }
 
@@ -162,8 +182,10 @@ __device__ __forceinline__ void epilogue_router_partials(uint32_t tb, bool valid
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const Params p) {
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA0,
+                        const __grid_constant__ CUtensorMap tmB0,
+                        const __grid_constant__ CUtensorMap tmA1,
+                        const __grid_constant__ CUtensorMap tmB1, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -178,15 +200,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 8 * (2 * STAGES + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* never_flag = abort_flag + 1;
+  int* pstart = const_cast<int*>(reinterpret_cast<volatile int*>(never_flag + 1));  // [3]
   int* goff = reinterpret_cast<int*>(tail + kTailBytes);
-  int* gtile = goff + (kMaxGroups + 1);
+  int* gtile = goff + kMaxProblems * kGroupStride;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int G = p.groups;
 
-  for (int i = threadIdx.x; i <= G; i += kThreads)
-    goff[i] = p.offsets ? __ldg(p.offsets + i) : (i == 0 ? 0 : p.dense_rows);
+  for (int pb = 0; pb < p.nprob; ++pb) {
+    const ProbParams& q = prob_params(p, pb);
+    for (int i = threadIdx.x; i <= q.groups; i += kThreads)
+      goff[pb * kGroupStride + i] = q.offsets ? __ldg(q.offsets + i) : (i == 0 ? 0 : q.dense_rows);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(full0 + 8u * s, 1);
@@ -202,8 +227,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    ptx::prefetch_tmap(&tmA);
-    ptx::prefetch_tmap(&tmB);
+    ptx::prefetch_tmap(&tmA0);
+    ptx::prefetch_tmap(&tmB0);
+    if (p.nprob > 1) {
+      ptx::prefetch_tmap(&tmA1);
+      ptx::prefetch_tmap(&tmB1);
+    }
   }
   if (warp == 1) {
     ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kTmemCols);
@@ -211,19 +240,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int g = 0; g < G; ++g) {
-      gtile[g] = acc;
-      const int m = goff[g + 1] - goff[g];
-      acc += m > 0 ? (m + BM - 1) / BM : 0;
+    int start = 0;
+    for (int pb = 0; pb < p.nprob; ++pb) {
+      const ProbParams& q = prob_params(p, pb);
+      int* go = goff + pb * kGroupStride;
+      int* gt = gtile + pb * kGroupStride;
+      int acc = 0;
+      for (int g = 0; g < q.groups; ++g) {
+        gt[g] = acc;
+        const int m = go[g + 1] - go[g];
+        acc += m > 0 ? (m + BM - 1) / BM : 0;
+      }
+      gt[q.groups] = acc;
+      pstart[pb] = start;
+      start += acc * q.n_tiles;
     }
-    gtile[G] = acc;
+    pstart[p.nprob] = start;
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const int total_tiles = gtile[G] * p.n_tiles;
+  const int total_tiles = pstart[p.nprob];
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -233,9 +271,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t used_mask = 0, phase_mask = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-        const TileInfo ti = decode_tile(t, p, goff, gtile);
-        const int kb0 = EPI == kRouter ? ti.nt * p.kb_per_split : 0;
-        const int kb1 = EPI == kRouter ? min(p.k_blocks, kb0 + p.kb_per_split) : p.k_blocks;
+        const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
+        const ProbParams& q = prob_params(p, ti.prob);
+        const CUtensorMap* tA = ti.prob ? &tmA1 : &tmA0;
+        const CUtensorMap* tB = ti.prob ? &tmB1 : &tmB0;
+        const int kb0 = EPI == kRouter ? ti.nt * q.kb_per_split : 0;
+        const int kb1 = EPI == kRouter ? min(q.k_blocks, kb0 + q.kb_per_split) : q.k_blocks;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag, p.status,
                               p.timeout_cycles, DS_ERR_TIMEOUT)) {
@@ -246,9 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
           const uint32_t a_dst = sA + stage * A_BYTES;
           const uint32_t b_dst = sB + stage * B_BYTES;
-          ptx::tma_load_2d(a_dst, &tmA, fb, kb * BK, ti.row0);
-          ptx::tma_load_2d(b_dst, &tmB, fb, kb * BK, ti.brow0);
-          ptx::tma_load_2d(b_dst + B_HALF_BYTES, &tmB, fb, kb * BK, ti.brow0 + p.b_half1_off);
+          ptx::tma_load_2d(a_dst, tA, fb, kb * BK, ti.row0);
+          ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
+          ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
           used_mask |= 1u << stage;
           phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -279,11 +320,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        int kb0 = 0, kb1 = p.k_blocks;
+        const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
+        const ProbParams& q = prob_params(p, ti.prob);
+        int kb0 = 0, kb1 = q.k_blocks;
         if constexpr (EPI == kRouter) {
-          const int nt = t % p.n_tiles;
-          kb0 = nt * p.kb_per_split;
-          kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+          kb0 = ti.nt * q.kb_per_split;
+          kb1 = min(q.k_blocks, kb0 + q.kb_per_split);
         }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(full0 + 8u * stage, phase, abort_flag, p.status, p.timeout_cycles,
@@ -324,7 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile(t, p, goff, gtile);
+      const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
+      const ProbParams& qp = prob_params(p, ti.prob);
       int ok = 1;
       if (lane == 0)
         ok = ptx::mbar_wait(tfull0 + 8u * acc, acc_phase, abort_flag, p.status,
@@ -338,14 +381,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
       const bool valid = r < ti.rows;
       int64_t orow = ti.row0 + r;
-      if (valid && p.out_row_map != nullptr) orow = __ldg(p.out_row_map + orow);
+      if (valid && qp.out_row_map != nullptr) orow = __ldg(qp.out_row_map + orow);
       if constexpr (EPI == kSwiGLU) {
-        epilogue_swiglu(tb, valid, p.out + orow * p.ldo + ti.nt * 128);
+        epilogue_swiglu(tb, valid, qp.out + orow * qp.ldo + ti.nt * 128);
       } else if constexpr (EPI == kRouter) {
         epilogue_router_partials(
-            tb, valid, p.logits_out + (static_cast<int64_t>(ti.nt) * p.dense_rows + orow) * 192);
+            tb, valid, qp.logits_out + (static_cast<int64_t>(ti.nt) * qp.dense_rows + orow) * 192);
       } else {
-        epilogue_plain(tb, valid, p.out + orow * p.ldo, ti.nt * p.b_tile_stride, p.b_half1_off);
+        epilogue_plain(tb, valid, qp.out + orow * qp.ldo, ti.nt * qp.b_tile_stride, qp.b_half1_off);
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -423,8 +466,9 @@ int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int cols) {
 
 }  // namespace
 
-int launch(const Problem& pr, cudaStream_t s) {
-  if (pr.a_rows <= 0) return DS_OK;
+namespace {
+
+int check_problem(const Problem& pr) {
   const bool router = pr.epilogue == kRouter;
   DS_REQUIRE(pr.A && pr.B && (router || pr.out), "gemm: null pointer");
   DS_REQUIRE(aligned16(pr.A) && aligned16(pr.B) && (router || aligned16(pr.out)),
@@ -439,56 +483,91 @@ int launch(const Problem& pr, cudaStream_t s) {
              pr.groups, kMaxGroups);
   DS_REQUIRE(pr.n_tiles >= 1 && pr.weight_group_mod >= 1, "gemm: bad tiling");
   DS_REQUIRE(pr.a_rows < (1LL << 31) && pr.b_rows < (1LL << 31), "gemm: too many rows");
-  DeviceInfo di;
-  DS_TRY(device_info(&di));
   DS_REQUIRE(pr.epilogue == kPlain || pr.epilogue == kSwiGLU || pr.epilogue == kRouter,
              "gemm: unknown epilogue %d", pr.epilogue);
+  return DS_OK;
+}
+
+ProbParams prob_params_of(const Problem& pr) {
+  ProbParams q{};
+  q.offsets = pr.offsets;
+  q.groups = pr.offsets ? pr.groups : 1;
+  q.dense_rows = static_cast<int>(pr.a_rows);
+  q.k_blocks = (pr.K + BK - 1) / BK;
+  q.n_tiles = pr.n_tiles;
+  q.b_rows_per_group = pr.b_rows_per_group;
+  q.b_tile_stride = pr.b_tile_stride;
+  q.b_half1_off = pr.b_half1_off;
+  q.weight_group_mod = pr.weight_group_mod;
+  q.out = static_cast<__nv_bfloat16*>(pr.out);
+  q.ldo = pr.ldo;
+  q.out_row_map = pr.out_row_map;
+  q.kb_per_split = (q.k_blocks + pr.n_tiles - 1) / pr.n_tiles;
+  q.logits_out = pr.logits_out;
+  return q;
+}
+
+}  // namespace
+
+int launch_multi(const Problem* const* probs, int n, cudaStream_t s) {
+  const Problem* live[kMaxProblems];
+  int nl = 0;
+  DS_REQUIRE(n >= 1 && n <= kMaxProblems, "gemm: 1 or 2 problems per launch");
+  for (int i = 0; i < n; ++i) {
+    if (probs[i] == nullptr || probs[i]->a_rows <= 0) continue;
+    DS_TRY(check_problem(*probs[i]));
+    live[nl++] = probs[i];
+  }
+  if (nl == 0) return DS_OK;
+  const int epi = live[0]->epilogue;
+  DS_REQUIRE(nl == 1 || live[1]->epilogue == epi, "gemm: problems of one launch share an epilogue");
+  DeviceInfo di;
+  DS_TRY(device_info(&di));
   {
     std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (!g_attr_set[pr.epilogue][di.device]) {
-      const void* fn = pr.epilogue == kSwiGLU  ? reinterpret_cast<const void*>(grouped_gemm_kernel<kSwiGLU>)
-                       : pr.epilogue == kRouter ? reinterpret_cast<const void*>(grouped_gemm_kernel<kRouter>)
-                                                : reinterpret_cast<const void*>(grouped_gemm_kernel<kPlain>);
+    if (!g_attr_set[epi][di.device]) {
+      const void* fn = epi == kSwiGLU  ? reinterpret_cast<const void*>(grouped_gemm_kernel<kSwiGLU>)
+                       : epi == kRouter ? reinterpret_cast<const void*>(grouped_gemm_kernel<kRouter>)
+                                        : reinterpret_cast<const void*>(grouped_gemm_kernel<kPlain>);
       DS_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(kSmemBytes)));
-      g_attr_set[pr.epilogue][di.device] = true;
+      g_attr_set[epi][di.device] = true;
     }
   }
-  CUtensorMap tmA, tmB;
-  DS_TRY(make_tmap(&tmA, pr.A, pr.a_rows, pr.K));
-  DS_TRY(make_tmap(&tmB, pr.B, pr.b_rows, pr.K));
+  CUtensorMap tmA[kMaxProblems], tmB[kMaxProblems];
   Params p{};
-  p.offsets = pr.offsets;
-  p.groups = pr.offsets ? pr.groups : 1;
-  p.dense_rows = static_cast<int>(pr.a_rows);
-  p.k_blocks = (pr.K + BK - 1) / BK;
-  p.n_tiles = pr.n_tiles;
-  p.b_rows_per_group = pr.b_rows_per_group;
-  p.b_tile_stride = pr.b_tile_stride;
-  p.b_half1_off = pr.b_half1_off;
-  p.weight_group_mod = pr.weight_group_mod;
-  p.out = static_cast<__nv_bfloat16*>(pr.out);
-  p.ldo = pr.ldo;
-  p.epilogue = pr.epilogue;
-  p.out_row_map = pr.out_row_map;
+  p.nprob = nl;
   p.status = device_status_ptr();
   p.timeout_cycles = kDefaultTimeoutCycles;
-  p.kb_per_split = (p.k_blocks + pr.n_tiles - 1) / pr.n_tiles;
-  p.logits_out = pr.logits_out;
   if (p.status == nullptr) return fail(DS_ERR_CUDA, "device status word unavailable");
-  const int64_t max_mtiles = (pr.a_rows + BM - 1) / BM + (pr.offsets ? p.groups : 0);
-  const int64_t max_tiles = max_mtiles * pr.n_tiles;
+  int64_t max_tiles = 0;
   int cap = di.num_sms;
-  if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
+  for (int i = 0; i < nl; ++i) {
+    const Problem& pr = *live[i];
+    DS_TRY(make_tmap(&tmA[i], pr.A, pr.a_rows, pr.K));
+    DS_TRY(make_tmap(&tmB[i], pr.B, pr.b_rows, pr.K));
+    p.pr[i] = prob_params_of(pr);
+    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
+    if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
+  }
+  if (nl == 1) {
+    tmA[1] = tmA[0];
+    tmB[1] = tmB[0];
+  }
   const int grid = static_cast<int>(max_tiles < cap ? max_tiles : cap);
-  if (pr.epilogue == kSwiGLU)
-    grouped_gemm_kernel<kSwiGLU><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, p);
-  else if (pr.epilogue == kRouter)
-    grouped_gemm_kernel<kRouter><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, p);
+  if (epi == kSwiGLU)
+    grouped_gemm_kernel<kSwiGLU><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], p);
+  else if (epi == kRouter)
+    grouped_gemm_kernel<kRouter><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], p);
   else
-    grouped_gemm_kernel<kPlain><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, p);
+    grouped_gemm_kernel<kPlain><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], p);
   DS_LAUNCH_CHECK("grouped_gemm_kernel");
   return DS_OK;
+}
+
+int launch(const Problem& pr, cudaStream_t s) {
+  const Problem* one[1] = {&pr};
+  return launch_multi(one, 1, s);
 }
 
 int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,

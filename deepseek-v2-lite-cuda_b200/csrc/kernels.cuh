@@ -86,6 +86,10 @@ struct Problem {
 
 int launch(const Problem& pr, cudaStream_t s);
 
+// One persistent launch over up to two problems with the same epilogue (their tiles are
+// enumerated one problem after the other; null or empty problems are skipped).
+int launch_multi(const Problem* const* probs, int n, cudaStream_t s);
+
 // Rows of out [S, ldo] outside [offsets[0], offsets[groups]) are set to zero.
 int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,
                           cudaStream_t s);

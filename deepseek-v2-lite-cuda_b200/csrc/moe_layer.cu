@@ -130,6 +130,9 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
                             b.dispatched, b.token_map, nullptr, b.slot_of, S, s));
   DS_TRY(mark(3));
 
+  // GEMM1 (+ SwiGLU) of the routed experts and of the shared expert in one persistent launch,
+  // then GEMM2 of both (the shared expert's long-K tiles first, so the short routed tiles
+  // fill the end of the launch).
   ds::gemm::Problem g1{};
   g1.A = b.dispatched;
   g1.a_rows = S;
@@ -146,7 +149,29 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
   g1.out = b.h;
   g1.ldo = I;
   g1.epilogue = ds::gemm::kSwiGLU;
-  DS_TRY(ds::gemm::launch(g1, s));
+
+  ds::gemm::Problem s1{};
+  if (has_shared) {
+    s1.A = x_bf16;
+    s1.a_rows = T;
+    s1.K = H;
+    s1.B = shared_w1_bf16;
+    s1.b_rows = 2 * static_cast<int64_t>(Is);
+    s1.offsets = nullptr;
+    s1.groups = 1;
+    s1.n_tiles = Is / 128;
+    s1.b_rows_per_group = 2 * Is;
+    s1.b_tile_stride = 128;
+    s1.b_half1_off = Is;
+    s1.weight_group_mod = 1;
+    s1.out = b.sh;
+    s1.ldo = Is;
+    s1.epilogue = ds::gemm::kSwiGLU;
+  }
+  {
+    const ds::gemm::Problem* probs[2] = {&g1, has_shared ? &s1 : nullptr};
+    DS_TRY(ds::gemm::launch_multi(probs, 2, s));
+  }
   DS_TRY(mark(4));
 
   ds::gemm::Problem g2{};
@@ -165,31 +190,9 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
   g2.out = b.eo;
   g2.ldo = H;
   g2.epilogue = ds::gemm::kPlain;
-  DS_TRY(ds::gemm::launch(g2, s));
-  DS_TRY(mark(5));
 
+  ds::gemm::Problem s2{};
   if (has_shared) {
-    ds::gemm::Problem s1{};
-    s1.A = x_bf16;
-    s1.a_rows = T;
-    s1.K = H;
-    s1.B = shared_w1_bf16;
-    s1.b_rows = 2 * static_cast<int64_t>(Is);
-    s1.offsets = nullptr;
-    s1.groups = 1;
-    s1.n_tiles = Is / 128;
-    s1.b_rows_per_group = 2 * Is;
-    s1.b_tile_stride = 128;
-    s1.b_half1_off = Is;
-    s1.weight_group_mod = 1;
-    s1.out = b.sh;
-    s1.ldo = Is;
-    s1.epilogue = ds::gemm::kSwiGLU;
-    DS_TRY(ds::gemm::launch(s1, s));
-  }
-  DS_TRY(mark(6));
-  if (has_shared) {
-    ds::gemm::Problem s2{};
     s2.A = b.sh;
     s2.a_rows = T;
     s2.K = Is;
@@ -205,8 +208,13 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
     s2.out = b.so;
     s2.ldo = H;
     s2.epilogue = ds::gemm::kPlain;
-    DS_TRY(ds::gemm::launch(s2, s));
   }
+  {
+    const ds::gemm::Problem* probs[2] = {has_shared ? &s2 : &g2, has_shared ? &g2 : nullptr};
+    DS_TRY(ds::gemm::launch_multi(probs, 2, s));
+  }
+  DS_TRY(mark(5));
+  DS_TRY(mark(6));  // the shared expert now runs inside the two launches above
   DS_TRY(mark(7));
   DS_TRY(ds::launch_combine_gather(b.eo, b.slot_of, b.w, K, has_shared ? b.so : nullptr, out_bf16,
                                    T, H, s));

@@ -132,3 +132,59 @@ def fused_moe_forward(hidden_states: torch.Tensor, gate_weight: torch.Tensor, ex
     split = ds_kernels.router_weight_split(gate_weight.to(hidden_states.device))
     return _layer(hidden_states.contiguous(), split, gate_weight.shape[0], packed_w1, w2, None,
                   None, top_k, _FN_WS)
+
+
+class HostPipeline:
+    """Streams batches that live in pinned host memory through a layer and back.
+
+    Each submitted batch is copied host->device on a copy stream, run through the layer on the
+    compute stream, and copied device->host on a second copy stream, so the copies of one
+    batch overlap the compute of its neighbours (the copy engines and the SMs work
+    concurrently).  Every batch still makes its own round trip.
+
+        pipe = HostPipeline(layer, max_tokens=8192, hidden=2048)
+        for x_host, out_host in batches:          # pinned CPU bf16 tensors [T, H]
+            pipe.submit(x_host, out_host)
+        pipe.synchronize()                        # every out_host now holds its result
+    """
+
+    def __init__(self, layer: nn.Module, max_tokens: int, hidden: int,
+                 device: Optional[torch.device] = None, depth: int = 2):
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.layer = layer
+        self.depth = depth
+        self.compute = torch.cuda.current_stream(dev)
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.x = [torch.empty((max_tokens, hidden), dtype=torch.bfloat16, device=dev)
+                  for _ in range(depth)]
+        self.in_ready = [torch.cuda.Event() for _ in range(depth)]
+        self.x_free = [torch.cuda.Event() for _ in range(depth)]
+        self.out_ready = [torch.cuda.Event() for _ in range(depth)]
+        self.used = [False] * depth
+        self.n = 0
+
+    def submit(self, x_host: torch.Tensor, out_host: torch.Tensor) -> None:
+        i = self.n % self.depth
+        T = x_host.shape[0]
+        xb = self.x[i][:T]
+        if self.used[i]:  # the slot's previous batch must be consumed by the layer first
+            self.h2d.wait_event(self.x_free[i])
+        with torch.cuda.stream(self.h2d):
+            xb.copy_(x_host, non_blocking=True)
+            self.in_ready[i].record(self.h2d)
+        self.compute.wait_event(self.in_ready[i])
+        with torch.cuda.stream(self.compute):
+            out = self.layer(xb)
+            self.x_free[i].record(self.compute)
+            self.out_ready[i].record(self.compute)
+        self.d2h.wait_event(self.out_ready[i])
+        with torch.cuda.stream(self.d2h):
+            out_host.copy_(out, non_blocking=True)
+            out.record_stream(self.d2h)
+        self.used[i] = True
+        self.n += 1
+
+    def synchronize(self) -> None:
+        self.d2h.synchronize()
+        self.compute.synchronize()
