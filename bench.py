@@ -18,9 +18,10 @@ a bounded sample of the same workload on this host's cores.
 --impl reference times the reference's CPU implementation of the path (the oracle port;
 the reference itself is a PyTorch CPU module) and prints the same metric.
 With --gpus N > 1 (torchrun, one process per GPU) the layer runs expert-parallel: each rank
-owns 64/N experts and its own 8192 tokens (weak scaling), dispatched rows and expert
-outputs move through NCCL all-to-all over NVLink; `value` = N*8192 / max-over-ranks step
-time.
+owns 64/N experts and its own 8192 tokens (weak scaling); by default (--ep p2p) the
+dispatched rows and expert outputs move over NVLink peer memory inside the layer's own
+kernels (ep_p2p.P2PEPMoELayer), --ep nccl uses NCCL all-to-alls (ep_moe.EPMoELayer);
+`value` = N*8192 / max-over-ranks step time.
 """
 from __future__ import annotations
 
@@ -202,6 +203,17 @@ def read_traffic():
     return None
 
 
+def ep_recv_rows(x, gate, rank, world):
+    """Rows rank 0 receives per forward (its experts' share of every rank's top-k), from the
+    router on each rank's tokens; computed once, outside the timed region."""
+    import ds_kernels
+    split = ds_kernels.router_weight_split(gate)
+    idx, _ = ds_kernels.moe_router(x, split, E, K)
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=E).to(torch.int64)
+    torch.distributed.all_reduce(counts)
+    return int(counts[: E // world].sum())
+
+
 def run_ours(args, rank, world, local_rank):
     import ds_kernels
     from moe_fused import FusedMoELayer
@@ -216,21 +228,36 @@ def run_ours(args, rank, world, local_rank):
     base = None
     if rank == 0 and world == 1 and not args.no_cpu:
         base = cpu_baseline(oracle_weights(Wd), x_cpu)
+    recv_rows = None
     if world == 1:
         layer = FusedMoELayer.from_packed(Wd.gate, Wd.packed_w1, Wd.w2, Wd.shared_w1,
                                           Wd.shared_w2, top_k=K)
+        # phase boundaries of ds_moe_layer_forward_from_x; shared1/shared2 are empty since the
+        # shared expert runs inside the two GEMM launches
         names = ["routing", "plan", "dispatch", "gemm1", "gemm2", "shared1", "shared2",
                  "combine"]
-        launches_per_step = 8
+        # router GEMM, routing, plan, scatter, GEMM1 (+shared), GEMM2 (+shared), combine
+        launches_per_step = 7
     else:
-        from ep_moe import EPMoELayer, shard_experts
+        from ep_moe import shard_experts
         w1l, w2l = shard_experts(Wd.packed_w1, Wd.w2, rank, world)
-        layer = EPMoELayer(Wd.gate, w1l.clone(), w2l.clone(), Wd.shared_w1, Wd.shared_w2,
-                           top_k=K)
+        recv_rows = ep_recv_rows(x, Wd.gate, rank, world)
+        if args.ep == "p2p":
+            from ep_p2p import P2PEPMoELayer
+            layer = P2PEPMoELayer(Wd.gate, w1l.clone(), w2l.clone(), Wd.shared_w1,
+                                  Wd.shared_w2, top_k=K, max_tokens=T_GLOBAL)
+            names = list(P2PEPMoELayer.PHASES)
+            # router GEMM, routing, plan+exchange, dispatch+send, GEMM1, GEMM2, combine
+            launches_per_step = 7
+        else:
+            from ep_moe import EPMoELayer
+            layer = EPMoELayer(Wd.gate, w1l.clone(), w2l.clone(), Wd.shared_w1,
+                               Wd.shared_w2, top_k=K)
+            names = list(EPMoELayer.PHASES)
+            # router 2, dispatch 3, ep_plan 2, gather, GEMM1, GEMM2, shared 2, combine
+            launches_per_step = 13
         Wd.packed_w1 = Wd.w2 = None
         torch.cuda.empty_cache()
-        names = list(EPMoELayer.PHASES)
-        launches_per_step = 11
     nev = len(names) + 1
 
     def step(events=None):
@@ -290,15 +317,27 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = ms_t.tolist()
+    if hasattr(layer, "check"):
+        layer.check()  # raises if a bounded cross-GPU wait ran out
+        layer.close()  # collective: every rank unmaps and frees its symmetric segment
     if rank != 0:
         return
     pk = peaks()
     fl = gemm_flops()
     if world == 1:
-        kernel = "grouped_gemm (routed GEMM1 + SwiGLU)"
-        kflops = fl["gemm1"]
+        kernel = ("grouped_gemm_kernel<SwiGLU>: one persistent launch of the routed GEMM1 "
+                  "(49152 dispatched rows) + the shared-expert GEMM1 (8192 rows), SwiGLU epilogue")
+        kflops = fl["gemm1"] + fl["shared1"]
         ksec = phase_ms["gemm1"] / 1000.0
         tr = read_traffic()
+    elif args.ep == "p2p":
+        R = recv_rows
+        kernel = ("grouped_gemm_kernel<SwiGLU> on rank 0: shared-expert GEMM1 (8192 rows) + "
+                  f"routed GEMM1 over the {R} rows received from all ranks, including the wait "
+                  "for their arrival over NVLink")
+        kflops = fl["shared1"] + 2.0 * R * H * 2 * I
+        ksec = phase_ms["gemm1"] / 1000.0
+        tr = None
     else:
         R = layer.last_recv_rows
         kernel = ("expert MLP on rank 0's experts (row gather + grouped GEMM1+SwiGLU + "
@@ -317,9 +356,12 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": "cfg2: full DeepSeek-V2-Lite MoE layer prefill, T=8192 per GPU",
                    "global_batch": T_GLOBAL * world, "seq_len": T_GLOBAL, "hidden": H,
                    "experts": E, "top_k": K, "shared_experts": N_SHARED,
-                   "parallelism": (f"ep{world}: {E // world} experts per GPU, NCCL all-to-all "
-                                   "of dispatched rows and expert outputs" if world > 1
-                                   else "single GPU"),
+                   "parallelism": (f"ep{world}: {E // world} experts per GPU, " +
+                                   ("dispatched rows and expert outputs over NVLink peer "
+                                    "memory inside the dispatch/GEMM2 kernels"
+                                    if args.ep == "p2p" else
+                                    "NCCL all-to-all of dispatched rows and expert outputs")
+                                   if world > 1 else "single GPU"),
                    "l2": "working set > L2: each step streams 1.1 GB of expert weights and "
                          "~0.6 GB of activations through the 126 MB L2"},
         "roofline": {"bound": "tensor", "kernel": kernel,
@@ -496,6 +538,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
+                    help="expert-parallel transport for --gpus > 1")
     ap.add_argument("--op-report", default=None)
     ap.add_argument("--kernel-case", default=None,
                     choices=["gemm1", "gemm2", "dispatch", "routing", "router", "combine",

@@ -48,6 +48,8 @@ int device_info(DeviceInfo* out) {
     DeviceInfo d{};
     d.device = dev;
     DS_CUDA(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    DS_CUDA(cudaDeviceGetAttribute(&d.clock_khz, cudaDevAttrClockRate, dev));
+    if (d.clock_khz <= 0) d.clock_khz = 2000000;
     g_info[dev] = d;
     g_info_ready[dev] = true;
   }

@@ -19,6 +19,7 @@ int cuda_fail(cudaError_t e, const char* where);
 struct DeviceInfo {
   int device;
   int num_sms;
+  int clock_khz;  // maximum SM clock: converts wall-time bounds to clock64() cycles
 };
 int device_info(DeviceInfo* out);
 

@@ -62,6 +62,11 @@ struct ProbParams {
   const int32_t* out_row_map;
   int kb_per_split;   // router: k-blocks per K slice (the n-tile index is the slice)
   float* logits_out;  // router: partial accumulators
+  // cross-GPU hooks (expert parallelism over peer memory)
+  const int* wait_flag;      // before this problem's first tile: wait until *flag >= target
+  int wait_target;
+  const int32_t* out_meta;   // per A row: (rank << 24) | row  -> out_peers[rank] + row * ldo
+  __nv_bfloat16* out_peers[8];
 };
 
 // A launch serves up to two problems with the same epilogue; their tiles are enumerated one
@@ -71,6 +76,11 @@ struct Params {
   int nprob;
   int* status;
   long long timeout_cycles;
+  // completion signal: every CTA fences its stores system-wide and bumps done_counter; the
+  // last CTA of the launch adds 1 to each flag (release) and resets the counter.
+  int* done_counter;
+  int nsignal;
+  int* signal_flags[8];
 };
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
@@ -270,9 +280,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t used_mask = 0, phase_mask = 0;
       bool ok = true;
+      uint32_t waited = 0;
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
         const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
         const ProbParams& q = prob_params(p, ti.prob);
+        if (q.wait_flag != nullptr && !(waited & (1u << ti.prob))) {
+          if (!ptx::wait_flag_ge(q.wait_flag, q.wait_target, abort_flag, p.status,
+                                 p.timeout_cycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          // peers wrote this problem's A rows with generic stores; order them before TMA reads
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          waited |= 1u << ti.prob;
+        }
         const CUtensorMap* tA = ti.prob ? &tmA1 : &tmA0;
         const CUtensorMap* tB = ti.prob ? &tmB1 : &tmB0;
         const int kb0 = EPI == kRouter ? ti.nt * q.kb_per_split : 0;
@@ -379,16 +400,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       const uint32_t tb =
           tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      const bool valid = r < ti.rows;
+      const bool vrow = r < ti.rows;
       int64_t orow = ti.row0 + r;
+      __nv_bfloat16* obase = qp.out;
+      bool valid = vrow;
       if (valid && qp.out_row_map != nullptr) orow = __ldg(qp.out_row_map + orow);
+      if (valid && qp.out_meta != nullptr) {
+        const int m = __ldg(qp.out_meta + orow);
+        const int rk = (m >> 24) & 7;
+        obase = rk == 0 ? qp.out_peers[0] : rk == 1 ? qp.out_peers[1] : rk == 2 ? qp.out_peers[2]
+              : rk == 3 ? qp.out_peers[3] : rk == 4 ? qp.out_peers[4] : rk == 5 ? qp.out_peers[5]
+              : rk == 6 ? qp.out_peers[6] : qp.out_peers[7];
+        orow = m & 0xFFFFFF;
+        valid = obase != nullptr;  // a rank outside the world has no segment: drop the row
+      }
       if constexpr (EPI == kSwiGLU) {
-        epilogue_swiglu(tb, valid, qp.out + orow * qp.ldo + ti.nt * 128);
+        epilogue_swiglu(tb, valid, obase + orow * qp.ldo + ti.nt * 128);
       } else if constexpr (EPI == kRouter) {
         epilogue_router_partials(
             tb, valid, qp.logits_out + (static_cast<int64_t>(ti.nt) * qp.dense_rows + orow) * 192);
       } else {
-        epilogue_plain(tb, valid, qp.out + orow * qp.ldo, ti.nt * qp.b_tile_stride, qp.b_half1_off);
+        epilogue_plain(tb, valid, obase + orow * qp.ldo, ti.nt * qp.b_tile_stride, qp.b_half1_off);
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -401,10 +433,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncwarp();  // lanes 1..31 of warps 0/1 rejoin their role lane before the CTA barrier
+  if (p.done_counter != nullptr) __threadfence_system();  // this thread's (peer) stores
   __syncthreads();
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (p.done_counter != nullptr && threadIdx.x == 0) {
+    const int prev = atomicAdd(p.done_counter, 1);
+    if (prev == static_cast<int>(gridDim.x) - 1) {  // the last CTA of this launch
+      __threadfence_system();
+      // a launch that failed (timeout) signals nothing: its waiters time out in turn
+      if (*reinterpret_cast<volatile int*>(p.status) == 0)
+        for (int i = 0; i < p.nsignal; ++i) ptx::red_release_sys_add(p.signal_flags[i], 1);
+      atomicExch(p.done_counter, 0);  // ready for the next launch on this stream
+    }
   }
 }
 
@@ -504,12 +547,16 @@ ProbParams prob_params_of(const Problem& pr) {
   q.out_row_map = pr.out_row_map;
   q.kb_per_split = (q.k_blocks + pr.n_tiles - 1) / pr.n_tiles;
   q.logits_out = pr.logits_out;
+  q.wait_flag = pr.wait_flag;
+  q.wait_target = pr.wait_target;
+  q.out_meta = pr.out_meta;
+  for (int i = 0; i < 8; ++i) q.out_peers[i] = static_cast<__nv_bfloat16*>(pr.out_peers[i]);
   return q;
 }
 
 }  // namespace
 
-int launch_multi(const Problem* const* probs, int n, cudaStream_t s) {
+int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signal* sig) {
   const Problem* live[kMaxProblems];
   int nl = 0;
   DS_REQUIRE(n >= 1 && n <= kMaxProblems, "gemm: 1 or 2 problems per launch");
@@ -518,7 +565,10 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s) {
     DS_TRY(check_problem(*probs[i]));
     live[nl++] = probs[i];
   }
-  if (nl == 0) return DS_OK;
+  if (nl == 0) {
+    DS_REQUIRE(sig == nullptr, "gemm: a signalling launch needs a non-empty problem");
+    return DS_OK;
+  }
   const int epi = live[0]->epilogue;
   DS_REQUIRE(nl == 1 || live[1]->epilogue == epi, "gemm: problems of one launch share an epilogue");
   DeviceInfo di;
@@ -549,12 +599,21 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s) {
     p.pr[i] = prob_params_of(pr);
     max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
     if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
+    // a cross-GPU wait may legitimately hold the pipeline: every wait gets its bound
+    if (pr.wait_timeout_cycles > p.timeout_cycles) p.timeout_cycles = pr.wait_timeout_cycles;
   }
   if (nl == 1) {
     tmA[1] = tmA[0];
     tmB[1] = tmB[0];
   }
   const int grid = static_cast<int>(max_tiles < cap ? max_tiles : cap);
+  if (sig != nullptr) {
+    DS_REQUIRE(sig->done_counter != nullptr && sig->nsignal >= 0 && sig->nsignal <= 8,
+               "gemm: bad completion signal");
+    p.done_counter = sig->done_counter;
+    p.nsignal = sig->nsignal;
+    for (int i = 0; i < sig->nsignal; ++i) p.signal_flags[i] = sig->flags[i];
+  }
   if (epi == kSwiGLU)
     grouped_gemm_kernel<kSwiGLU><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], p);
   else if (epi == kRouter)
@@ -567,7 +626,21 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s) {
 
 int launch(const Problem& pr, cudaStream_t s) {
   const Problem* one[1] = {&pr};
-  return launch_multi(one, 1, s);
+  return launch_multi(one, 1, s, nullptr);
+}
+
+int grid_for(const Problem* const* probs, int n) {
+  DeviceInfo di;
+  if (device_info(&di) != DS_OK) return -1;
+  int64_t max_tiles = 0;
+  int cap = di.num_sms;
+  for (int i = 0; i < n; ++i) {
+    if (probs[i] == nullptr || probs[i]->a_rows <= 0) continue;
+    const Problem& pr = *probs[i];
+    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
+    if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
+  }
+  return static_cast<int>(max_tiles < cap ? max_tiles : cap);
 }
 
 int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,

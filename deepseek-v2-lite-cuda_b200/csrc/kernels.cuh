@@ -46,9 +46,13 @@ int launch_scatter(const void* x, int T, int H, int E, int K, const int32_t* idx
                    void* dispatched, int32_t* token_map, float* dispatched_weights,
                    int32_t* slot_of, int S, cudaStream_t s);
 
-// out[t] = sum_j w[t,j] * eo[slot_of[t,j]] (+ shared[t]), slots in ascending order.
+// out[t] = sum_j w[t,j] * eo[slot_of[t,j]] (+ shared[t]), slots in ascending order.  With
+// wait_flag, each CTA first waits (bounded by timeout_cycles) until *wait_flag >= wait_target
+// (rows of eo written by other GPUs) and reads eo through L2.
 int launch_combine_gather(const void* eo, const int32_t* slot_of, const float* w, int K,
-                          const void* shared_out, void* out, int T, int H, cudaStream_t s);
+                          const void* shared_out, void* out, int T, int H, cudaStream_t s,
+                          const int* wait_flag = nullptr, int wait_target = 0,
+                          long long timeout_cycles = 0);
 
 int launch_swiglu(const void* in, void* out, int64_t rows, int I, cudaStream_t s);
 
@@ -82,13 +86,34 @@ struct Problem {
   // slices; slice s writes its raw accumulator columns [0, 192) as f32 to
   // logits_out + (s * a_rows + row) * 192
   float* logits_out = nullptr;
+  // expert parallelism over peer memory: wait until *wait_flag >= wait_target before reading
+  // this problem's A; write output row i to out_peers[meta >> 24] + (meta & 0xFFFFFF) * ldo
+  // with meta = out_meta[i] (out unused then)
+  const int* wait_flag = nullptr;
+  int wait_target = 0;
+  long long wait_timeout_cycles = 0;  // 0: the default bound of every wait in the kernel
+  const int32_t* out_meta = nullptr;
+  void* out_peers[8] = {};
+};
+
+// Completion signal of a launch: when all its CTAs are done (their stores fenced system
+// wide), 1 is added to each of `flags` (release).  done_counter: a zeroed device int that
+// the launch leaves at zero again.
+struct Signal {
+  int* done_counter = nullptr;
+  int nsignal = 0;
+  int* flags[8] = {};
 };
 
 int launch(const Problem& pr, cudaStream_t s);
 
 // One persistent launch over up to two problems with the same epilogue (their tiles are
 // enumerated one problem after the other; null or empty problems are skipped).
-int launch_multi(const Problem* const* probs, int n, cudaStream_t s);
+int launch_multi(const Problem* const* probs, int n, cudaStream_t s,
+                 const Signal* sig = nullptr);
+
+// Grid size launch_multi would use for these problems (-1 on error).
+int grid_for(const Problem* const* probs, int n);
 
 // Rows of out [S, ldo] outside [offsets[0], offsets[groups]) are set to zero.
 int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,

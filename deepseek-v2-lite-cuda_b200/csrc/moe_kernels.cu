@@ -11,6 +11,7 @@
 #include <cmath>
 
 #include "kernels.cuh"
+#include "ptx.cuh"
 
 namespace ds {
 namespace {
@@ -383,13 +384,33 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float (&a)[8]) {
   return r;
 }
 
+// 16-byte load through L2 only: rows that other GPUs wrote while this kernel was waiting.
+__device__ __forceinline__ uint4 ld_cg16(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 // K7 (fused path): one warp per token gathers its K expert rows in ascending slot order.
+// With wait_flag (expert parallelism over peer memory) every CTA first waits, bounded, until
+// the other GPUs have returned their expert outputs (*wait_flag >= wait_target).
 template <int K>
 __global__ void __launch_bounds__(256)
     combine_gather_kernel(const uint4* __restrict__ eo, const int32_t* __restrict__ slot_of,
                           const float* __restrict__ w, const uint4* __restrict__ shared_out,
-                          uint4* __restrict__ out, int T, int H8) {
+                          uint4* __restrict__ out, int T, int H8, const int* wait_flag,
+                          int wait_target, int* status, long long timeout_cycles) {
   const int lane = threadIdx.x & 31;
+  if (wait_flag != nullptr) {
+    __shared__ int ok;
+    if (threadIdx.x == 0)
+      ok = ptx::wait_flag_ge(wait_flag, wait_target, nullptr, status, timeout_cycles,
+                             DS_ERR_TIMEOUT);
+    __syncthreads();
+    if (!ok) return;
+  }
   const int warps = gridDim.x * (blockDim.x >> 5);
   for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
     int my_s = INT_MAX;
@@ -428,8 +449,11 @@ __global__ void __launch_bounds__(256)
       float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint4 v[K];
 #pragma unroll
-      for (int j = 0; j < K; ++j)
-        if (s[j] != INT_MAX) v[j] = __ldg(eo + static_cast<int64_t>(s[j]) * H8 + c);
+      for (int j = 0; j < K; ++j) {
+        if (s[j] == INT_MAX) continue;
+        const uint4* src = eo + static_cast<int64_t>(s[j]) * H8 + c;
+        v[j] = wait_flag != nullptr ? ld_cg16(src) : __ldg(src);
+      }
 #pragma unroll
       for (int j = 0; j < K; ++j)
         if (s[j] != INT_MAX) acc_bf16x8(a, v[j], ww[j]);
@@ -649,7 +673,8 @@ int launch_scatter(const void* x, int T, int H, int E, int K, const int32_t* idx
 }
 
 int launch_combine_gather(const void* eo, const int32_t* slot_of, const float* w, int K,
-                          const void* shared_out, void* out, int T, int H, cudaStream_t s) {
+                          const void* shared_out, void* out, int T, int H, cudaStream_t s,
+                          const int* wait_flag, int wait_target, long long timeout_cycles) {
   if (T <= 0) return DS_OK;
   DeviceInfo di;
   DS_TRY(device_info(&di));
@@ -657,7 +682,7 @@ int launch_combine_gather(const void* eo, const int32_t* slot_of, const float* w
   DS_DISPATCH_K(K, combine_gather_kernel<KK><<<grid, 256, 0, s>>>(
                        static_cast<const uint4*>(eo), slot_of, w,
                        static_cast<const uint4*>(shared_out), static_cast<uint4*>(out), T,
-                       H / 8));
+                       H / 8, wait_flag, wait_target, device_status_ptr(), timeout_cycles));
   DS_LAUNCH_CHECK("combine_gather_kernel");
   return DS_OK;
 }

@@ -179,5 +179,40 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
 
+// ---- flags shared between GPUs (peer memory): release/acquire at system scope -----------
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(int* p, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait (one thread) until *flag >= target, where another GPU's kernel raises the
+// flag.  Gives up when *abort_flag is set (if given), when the device status word already
+// holds an error (a failed exchange upstream), or after timeout_cycles; on timeout it sets
+// *abort_flag and ORs err into *status.  Returns true when the flag was reached.
+__device__ __forceinline__ bool wait_flag_ge(const int* flag, int target, volatile int* abort_flag,
+                                             int* status, long long timeout_cycles, int err) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire_sys(flag) >= target) return true;
+    if ((i & 15u) == 0u) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (*reinterpret_cast<volatile int*>(status) != 0) {
+        if (abort_flag != nullptr) *abort_flag = 1;
+        return false;
+      }
+      if (clock64() - t0 > timeout_cycles) {
+        if (abort_flag != nullptr) *abort_flag = 1;
+        atomicOr(status, err);
+        return false;
+      }
+      __nanosleep(100);
+    }
+  }
+}
+
 }  // namespace ptx
 }  // namespace ds

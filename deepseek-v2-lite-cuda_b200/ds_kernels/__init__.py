@@ -29,6 +29,8 @@ DS_ERR_CUDA = 3
 DS_ERR_TIMEOUT = 4
 DS_ERR_WORKSPACE = 5
 LAYER_NUM_EVENTS = 9
+EP_NUM_EVENTS = 7
+EP_IPC_HANDLE_BYTES = 64
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
@@ -80,6 +82,15 @@ SIGNATURES = {
     "ds_ep_plan_workspace_size": (_sz, [_i, _i]),
     "ds_ep_plan": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _sz, _vp]),
     "ds_gather_rows": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "ds_ep_symmetric_size": (_i, [_i, _i, _i, _i, _i, ctypes.POINTER(_sz)]),
+    "ds_ep_alloc": (_i, [_sz, ctypes.POINTER(_vp)]),
+    "ds_ep_free": (_i, [_vp]),
+    "ds_ep_ipc_handle": (_i, [_vp, _vp]),
+    "ds_ep_ipc_open": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "ds_ep_ipc_close": (_i, [_vp]),
+    "ds_ep_layer_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
+    "ds_ep_layer_forward": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
+                                 _i, _i, _i, _vp, _i, _i, _vp, _sz, _vp, _vp]),
 }
 
 
@@ -735,4 +746,96 @@ def dense_gemm2(h: torch.Tensor, w2: torch.Tensor, max_ctas: int = 0) -> torch.T
     with _on_device(h):
         _check(_lib.ds_dense_gemm2(_ptr(h), R, _ptr(w2), I, H, _ptr(out), int(max_ctas),
                                    _stream(h)), "dense_gemm2")
+    return out
+
+
+# ---- expert parallelism over NVLink peer memory (symmetric segments via CUDA IPC) ---------
+
+def ep_symmetric_size(max_tokens: int, hidden_size: int, num_experts: int, top_k: int,
+                      world: int) -> int:
+    n = _sz(0)
+    _check(_lib.ds_ep_symmetric_size(max_tokens, hidden_size, num_experts, top_k, world,
+                                     ctypes.byref(n)), "ep_symmetric_size")
+    return n.value
+
+
+def ep_alloc(nbytes: int, device: torch.device) -> int:
+    """cudaMalloc'd, zero-filled segment on `device` (a raw pointer; free with ep_free)."""
+    p = _vp()
+    with torch.cuda.device(device):
+        _check(_lib.ds_ep_alloc(nbytes, ctypes.byref(p)), "ep_alloc")
+    return p.value
+
+
+def ep_free(ptr: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        _check(_lib.ds_ep_free(ptr), "ep_free")
+
+
+def ep_ipc_handle(ptr: int, device: torch.device) -> bytes:
+    buf = ctypes.create_string_buffer(EP_IPC_HANDLE_BYTES)
+    with torch.cuda.device(device):
+        _check(_lib.ds_ep_ipc_handle(ptr, buf), "ep_ipc_handle")
+    return buf.raw
+
+
+def ep_ipc_open(handle: bytes, device: torch.device) -> int:
+    _require(len(handle) == EP_IPC_HANDLE_BYTES, "ep_ipc_open: bad handle size")
+    p = _vp()
+    buf = ctypes.create_string_buffer(bytes(handle), EP_IPC_HANDLE_BYTES)
+    with torch.cuda.device(device):
+        _check(_lib.ds_ep_ipc_open(buf, ctypes.byref(p)), "ep_ipc_open")
+    return p.value
+
+
+def ep_ipc_close(ptr: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        _check(_lib.ds_ep_ipc_close(ptr), "ep_ipc_close")
+
+
+def ep_layer_workspace_size(max_tokens: int, hidden_size: int, num_experts: int, top_k: int,
+                            intermediate_size: int, shared_intermediate_size: int,
+                            world: int) -> int:
+    return int(_lib.ds_ep_layer_workspace_size(max_tokens, hidden_size, num_experts, top_k,
+                                               intermediate_size, shared_intermediate_size,
+                                               world))
+
+
+def ep_layer_forward(x: torch.Tensor, router_w_split: torch.Tensor, num_experts: int,
+                     w1_local: torch.Tensor, w2_local: torch.Tensor,
+                     shared_w1: Optional[torch.Tensor], shared_w2: Optional[torch.Tensor],
+                     top_k: int, rank: int, world: int, max_tokens: int,
+                     sym_bases: Sequence[int], epoch: int, workspace: torch.Tensor,
+                     out: Optional[torch.Tensor] = None, timeout_ms: int = 10000,
+                     events: Optional[Sequence[torch.cuda.Event]] = None,
+                     logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One expert-parallel MoE layer forward of this rank's tokens (every rank calls it for
+    every forward with the same epoch sequence 1, 2, ...).  w1_local [El, 2I, H] and
+    w2_local [El, H, I] hold this rank's experts; sym_bases[r] = rank r's symmetric segment
+    as mapped in this process."""
+    _check_tensor(x, "x", torch.bfloat16, "bfloat16", 2, "[T, H]")
+    T, H = x.shape
+    E = num_experts
+    El = w1_local.shape[0]
+    I = w1_local.shape[1] // 2
+    _require(El * world == E and tuple(w2_local.shape) == (El, H, I), "local expert weight shapes")
+    Is = 0 if shared_w1 is None else shared_w1.shape[0] // 2
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    need = ep_layer_workspace_size(max_tokens, H, E, top_k, I, Is, world)
+    _require(workspace.numel() >= need, f"ep_layer_forward: workspace needs {need} bytes")
+    ev = None
+    if events is not None:
+        _require(len(events) == EP_NUM_EVENTS, f"events must hold {EP_NUM_EVENTS} events")
+        st = torch.cuda.current_stream(x.device)
+        for e in events:
+            e.record(st)
+        ev = (ctypes.c_void_p * EP_NUM_EVENTS)(*[e.cuda_event for e in events])
+    bases = (ctypes.c_void_p * world)(*sym_bases)
+    with _on_device(x):
+        _check(_lib.ds_ep_layer_forward(
+            _ptr(x) if T else None, T, _ptr(router_w_split), _ptr(logits_out), _ptr(w1_local),
+            _ptr(w2_local), _ptr(shared_w1), _ptr(shared_w2), _ptr(out) if T else None, H, E,
+            top_k, I, Is, rank, world, max_tokens, bases, epoch, timeout_ms, _ptr(workspace),
+            workspace.numel(), ev, _stream(x)), "ep_layer_forward")
     return out

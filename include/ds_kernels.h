@@ -310,6 +310,49 @@ DS_API int ds_moe_layer_forward_from_x(const void* x_bf16, const void* router_w_
                                        size_t workspace_bytes, void** events, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Expert parallelism over NVLink peer memory (additive: the reference is single-GPU; this is
+ * its fused pipeline, src/kernels/moe_fused.py:118-154, with experts partitioned
+ * contiguously over `world` ranks, one process per GPU).  Each rank allocates one symmetric
+ * segment with ds_ep_alloc(ds_ep_symmetric_size(...)), exports it with ds_ep_ipc_handle,
+ * and maps every other rank's segment with ds_ep_ipc_open; sym_bases[r] is rank r's
+ * segment as seen from this process (its own pointer at [rank]).  No host synchronisation
+ * and no collective library call on the data path: the count exchange, row transfer and
+ * result return run inside the plan, dispatch, GEMM2 and combine kernels, ordered by
+ * per-forward flags in the segments.  Every cross-GPU wait is bounded by timeout_ms; a
+ * wait that runs out sets the device status to DS_ERR_TIMEOUT (read it with
+ * ds_get_device_status), the ranks behind it time out in turn, and the segments must be
+ * re-created before the next forward. */
+#define DS_EP_IPC_HANDLE_BYTES 64
+#define DS_EP_NUM_EVENTS 7
+
+DS_API int ds_ep_symmetric_size(int max_tokens, int hidden_size, int num_experts, int top_k,
+                                int world, size_t* bytes);
+/* cudaMalloc + zero fill (the flags start at zero); ds_ep_free releases it. */
+DS_API int ds_ep_alloc(size_t bytes, void** ptr);
+DS_API int ds_ep_free(void* ptr);
+DS_API int ds_ep_ipc_handle(void* ptr, void* handle_out /* DS_EP_IPC_HANDLE_BYTES */);
+DS_API int ds_ep_ipc_open(const void* handle, void** ptr);
+DS_API int ds_ep_ipc_close(void* ptr);
+DS_API size_t ds_ep_layer_workspace_size(int max_tokens, int hidden_size, int num_experts,
+                                         int top_k, int intermediate_size,
+                                         int shared_intermediate_size, int world);
+/* One expert-parallel MoE layer forward of this rank's num_tokens (0 allowed; every rank
+ * must call it for every forward, with epoch = 1, 2, 3, ...).  w1_local [El*2I, H] and
+ * w2_local [El*H, I] hold experts [rank*El, (rank+1)*El) in the prepacked layout; router,
+ * shared expert, logits_out and out as ds_moe_layer_forward_from_x.  events: NULL or
+ * DS_EP_NUM_EVENTS handles bracketing route | plan+count exchange | dispatch+send |
+ * GEMM1 (+shared) | GEMM2 (+shared, return) | combine. */
+DS_API int ds_ep_layer_forward(const void* x_bf16, int num_tokens,
+                               const void* router_w_split_bf16, float* logits_out,
+                               const void* w1_local_bf16, const void* w2_local_bf16,
+                               const void* shared_w1_bf16, const void* shared_w2_bf16,
+                               void* out_bf16, int hidden_size, int num_experts, int top_k,
+                               int intermediate_size, int shared_intermediate_size, int rank,
+                               int world, int max_tokens, void* const* sym_bases, int epoch,
+                               int timeout_ms, void* workspace, size_t workspace_bytes,
+                               void** events, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Failure-detection probe (no reference counterpart): launches one CTA that waits on an
  * mbarrier nothing arrives on, through the same bounded-wait routine the GEMM pipeline
  * uses, with a limit of `timeout_cycles` SM clock cycles.  The wait runs out, the kernel
