@@ -5,8 +5,9 @@
 // src/kernels/mla/kv_upproj.cu:77-119.
 //
 // Structure (one persistent CTA per SM, 192 threads):
-//   warp 0       TMA producer: A tile 128x64 and B tile 256x64 (two 128-row boxes) per
-//                k-block into a 4-stage shared-memory ring (128-byte swizzle).
+//   warp 0       producer: A tile 128x64 (one TMA box, or in gather mode rows picked by
+//                index, copied by the warp with cp.async) and B tile 256x64 (two 128-row
+//                TMA boxes) per k-block into a 4-stage shared-memory ring (128-byte swizzle).
 //   warp 1       MMA issuer: tcgen05.mma kind::f16, M=128 N=256 K=16, f32 accumulator in
 //                TMEM, two accumulator buffers (2 x 256 columns) so the epilogue of tile i
 //                overlaps the MMAs of tile i+1.
@@ -19,6 +20,7 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
+#include <cstring>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -40,9 +42,13 @@ constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
 constexpr int kMaxGroups = 512;
 constexpr int kMaxProblems = 2;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTailBytes = 256;  // barriers + tmem holder + flags + problem tile starts
+// barriers + tmem holder + flags + problem tile starts (256 B), gather row indices (512 B)
+constexpr uint32_t kTailBytes = 256 + 512;
 constexpr int kGroupStride = kMaxGroups + 1;
-constexpr size_t kSmemBytes = 1024 + STAGES * (A_BYTES + B_BYTES) + kTailBytes +
+// output staging: per epilogue warp one 32-row x 128-byte slab (swizzled as SWIZZLE_128B)
+constexpr uint32_t kSlabBytes = 32 * 128;
+constexpr uint32_t kOutStageBytes = 4 * kSlabBytes;
+constexpr size_t kSmemBytes = 1024 + STAGES * (A_BYTES + B_BYTES) + kOutStageBytes + kTailBytes +
                               2 * kMaxProblems * kGroupStride * sizeof(int);
 constexpr long long kDefaultTimeoutCycles = 4000000000LL;  // ~2 s at 2 GHz
 
@@ -60,6 +66,10 @@ struct ProbParams {
   __nv_bfloat16* out;
   int ldo;
   const int32_t* out_row_map;
+  int tma_out;        // contiguous output rows: full 32-row slabs leave by TMA store
+  const int32_t* a_gather;  // gather mode: A row of each tile row (slot -> token)
+  const void* a_ptr;        // gather mode: A base and row pitch in bytes
+  int64_t a_ld_bytes;
   int kb_per_split;   // router: k-blocks per K slice (the n-tile index is the slice)
   float* logits_out;  // router: partial accumulators
   // cross-GPU hooks (expert parallelism over peer memory)
@@ -97,6 +107,12 @@ struct TileInfo {
   int brow0;
   int nt;
 };
+
+__device__ __forceinline__ int ld_cg_i32(const int32_t* p) {
+  int v;
+  asm volatile("ld.global.cg.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
 
 __device__ __forceinline__ const ProbParams& prob_params(const Params& p, int pb) {
   return pb ? p.pr[1] : p.pr[0];
@@ -170,6 +186,116 @@ __device__ __forceinline__ void epilogue_plain(uint32_t tb, bool valid, __nv_bfl
   }
 }
 
+// ---- staged epilogues: a warp's 32 rows x 64 columns go through a 4 KB shared-memory slab
+// (128-byte rows, 16-byte chunks XOR-swizzled by row as the SWIZZLE_128B output tensor map
+// expects, so the 8 lanes of each store phase hit 8 different bank groups) and leave in one
+// TMA bulk-tensor store of whole 128-byte lines.
+__device__ __forceinline__ void slab_put_row(uint32_t slab, int lane, const uint32_t (&w)[32]) {
+  const uint32_t row = slab + static_cast<uint32_t>(lane) * 128u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t addr = row + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * j]),
+                 "r"(w[4 * j + 1]), "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                 : "memory");
+  }
+}
+// before refilling the slab: the previous store of this warp has read it
+__device__ __forceinline__ void slab_acquire(int lane) {
+  if (lane == 0) ptx::bulk_wait_read0();
+  __syncwarp();
+}
+__device__ __forceinline__ void slab_store(const CUtensorMap* tm, uint32_t slab, int lane, int col,
+                                           int row) {
+  ptx::fence_async_shared();
+  __syncwarp();
+  if (lane == 0) {
+    ptx::tma_store_2d(tm, slab, col, row);
+    ptx::bulk_commit();
+  }
+}
+
+__device__ __forceinline__ void epilogue_plain_staged(uint32_t tb, const CUtensorMap* tm,
+                                                      uint32_t slab, int lane, int row, int col0,
+                                                      int half1_off) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t a[32], b[32];
+    ptx::tmem_ld32(tb + c * 64, a);
+    ptx::tmem_ld32(tb + c * 64 + 32, b);
+    ptx::tmem_wait_ld2(a, b);
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      w[i] = pack2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
+      w[16 + i] = pack2(__uint_as_float(b[2 * i]), __uint_as_float(b[2 * i + 1]));
+    }
+    slab_acquire(lane);
+    slab_put_row(slab, lane, w);
+    slab_store(tm, slab, lane, col0 + (c >> 1) * half1_off + (c & 1) * 64, row);
+  }
+}
+
+// Rows with arbitrary destinations (a row map, or another GPU's memory): the slab is copied
+// out by the whole warp, 8 lanes per row, so every store instruction writes four full
+// 128-byte row segments (whole NVLink / L2 lines) instead of 32 scattered 16-byte pieces.
+// dst: this lane's output row (nullptr = row not written).
+__device__ __forceinline__ void epilogue_plain_mapped(uint32_t tb, uint32_t slab, int lane,
+                                                      __nv_bfloat16* dst, int col0, int half1_off) {
+  const unsigned long long my = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t a[32], b[32];
+    ptx::tmem_ld32(tb + c * 64, a);
+    ptx::tmem_ld32(tb + c * 64 + 32, b);
+    ptx::tmem_wait_ld2(a, b);
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      w[i] = pack2(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1]));
+      w[16 + i] = pack2(__uint_as_float(b[2 * i]), __uint_as_float(b[2 * i + 1]));
+    }
+    slab_acquire(lane);  // the previous chunk's copy-out (or TMA store) has read the slab
+    slab_put_row(slab, lane, w);
+    __syncwarp();
+    const int col = col0 + (c >> 1) * half1_off + (c & 1) * 64 + (lane & 7) * 8;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int rr = it * 4 + (lane >> 3);
+      const unsigned long long d = __shfl_sync(0xffffffffu, my, rr);
+      const uint32_t addr = slab + static_cast<uint32_t>(rr) * 128u +
+                            ((static_cast<uint32_t>(lane & 7) ^ (rr & 7u)) << 4);
+      uint4 v;
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                   : "r"(addr));
+      if (d != 0ull) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d) + col) = v;
+    }
+  }
+}
+
+__device__ __forceinline__ void epilogue_swiglu_staged(uint32_t tb, const CUtensorMap* tm,
+                                                       uint32_t slab, int lane, int row, int col0) {
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    uint32_t w[32];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t g[32], u[32];
+      ptx::tmem_ld32(tb + c * 64 + h * 32, g);
+      ptx::tmem_ld32(tb + 128 + c * 64 + h * 32, u);
+      ptx::tmem_wait_ld2(g, u);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        w[h * 16 + i] = pack2(silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
+                              silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1])));
+    }
+    slab_acquire(lane);
+    slab_put_row(slab, lane, w);
+    slab_store(tm, slab, lane, col0 + c * 64, row);
+  }
+}
+
 // Router: the B operand is the f32 gate split exactly into three bf16 parts (rows [0,64) hi,
 // [64,128) mid, [128,192) lo, zero above), and each tile covers one K slice; the epilogue
 // stores the 192 raw accumulator columns of its row as f32 into the slice's partial buffer
@@ -195,13 +321,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA0,
                         const __grid_constant__ CUtensorMap tmB0,
                         const __grid_constant__ CUtensorMap tmA1,
-                        const __grid_constant__ CUtensorMap tmB1, const Params p) {
+                        const __grid_constant__ CUtensorMap tmB1,
+                        const __grid_constant__ CUtensorMap tmO0,
+                        const __grid_constant__ CUtensorMap tmO1, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t sA = ptx::smem_u32(smem);
   const uint32_t sB = sA + STAGES * A_BYTES;
-  uint8_t* tail = smem + STAGES * (A_BYTES + B_BYTES);
+  const uint32_t sOut = sA + STAGES * (A_BYTES + B_BYTES);  // 1024-aligned slabs
+  uint8_t* tail = smem + STAGES * (A_BYTES + B_BYTES) + kOutStageBytes;
   const uint32_t bar0 = ptx::smem_u32(tail);
   // barrier k lives at bar0 + 8k: full[0..S), empty[S..2S), tfull[2], tempty[2], drain
   const uint32_t full0 = bar0, empty0 = bar0 + 8u * STAGES;
@@ -211,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* never_flag = abort_flag + 1;
   int* pstart = const_cast<int*>(reinterpret_cast<volatile int*>(never_flag + 1));  // [3]
+  int* gidx = reinterpret_cast<int*>(tail + 256);  // gather mode: A row of each tile row
   int* goff = reinterpret_cast<int*>(tail + kTailBytes);
   int* gtile = goff + kMaxProblems * kGroupStride;
 
@@ -224,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      ptx::mbar_init(full0 + 8u * s, 1);
+      ptx::mbar_init(full0 + 8u * s, 32);  // one arrival per producer lane
       ptx::mbar_init(empty0 + 8u * s, 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -275,51 +405,110 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t used_mask = 0, phase_mask = 0;
-      bool ok = true;
-      uint32_t waited = 0;
-      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-        const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
-        const ProbParams& q = prob_params(p, ti.prob);
-        if (q.wait_flag != nullptr && !(waited & (1u << ti.prob))) {
-          if (!ptx::wait_flag_ge(q.wait_flag, q.wait_target, abort_flag, p.status,
-                                 p.timeout_cycles, DS_ERR_TIMEOUT)) {
-            ok = false;
-            break;
-          }
+    // Lane 0 waits on the ring and loads B (and A as one 128-row box) by TMA; in gather mode
+    // the whole warp copies the tile's A rows, picked by row index, with cp.async.
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t used_mask = 0, phase_mask = 0;
+    bool ok = true;
+    uint32_t waited = 0;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
+      const ProbParams& q = prob_params(p, ti.prob);
+      if (q.wait_flag != nullptr && !(waited & (1u << ti.prob))) {
+        int wok = 1;
+        if (lane == 0) {
+          wok = ptx::wait_flag_ge(q.wait_flag, q.wait_target, abort_flag, p.status,
+                                  p.timeout_cycles, DS_ERR_TIMEOUT)
+                    ? 1
+                    : 0;
           // peers wrote this problem's A rows with generic stores; order them before TMA reads
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-          waited |= 1u << ti.prob;
+          if (wok) asm volatile("fence.proxy.async.global;" ::: "memory");
         }
-        const CUtensorMap* tA = ti.prob ? &tmA1 : &tmA0;
-        const CUtensorMap* tB = ti.prob ? &tmB1 : &tmB0;
-        const int kb0 = EPI == kRouter ? ti.nt * q.kb_per_split : 0;
-        const int kb1 = EPI == kRouter ? min(q.k_blocks, kb0 + q.kb_per_split) : q.k_blocks;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!ptx::mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag, p.status,
-                              p.timeout_cycles, DS_ERR_TIMEOUT)) {
-            ok = false;
-            break;
+        if (!__shfl_sync(0xffffffffu, wok, 0)) {
+          ok = false;
+          break;
+        }
+        __syncwarp();  // lane 0's acquire orders the other lanes' index loads too
+        waited |= 1u << ti.prob;
+      }
+      const CUtensorMap* tA = ti.prob ? &tmA1 : &tmA0;
+      const CUtensorMap* tB = ti.prob ? &tmB1 : &tmB0;
+      const bool gather = q.a_gather != nullptr;
+      // gather mode: lane l copies, for i = 0..31, the 16-byte chunk (l & 7) of tile row
+      // 4i + (l >> 3); roff[i] = byte offset of that row in A (32 bits: A < 4 GB)
+      uint32_t roff[32];
+      if (gather) {
+        // the tile's 128 A-row indices; rows past the tile's group repeat its last row (in
+        // range, never stored), clamped into A's rows so every copy stays in bounds.
+        // Coherent loads: with a wait flag the indices were written by other GPUs meanwhile.
+        const int last = ti.row0 + ti.rows - 1;
+        __syncwarp();  // the previous tile's offsets were read from gidx
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          gidx[lane * 4 + j] =
+              min(max(ld_cg_i32(q.a_gather + min(ti.row0 + lane * 4 + j, last)), 0), q.dense_rows - 1);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          roff[i] = static_cast<uint32_t>(gidx[i * 4 + (lane >> 3)]) * static_cast<uint32_t>(q.a_ld_bytes);
+      }
+      const int kb0 = EPI == kRouter ? ti.nt * q.kb_per_split : 0;
+      const int kb1 = EPI == kRouter ? min(q.k_blocks, kb0 + q.kb_per_split) : q.k_blocks;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        int eok = 1;
+        if (lane == 0)
+          eok = ptx::mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag, p.status,
+                               p.timeout_cycles, DS_ERR_TIMEOUT)
+                    ? 1
+                    : 0;
+        if (!__shfl_sync(0xffffffffu, eok, 0)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = full0 + 8u * stage;
+        const uint32_t a_dst = sA + stage * A_BYTES;
+        const uint32_t b_dst = sB + stage * B_BYTES;
+        if (!gather) {
+          // A and B by TMA; 32 arrivals: lane 0 with the byte count, the others plain
+          if (lane == 0) {
+            ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
+            ptx::tma_load_2d(a_dst, tA, fb, kb * BK, ti.row0);
+            ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
+            ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
+          } else {
+            ptx::mbar_arrive(fb);
           }
-          const uint32_t fb = full0 + 8u * stage;
-          ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
-          const uint32_t a_dst = sA + stage * A_BYTES;
-          const uint32_t b_dst = sB + stage * B_BYTES;
-          ptx::tma_load_2d(a_dst, tA, fb, kb * BK, ti.row0);
-          ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
-          ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
-          used_mask |= 1u << stage;
-          phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+        } else {
+          // B by TMA; A gathered with cp.async: instruction i copies tile rows 4i..4i+3, 8
+          // lanes x 16 bytes per row, into the 128-byte swizzled slots the MMA expects; each
+          // lane's arrival fires when its copies have landed
+          if (lane == 0) {
+            ptx::mbar_expect_tx(fb, B_BYTES);
+            ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
+            ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
           }
+          // row r = 4i + g (g = lane >> 3) lands at r*128 + ((chunk ^ (r & 7)) << 4), and
+          // r & 7 = g + 4 (i & 1): two lane constants, the rest is per-i immediates
+          const uint32_t ch = lane & 7, g = lane >> 3;
+          const uint32_t d_even = a_dst + g * 128u + ((ch ^ g) << 4);
+          const uint32_t d_odd = a_dst + g * 128u + ((ch ^ (g + 4u)) << 4);
+          const char* abase = static_cast<const char*>(q.a_ptr) + static_cast<int64_t>(kb) * BK * 2 + ch * 16;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            ptx::cp_async16((i & 1 ? d_odd : d_even) + static_cast<uint32_t>(i) * 512u, abase + roff[i]);
+          ptx::cp_async_arrive_noinc(fb);
+        }
+        used_mask |= 1u << stage;
+        phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      // Every load issued here must land before the CTA may exit.
+    }
+    // Every load issued here must land before the CTA may exit.
+    if (lane == 0) {
       for (int s = 0; s < STAGES; ++s) {
         if (used_mask & (1u << s))
           ptx::mbar_wait(full0 + 8u * s, (phase_mask >> s) & 1u, never_flag, p.status,
@@ -355,6 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           ptx::tc_fence_after();
+          // A rows gathered by cp.async are generic-proxy writes: make them visible to the
+          // tensor core's (async-proxy) operand reads
+          if (q.a_gather != nullptr) ptx::fence_async_shared();
           const uint32_t a0 = sA + stage * A_BYTES;
           const uint32_t b0 = sB + stage * B_BYTES;
 #pragma unroll
@@ -414,13 +606,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         orow = m & 0xFFFFFF;
         valid = obase != nullptr;  // a rank outside the world has no segment: drop the row
       }
+      // a warp whose 32 rows are all in the tile's group, with contiguous output rows,
+      // stores through its shared-memory slab and TMA
+      const bool staged = qp.tma_out && q * 32 + 32 <= ti.rows;
+      const CUtensorMap* tO = ti.prob ? &tmO1 : &tmO0;
+      const uint32_t slab = sOut + static_cast<uint32_t>(warp - 2) * kSlabBytes;
       if constexpr (EPI == kSwiGLU) {
-        epilogue_swiglu(tb, valid, obase + orow * qp.ldo + ti.nt * 128);
+        if (staged)
+          epilogue_swiglu_staged(tb, tO, slab, lane, ti.row0 + q * 32, ti.nt * 128);
+        else
+          epilogue_swiglu(tb, valid, obase + orow * qp.ldo + ti.nt * 128);
       } else if constexpr (EPI == kRouter) {
         epilogue_router_partials(
             tb, valid, qp.logits_out + (static_cast<int64_t>(ti.nt) * qp.dense_rows + orow) * 192);
       } else {
-        epilogue_plain(tb, valid, obase + orow * qp.ldo, ti.nt * qp.b_tile_stride, qp.b_half1_off);
+        if (staged)
+          epilogue_plain_staged(tb, tO, slab, lane, ti.row0 + q * 32, ti.nt * qp.b_tile_stride,
+                                qp.b_half1_off);
+        else if (!qp.tma_out)
+          epilogue_plain_mapped(tb, slab, lane, valid ? obase + orow * qp.ldo : nullptr,
+                                ti.nt * qp.b_tile_stride, qp.b_half1_off);
+        else
+          epilogue_plain(tb, valid, obase + orow * qp.ldo, ti.nt * qp.b_tile_stride,
+                         qp.b_half1_off);
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -430,6 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    if (lane == 0) ptx::bulk_wait0();  // this warp's TMA stores are written
   }
 
   __syncwarp();  // lanes 1..31 of warps 0/1 rejoin their role lane before the CTA barrier
@@ -490,12 +699,13 @@ int get_encode(PFN_cuTensorMapEncodeTiled_v12000* fn) {
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix, box 64 x 128, 128-byte swizzle,
 // zero fill outside the matrix.
-int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int cols) {
+// bf16 [rows, cols] row-major, 128-byte swizzle, box {64 columns, box_rows rows}
+int make_tmap(CUtensorMap* m, const void* ptr, int64_t rows, int cols, uint32_t box_rows = 128u) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   DS_TRY(get_encode(&enc));
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), 128u};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
   cuuint32_t estr[2] = {1u, 1u};
   const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -528,6 +738,9 @@ int check_problem(const Problem& pr) {
   DS_REQUIRE(pr.a_rows < (1LL << 31) && pr.b_rows < (1LL << 31), "gemm: too many rows");
   DS_REQUIRE(pr.epilogue == kPlain || pr.epilogue == kSwiGLU || pr.epilogue == kRouter,
              "gemm: unknown epilogue %d", pr.epilogue);
+  DS_REQUIRE(pr.a_gather == nullptr ||
+                 (pr.offsets != nullptr && pr.m_rows > 0 && pr.m_rows < (1LL << 31) && !router),
+             "gemm: gather mode needs group offsets and m_rows");
   return DS_OK;
 }
 
@@ -547,6 +760,9 @@ ProbParams prob_params_of(const Problem& pr) {
   q.out_row_map = pr.out_row_map;
   q.kb_per_split = (q.k_blocks + pr.n_tiles - 1) / pr.n_tiles;
   q.logits_out = pr.logits_out;
+  q.a_gather = pr.a_gather;
+  q.a_ptr = pr.A;
+  q.a_ld_bytes = static_cast<int64_t>(pr.K) * 2;
   q.wait_flag = pr.wait_flag;
   q.wait_target = pr.wait_target;
   q.out_meta = pr.out_meta;
@@ -584,7 +800,8 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
       g_attr_set[epi][di.device] = true;
     }
   }
-  CUtensorMap tmA[kMaxProblems], tmB[kMaxProblems];
+  CUtensorMap tmA[kMaxProblems], tmB[kMaxProblems], tmO[kMaxProblems];
+  memset(tmO, 0, sizeof(tmO));
   Params p{};
   p.nprob = nl;
   p.status = device_status_ptr();
@@ -594,10 +811,17 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
   int cap = di.num_sms;
   for (int i = 0; i < nl; ++i) {
     const Problem& pr = *live[i];
-    DS_TRY(make_tmap(&tmA[i], pr.A, pr.a_rows, pr.K));
+    const bool gather = pr.a_gather != nullptr;
+    const int64_t m_rows = gather ? pr.m_rows : pr.a_rows;  // rows of the tile space / output
+    DS_TRY(make_tmap(&tmA[i], pr.A, pr.a_rows, pr.K));  // unused in gather mode
     DS_TRY(make_tmap(&tmB[i], pr.B, pr.b_rows, pr.K));
     p.pr[i] = prob_params_of(pr);
-    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
+    // output rows in tile-row order: stores leave through TMA (box = one warp's slab)
+    if (pr.epilogue != kRouter && pr.out_row_map == nullptr && pr.out_meta == nullptr) {
+      DS_TRY(make_tmap(&tmO[i], pr.out, m_rows, pr.ldo, 32u));
+      p.pr[i].tma_out = 1;
+    }
+    max_tiles += ((m_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
     if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
     // a cross-GPU wait may legitimately hold the pipeline: every wait gets its bound
     if (pr.wait_timeout_cycles > p.timeout_cycles) p.timeout_cycles = pr.wait_timeout_cycles;
@@ -605,6 +829,7 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
   if (nl == 1) {
     tmA[1] = tmA[0];
     tmB[1] = tmB[0];
+    tmO[1] = tmO[0];
   }
   const int grid = static_cast<int>(max_tiles < cap ? max_tiles : cap);
   if (sig != nullptr) {
@@ -615,11 +840,11 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
     for (int i = 0; i < sig->nsignal; ++i) p.signal_flags[i] = sig->flags[i];
   }
   if (epi == kSwiGLU)
-    grouped_gemm_kernel<kSwiGLU><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], p);
+    grouped_gemm_kernel<kSwiGLU><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
   else if (epi == kRouter)
-    grouped_gemm_kernel<kRouter><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], p);
+    grouped_gemm_kernel<kRouter><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
   else
-    grouped_gemm_kernel<kPlain><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], p);
+    grouped_gemm_kernel<kPlain><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
   DS_LAUNCH_CHECK("grouped_gemm_kernel");
   return DS_OK;
 }
@@ -637,7 +862,8 @@ int grid_for(const Problem* const* probs, int n) {
   for (int i = 0; i < n; ++i) {
     if (probs[i] == nullptr || probs[i]->a_rows <= 0) continue;
     const Problem& pr = *probs[i];
-    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
+    const int64_t m_rows = pr.a_gather ? pr.m_rows : pr.a_rows;
+    max_tiles += ((m_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
     if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
   }
   return static_cast<int>(max_tiles < cap ? max_tiles : cap);

@@ -9,6 +9,75 @@
 namespace ds {
 namespace {
 
+// Rows of at most 512 elements (the 512-d kv latent): one warp takes two rows at a time and
+// issues all four 16-byte loads per lane before the reductions, so twice the bytes are in
+// flight per warp as with one row.
+__global__ void __launch_bounds__(256)
+    rms_norm_pair_kernel(const uint4* __restrict__ in, int64_t in_stride8,
+                         const float4* __restrict__ weight, uint4* __restrict__ out,
+                         int64_t out_stride8, int rows, int H, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int H8 = H >> 3;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const float inv_h = 1.f / static_cast<float>(H);
+  for (int r0 = 2 * (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)); r0 < rows;
+       r0 += 2 * warps) {
+    uint4 v[2][2];
+    float ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = u * 32 + lane;
+        if (r0 + j < rows && c < H8) v[j][u] = __ldg(in + (r0 + j) * in_stride8 + c);
+      }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = u * 32 + lane;
+        if (r0 + j < rows && c < H8) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j][u]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            ss[j] = fmaf(f.x, f.x, ss[j]);
+            ss[j] = fmaf(f.y, f.y, ss[j]);
+          }
+        }
+      }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], d);
+      ss[1] += __shfl_xor_sync(0xffffffffu, ss[1], d);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float scale = rsqrtf(ss[j] * inv_h + eps);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = u * 32 + lane;
+        if (r0 + j < rows && c < H8) {
+          const float4 w0 = __ldg(weight + 2 * c);
+          const float4 w1 = __ldg(weight + 2 * c + 1);
+          const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j][u]);
+          uint4 o;
+          uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            const __nv_bfloat162 b =
+                __floats2bfloat162_rn(f.x * scale * wv[2 * i], f.y * scale * wv[2 * i + 1]);
+            ou[i] = *reinterpret_cast<const uint32_t*>(&b);
+          }
+          out[(r0 + j) * out_stride8 + c] = o;
+        }
+      }
+    }
+  }
+}
+
 // One warp per row.  Rows of up to 2048 elements stay in registers (8 x 16 B per lane);
 // longer rows take a second pass over global memory.
 __global__ void __launch_bounds__(256)
@@ -147,6 +216,86 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 f32x8_to_bf16(const float (&f)[8]) {
+  uint4 r;
+  uint32_t* u = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    u[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  return r;
+}
+
+// rope_dim % 16 == 0: one thread per (batch, position, 16-element chunk, group of 4 rows)
+// where the rows of a (batch, position) are the q heads and then k.  The chunk's 8 rotation
+// pairs k = 8c..8c+7 need cos/sin[k] and cos/sin[half + k] (one 16-byte load each), loaded
+// once per thread for 4 rows instead of once per row; the 4 rows' loads are issued together.
+constexpr int kRopeRows = 4;
+__global__ void __launch_bounds__(256)
+    rope_heads_kernel(const uint4* __restrict__ q, const uint4* __restrict__ k,
+                      const uint4* __restrict__ cos_t, const uint4* __restrict__ sin_t,
+                      uint4* __restrict__ qo, uint4* __restrict__ ko, int64_t bs_rows,
+                      int heads, int seq, int D) {
+  const int D8 = D >> 3, D16 = D >> 4, H8 = D >> 4;  // H8: uint4 offset of the second half
+  const int groups = (heads + 1 + kRopeRows - 1) / kRopeRows;
+  const int64_t total = bs_rows * D16 * groups;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    // consecutive threads: chunks of one row, then positions (contiguous rows), then groups
+    const int c = static_cast<int>(i % D16);
+    const int64_t t = i / D16;
+    const int64_t bs = t % bs_rows;  // b * seq + s
+    const int g = static_cast<int>(t / bs_rows);
+    const int64_t b = bs / seq, sp = bs - b * seq;
+    float cl[8], ch[8], sl[8], sh[8];
+    bf16x8_to_f32(__ldg(cos_t + bs * D8 + c), cl);
+    bf16x8_to_f32(__ldg(cos_t + bs * D8 + H8 + c), ch);
+    bf16x8_to_f32(__ldg(sin_t + bs * D8 + c), sl);
+    bf16x8_to_f32(__ldg(sin_t + bs * D8 + H8 + c), sh);
+    uint4 xv[kRopeRows][2];
+    int64_t rows[kRopeRows];
+#pragma unroll
+    for (int j = 0; j < kRopeRows; ++j) {
+      const int h = g * kRopeRows + j;  // h == heads: the k row
+      rows[j] = h < heads ? (b * heads + h) * seq + sp : (h == heads ? bs : -1);
+      if (rows[j] >= 0) {
+        const uint4* src = (h < heads ? q : k) + rows[j] * D8 + 2 * c;
+        xv[j][0] = __ldg(src);
+        xv[j][1] = __ldg(src + 1);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kRopeRows; ++j) {
+      if (rows[j] < 0) continue;
+      float x0[8], x1[8];
+      bf16x8_to_f32(xv[j][0], x0);
+      bf16x8_to_f32(xv[j][1], x1);
+      float lo[8], hi[8];
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        const float xe = p < 4 ? x0[2 * p] : x1[2 * p - 8];
+        const float xo = p < 4 ? x0[2 * p + 1] : x1[2 * p - 7];
+        lo[p] = xe * cl[p] - xo * sl[p];
+        hi[p] = xo * ch[p] + xe * sh[p];
+      }
+      uint4* dst = (g * kRopeRows + j < heads ? qo : ko) + rows[j] * D8;
+      dst[c] = f32x8_to_bf16(lo);
+      dst[H8 + c] = f32x8_to_bf16(hi);
+    }
+  }
+}
+
 // Scalar fallback for rope_dim not divisible by 8: one thread per rotation pair.
 __global__ void rope_pair_kernel(const __nv_bfloat16* __restrict__ q,
                                  const __nv_bfloat16* __restrict__ k,
@@ -203,6 +352,14 @@ int ds_rms_norm_strided(const void* input_bf16, int64_t in_stride, const float* 
                       ds::aligned16(weight))
                          ? 1
                          : 0;
+  if (vec_ok && hidden_size <= 512) {
+    const int grid = ds::grid_cap((static_cast<int64_t>(rows) + 1) / 2, 8, di.num_sms);
+    ds::rms_norm_pair_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(input_bf16), in_stride / 8, reinterpret_cast<const float4*>(weight),
+        static_cast<uint4*>(output_bf16), out_stride / 8, rows, hidden_size, eps);
+    DS_LAUNCH_CHECK("rms_norm_pair_kernel");
+    return DS_OK;
+  }
   const int grid = ds::grid_cap(rows, 8, di.num_sms);
   ds::rms_norm_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(input_bf16), in_stride, weight,
@@ -234,7 +391,17 @@ int ds_rope(const void* q_pe_bf16, const void* k_pe_bf16, const void* cos_bf16,
                    ds::aligned16(q_out_bf16) && ds::aligned16(k_out_bf16) &&
                    (reinterpret_cast<uintptr_t>(cos_bf16) & 7u) == 0 &&
                    (reinterpret_cast<uintptr_t>(sin_bf16) & 7u) == 0;
-  if (vec) {
+  const bool heads16 = vec && rope_dim % 16 == 0 && ds::aligned16(cos_bf16) && ds::aligned16(sin_bf16);
+  if (heads16) {
+    const int64_t bs_rows = static_cast<int64_t>(bsz) * seq;
+    const int groups = (heads + 1 + ds::kRopeRows - 1) / ds::kRopeRows;
+    const int grid = ds::grid_cap(bs_rows * (rope_dim / 16) * groups, 256, di.num_sms);
+    ds::rope_heads_kernel<<<grid, 256, 0, s>>>(
+        static_cast<const uint4*>(q_pe_bf16), static_cast<const uint4*>(k_pe_bf16),
+        static_cast<const uint4*>(cos_bf16), static_cast<const uint4*>(sin_bf16),
+        static_cast<uint4*>(q_out_bf16), static_cast<uint4*>(k_out_bf16), bs_rows, heads, seq,
+        rope_dim);
+  } else if (vec) {
     const int grid = ds::grid_cap((q_rows + k_rows) * (rope_dim / 8), 256, di.num_sms);
     ds::rope_vec_kernel<<<grid, 256, 0, s>>>(
         static_cast<const uint4*>(q_pe_bf16), static_cast<const uint4*>(k_pe_bf16),

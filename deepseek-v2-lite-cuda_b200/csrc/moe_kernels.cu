@@ -7,6 +7,7 @@
 // order src/reference/moe.py:95 visits tokens).  Both make every integer output
 // deterministic; the reference kernels order by warp lane (routing.cu:160-170) and by atomic
 // slot claims (dispatch.cu:76-83).
+#include <algorithm>
 #include <climits>
 #include <cmath>
 
@@ -353,6 +354,29 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Dispatch without the row copy (the GEMM gathers A rows by token id): one thread per
+// (token, pick) resolves its slot, writes token_map[slot] = token and slot_of.
+template <int K>
+__global__ void __launch_bounds__(256)
+    slot_index_kernel(int T, int E, const int32_t* __restrict__ idx,
+                      const int32_t* __restrict__ blk_base, const int32_t* __restrict__ local_rank,
+                      int32_t* __restrict__ token_map, int32_t* __restrict__ slot_of, int S) {
+  const int64_t n = static_cast<int64_t>(T) * K;
+  for (int64_t tk = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; tk < n;
+       tk += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(tk / K);
+    const int e = __ldg(idx + tk);
+    int slot = -1;
+    if (e >= 0 && e < E) {
+      const int sl = __ldg(blk_base + static_cast<int64_t>(t / kRouteTokens) * E + e) +
+                     __ldg(local_rank + tk);
+      if (sl >= 0 && sl < S) slot = sl;
+    }
+    if (slot >= 0) token_map[slot] = t;
+    slot_of[tk] = slot;
+  }
+}
+
 __device__ __forceinline__ void acc_bf16x8(float (&a)[8], const uint4& v, float w) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
@@ -481,9 +505,46 @@ __global__ void csr_fill_kernel(const int32_t* __restrict__ tm, int S, int T,
   }
 }
 
-// One warp per token.  The token's slots are visited in ascending order in batches of up
-// to 32 (rank sort when the segment fits one batch, repeated warp-min selection otherwise);
-// columns are processed 2048 at a time with f32 accumulators in registers.
+// Tokens with at most 8 slots (top-k routing): the slots are rank-sorted into shared memory
+// and each lane issues the loads of all of them for a column before summing in slot order.
+__global__ void __launch_bounds__(256)
+    combine_csr8_kernel(const uint4* __restrict__ eo, const int32_t* __restrict__ row_ptr,
+                        const int32_t* __restrict__ csr, const float* __restrict__ dw,
+                        uint4* __restrict__ out, int T, int H8) {
+  __shared__ int sl[8][8];
+  __shared__ float sw[8][8];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int t = blockIdx.x * (blockDim.x >> 5) + wid; t < T; t += warps) {
+    const int beg = __ldg(row_ptr + t);
+    const int n = __ldg(row_ptr + t + 1) - beg;
+    if (n > 8) continue;  // combine_csr_kernel
+    const int sv = lane < n ? __ldg(csr + beg + lane) : INT_MAX;
+    int rank = 0;
+    for (int q = 0; q < n; ++q) rank += (__shfl_sync(0xffffffffu, sv, q) < sv);
+    if (lane < n) {
+      sl[wid][rank] = sv;
+      sw[wid][rank] = __ldg(dw + sv);
+    }
+    __syncwarp();
+    for (int c = lane; c < H8; c += 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < n) v[j] = __ldg(eo + static_cast<int64_t>(sl[wid][j]) * H8 + c);
+      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < n) acc_bf16x8(a, v[j], sw[wid][j]);
+      out[static_cast<int64_t>(t) * H8 + c] = pack_bf16x8(a);
+    }
+    __syncwarp();  // the slot list is read before the next token's overwrites it
+  }
+}
+
+// Tokens with more than 8 slots: one warp per token visits the slots in ascending order in
+// batches of up to 32 (rank sort when the segment fits one batch, repeated warp-min
+// selection otherwise), columns 1024 at a time with f32 accumulators.
 __global__ void __launch_bounds__(256)
     combine_csr_kernel(const uint4* __restrict__ eo, const int32_t* __restrict__ row_ptr,
                        const int32_t* __restrict__ csr, const float* __restrict__ dw,
@@ -495,10 +556,11 @@ __global__ void __launch_bounds__(256)
   for (int t = blockIdx.x * (blockDim.x >> 5) + wid; t < T; t += warps) {
     const int beg = __ldg(row_ptr + t);
     const int n = __ldg(row_ptr + t + 1) - beg;
-    for (int col0 = 0; col0 < H8; col0 += 256) {
-      float a[8][8];
+    if (n <= 8) continue;  // combine_csr8_kernel
+    for (int col0 = 0; col0 < H8; col0 += 128) {
+      float a[4][8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int i = 0; i < 8; ++i) a[u][i] = 0.f;
       int done = 0;
@@ -534,7 +596,7 @@ __global__ void __launch_bounds__(256)
           const int s = sl[wid][r];
           const float wv = sw[wid][r];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
+          for (int u = 0; u < 4; ++u) {
             const int c = col0 + u * 32 + lane;
             if (c < H8) acc_bf16x8(a[u], __ldg(eo + static_cast<int64_t>(s) * H8 + c), wv);
           }
@@ -543,7 +605,7 @@ __global__ void __launch_bounds__(256)
         done += m;
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < 4; ++u) {
         const int c = col0 + u * 32 + lane;
         if (c < H8) out[static_cast<int64_t>(t) * H8 + c] = pack_bf16x8(a[u]);
       }
@@ -669,6 +731,20 @@ int launch_scatter(const void* x, int T, int H, int E, int K, const int32_t* idx
                        local_rank, static_cast<uint4*>(dispatched), token_map,
                        dispatched_weights, slot_of, S));
   DS_LAUNCH_CHECK("scatter_kernel");
+  return DS_OK;
+}
+
+int launch_slot_index(int T, int E, int K, const int32_t* idx, const int32_t* blk_base,
+                      const int32_t* local_rank, int32_t* token_map, int32_t* slot_of, int S,
+                      cudaStream_t s) {
+  if (T <= 0) return DS_OK;
+  DeviceInfo di;
+  DS_TRY(device_info(&di));
+  const int64_t n = static_cast<int64_t>(T) * K;
+  const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 8LL * di.num_sms));
+  DS_DISPATCH_K(K, slot_index_kernel<KK><<<grid, 256, 0, s>>>(T, E, idx, blk_base, local_rank,
+                                                               token_map, slot_of, S));
+  DS_LAUNCH_CHECK("slot_index_kernel");
   return DS_OK;
 }
 
@@ -823,6 +899,11 @@ int ds_moe_combine(const void* expert_output_bf16, const int32_t* token_map,
     DS_LAUNCH_CHECK("csr_fill_kernel");
   }
   const int g = ds::grid_for(num_tokens, 8, di.num_sms, 8);
+  ds::combine_csr8_kernel<<<g, 256, 0, s>>>(static_cast<const uint4*>(expert_output_bf16),
+                                            row_ptr, csr, dispatched_weights,
+                                            static_cast<uint4*>(final_output_bf16), num_tokens,
+                                            hidden_size / 8);
+  DS_LAUNCH_CHECK("combine_csr8_kernel");
   ds::combine_csr_kernel<<<g, 256, 0, s>>>(static_cast<const uint4*>(expert_output_bf16),
                                            row_ptr, csr, dispatched_weights,
                                            static_cast<uint4*>(final_output_bf16), num_tokens,
