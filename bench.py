@@ -11,8 +11,8 @@ experts fused to 2048->2816->2048, top-6 softmax routing).
 Prints ONE JSON line on rank 0.  `value` = tokens/s with inputs resident in HBM (device
 time, CUDA events, max over ranks); `e2e` = the same metric through the public API
 (FusedMoELayer) with the input copied from pinned host memory and the output copied back
-every step; `roofline` = the dominant kernel (routed grouped GEMM1) against the measured
-bf16 peak; `cpu_baseline` = the f32 CPU oracle (a restatement of src/reference/moe.py) on
+every step; `roofline` = the dominant kernel (the GEMM1 launch: routed experts + shared
+expert + SwiGLU epilogue) against the measured sustained bf16 peak; `cpu_baseline` = the f32 CPU oracle (a restatement of src/reference/moe.py) on
 a bounded sample of the same workload on this host's cores.
 
 --impl reference times the reference's CPU implementation of the path (the oracle port;

@@ -8,15 +8,12 @@
 //             a bounded wait until all rows of this forward are in (this also separates
 //             consecutive forwards: no rank passes it before every rank finished the previous
 //             one); then the bases this rank sends to and its own receive offsets.
-//   scatter : each token row is read once and written once per destination RANK (not per
-//             expert) straight into that rank's unique-row buffer (source-major, ascending
-//             token); for each selected expert the source also writes, at the expert-major
-//             position (expert-major, source rank minor, ascending token within), the row's
-//             index in the unique-row buffer and its return address (source rank, slot).  The
-//             launch's last CTA raises every rank's arrival flag.
+//   scatter : each token row is read once and written, per selected expert, straight into the
+//             owner's receive buffer (expert-major, source rank minor, ascending token within)
+//             together with its return address (source rank, slot); the launch's last CTA
+//             raises every rank's arrival flag.
 //   GEMM1   : shared-expert tiles first; the producer of the routed tiles waits for the
-//             arrival flag (every rank's rows are in), so the transfer hides behind them, then
-//             gathers each expert-major A row from the unique rows by index (cp.async).
+//             arrival flag (every rank's rows are in), so the transfer hides behind them.
 //   GEMM2   : routed tiles store each output row straight into the source rank's return
 //             buffer at its slot; the launch's last CTA raises every rank's return flag.
 //   combine : waits for the return flag, then gathers in ascending slot order as on one GPU.
@@ -40,21 +37,15 @@ constexpr int kFlagMeta = 0, kFlagArrive = 32, kFlagReturn = 64;
 constexpr int kCounterScatter = 96, kCounterGemm2 = 112;
 constexpr int kFlagInts = 128;
 
-// Count matrix row of one source rank: [0, E) tokens per expert, [E, E + world) distinct
-// tokens sent to each rank.
-constexpr int kCountStride = kMaxExperts + kMaxRanks;
-
 struct SymLayout {
-  size_t flags, counts, recv_meta, recv_index, urows, ret_rows, total;
-  int64_t cap;   // expert-major receive capacity (rows of GEMM1 / GEMM2)
-  int64_t ucap;  // unique-row capacity (one row per (source token, this rank))
+  size_t flags, counts, recv_meta, recv_rows, ret_rows, total;
+  int64_t cap;  // receive capacity in rows
 };
 
 SymLayout sym_layout(int max_tokens, int H, int E, int K, int world) {
   SymLayout L{};
   const int El = E / world;
   L.cap = static_cast<int64_t>(world) * max_tokens * (K < El ? K : El);
-  L.ucap = static_cast<int64_t>(world) * max_tokens;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -62,10 +53,9 @@ SymLayout sym_layout(int max_tokens, int H, int E, int K, int world) {
     return o;
   };
   L.flags = take(kFlagInts * sizeof(int));
-  L.counts = take(static_cast<size_t>(world) * kCountStride * sizeof(int));
+  L.counts = take(static_cast<size_t>(world) * E * sizeof(int));
   L.recv_meta = take(static_cast<size_t>(L.cap) * sizeof(int));
-  L.recv_index = take(static_cast<size_t>(L.cap) * sizeof(int));
-  L.urows = take(static_cast<size_t>(L.ucap) * H * 2);
+  L.recv_rows = take(static_cast<size_t>(L.cap) * H * 2);
   L.ret_rows = take(static_cast<size_t>(max_tokens) * K * H * 2);
   L.total = off;
   return L;
@@ -79,28 +69,21 @@ __device__ __forceinline__ int* flag_at(char* const base, size_t flags_off, int 
   return reinterpret_cast<int*>(base + flags_off) + which;
 }
 
-// Plan + count exchange.  One CTA of 1024 threads.  Local part (as the single-GPU plan):
-// 16 partitions of the routing blocks x 64 experts -> per-expert counts, offsets and block
-// bases.  Destination ranks: each thread takes a chunk of tokens, forms each token's set of
-// destination ranks, and a block scan gives every (token, rank) pair its ordinal among this
-// rank's tokens sent there (tok_uord [T, world]).
+// Plan + count exchange.  One CTA of 1024 threads = 16 partitions of the routing blocks x 64
+// experts (the local part is the single-GPU plan).
 __global__ void __launch_bounds__(1024)
-    ep_plan_kernel(const int32_t* __restrict__ hist, int nblk, const int32_t* __restrict__ idx,
-                   int T, int K, int E, int El, int rank, int world,
-                   const __grid_constant__ PeerTable peers, size_t flags_off, size_t counts_off,
-                   int target, int32_t* __restrict__ offsets, int32_t* __restrict__ blk_base,
-                   int32_t* __restrict__ dest_base, int32_t* __restrict__ recv_off,
-                   int32_t* __restrict__ tok_uord, int32_t* __restrict__ ubase_send, int64_t cap,
-                   int64_t ucap, int* status, long long timeout_cycles) {
+    ep_plan_kernel(const int32_t* __restrict__ hist, int nblk, int E, int El, int rank,
+                   int world, const __grid_constant__ PeerTable peers, size_t flags_off,
+                   size_t counts_off, int target,
+                   int32_t* __restrict__ offsets, int32_t* __restrict__ blk_base,
+                   int32_t* __restrict__ dest_base, int32_t* __restrict__ recv_off, int64_t cap,
+                   int* status, long long timeout_cycles) {
   constexpr int P = 1024 / kMaxExperts;
   __shared__ int part[P][kMaxExperts];
   __shared__ int pbase[P][kMaxExperts];
   __shared__ int off[kMaxExperts + 1];
-  __shared__ int cnt[kMaxRanks][kCountStride];
-  __shared__ int wsum[32][kMaxRanks];
-  __shared__ int utot[kMaxRanks];
+  __shared__ int cnt[kMaxRanks][kMaxExperts];
   __shared__ int ok;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e = threadIdx.x % kMaxExperts;
   const int p = threadIdx.x / kMaxExperts;
   const int chunk = (nblk + P - 1) / P;
@@ -136,78 +119,17 @@ __global__ void __launch_bounds__(1024)
       run += __ldg(hist + static_cast<int64_t>(b) * E + e);
     }
   }
-  // ---- destination ranks of this rank's tokens
-  const int tchunk = (T + 1023) / 1024;
-  const int t0 = min(T, static_cast<int>(threadIdx.x) * tchunk), t1 = min(T, t0 + tchunk);
-  auto dest_mask = [&](int t) {
-    uint32_t m = 0;
-    for (int k = 0; k < K; ++k) {
-      const int ek = __ldg(idx + static_cast<int64_t>(t) * K + k);
-      if (ek >= 0 && ek < E) m |= 1u << (ek / El);
-    }
-    return m;
-  };
-  int dc[kMaxRanks];
-#pragma unroll
-  for (int d = 0; d < kMaxRanks; ++d) dc[d] = 0;
-  for (int t = t0; t < t1; ++t) {
-    const uint32_t m = dest_mask(t);
-#pragma unroll
-    for (int d = 0; d < kMaxRanks; ++d) dc[d] += (m >> d) & 1u;
-  }
-  int incl[kMaxRanks];
-#pragma unroll
-  for (int d = 0; d < kMaxRanks; ++d) {
-    int v = dc[d];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += y;
-    }
-    incl[d] = v;
-    if (lane == 31) wsum[warp][d] = v;
-  }
-  __syncthreads();
-  if (warp == 0) {
-#pragma unroll
-    for (int d = 0; d < kMaxRanks; ++d) {
-      int v = wsum[lane][d];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += y;
-      }
-      wsum[lane][d] = v;  // inclusive over warps
-      if (lane == 31) utot[d] = v;
-    }
-  }
-  __syncthreads();
-  {
-    int run[kMaxRanks];
-#pragma unroll
-    for (int d = 0; d < kMaxRanks; ++d) run[d] = incl[d] - dc[d] + (warp > 0 ? wsum[warp - 1][d] : 0);
-    for (int t = t0; t < t1; ++t) {
-      const uint32_t m = dest_mask(t);
-#pragma unroll
-      for (int d = 0; d < kMaxRanks; ++d) {
-        if (d < world) tok_uord[static_cast<int64_t>(t) * world + d] = ((m >> d) & 1u) ? run[d] : -1;
-        run[d] += (m >> d) & 1u;
-      }
-    }
-  }
   // ---- count exchange: row `rank` of every rank's matrix, then one release per rank
-  if (threadIdx.x < E + world) {
-    const int v = threadIdx.x < E ? part[0][threadIdx.x] : utot[threadIdx.x - E];
+  if (threadIdx.x < E) {
     for (int d = 0; d < world; ++d) {
       volatile int* c = reinterpret_cast<volatile int*>(peers.base[d] + counts_off);
-      c[rank * kCountStride + threadIdx.x] = v;
+      c[rank * E + threadIdx.x] = part[0][threadIdx.x];
     }
   }
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int d = 0; d < world; ++d)
-      ptx::red_release_sys_add(flag_at(peers.base[d], flags_off, kFlagMeta), 1);
+    for (int d = 0; d < world; ++d) ptx::red_release_sys_add(flag_at(peers.base[d], flags_off, kFlagMeta), 1);
     ok = ptx::wait_flag_ge(flag_at(peers.base[rank], flags_off, kFlagMeta), target, nullptr,
                            status, timeout_cycles, DS_ERR_TIMEOUT);
   }
@@ -219,8 +141,7 @@ __global__ void __launch_bounds__(1024)
   }
   {
     const volatile int* mine = reinterpret_cast<const volatile int*>(peers.base[rank] + counts_off);
-    for (int i = threadIdx.x; i < world * kCountStride; i += blockDim.x)
-      cnt[i / kCountStride][i % kCountStride] = mine[i];
+    for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i / E][i % E] = mine[i];
   }
   __syncthreads();
   if (threadIdx.x < E) {
@@ -242,15 +163,9 @@ __global__ void __launch_bounds__(1024)
       if (d == rank) recv_off[j] = run;
       run += part[1][g];
     }
-    int ub = 0, utotal = 0;  // unique rows rank d receives from the ranks below this one
-    for (int r = 0; r < world; ++r) {
-      if (r < rank) ub += cnt[r][E + d];
-      utotal += cnt[r][E + d];
-    }
-    ubase_send[d] = ub;
     if (d == rank) {
       recv_off[El] = run;
-      if (run > cap || utotal > ucap) {  // cannot happen while every rank keeps T <= max_tokens
+      if (run > cap) {  // cannot happen while every rank keeps T <= max_tokens
         atomicOr(status, DS_ERR_WORKSPACE);
         for (int j = 0; j <= El; ++j) recv_off[j] = 0;
       }
@@ -259,30 +174,24 @@ __global__ void __launch_bounds__(1024)
 }
 
 // Fused dispatch + send: one warp per token; lanes j < K resolve the K destinations (owner
-// rank, expert-major row there) and write the return address and unique-row index there; the
-// warp reads the token row once and stores it once per distinct destination rank (local, or
-// a peer's memory over NVLink).
+// rank, row there) and write the return metadata; the warp reads the row once and stores it
+// to each destination (local or a peer's memory over NVLink).
 template <int K>
 __global__ void __launch_bounds__(256)
     ep_scatter_kernel(const uint4* __restrict__ x, int T, int H8, int E, int El, int rank,
                       int world, const int32_t* __restrict__ idx,
                       const int32_t* __restrict__ blk_base, const int32_t* __restrict__ local_rank,
                       const int32_t* __restrict__ offsets, const int32_t* __restrict__ dest_base,
-                      const int32_t* __restrict__ tok_uord, const int32_t* __restrict__ ubase_send,
                       int32_t* __restrict__ slot_of, const __grid_constant__ PeerTable peers,
-                      size_t flags_off, size_t meta_off, size_t index_off, size_t urows_off,
-                      int64_t cap, int64_t ucap, int* status) {
-  __shared__ uint4* urows_of[kMaxRanks];
+                      size_t flags_off,
+                      size_t meta_off, size_t rows_off, int64_t cap, int* status) {
+  __shared__ uint4* rows_of[kMaxRanks];
   __shared__ int* meta_of[kMaxRanks];
-  __shared__ int* index_of[kMaxRanks];
-  __shared__ int ubase[kMaxRanks];
   __shared__ int bail;
   if (threadIdx.x < kMaxRanks) {
     char* b = threadIdx.x < world ? peers.base[threadIdx.x] : nullptr;
-    urows_of[threadIdx.x] = b ? reinterpret_cast<uint4*>(b + urows_off) : nullptr;
+    rows_of[threadIdx.x] = b ? reinterpret_cast<uint4*>(b + rows_off) : nullptr;
     meta_of[threadIdx.x] = b ? reinterpret_cast<int*>(b + meta_off) : nullptr;
-    index_of[threadIdx.x] = b ? reinterpret_cast<int*>(b + index_off) : nullptr;
-    ubase[threadIdx.x] = threadIdx.x < world ? __ldg(ubase_send + threadIdx.x) : 0;
   }
   if (threadIdx.x == 0) bail = *reinterpret_cast<volatile int*>(status) != 0;
   __syncthreads();
@@ -290,7 +199,7 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
   for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
-    int my_d = -1, my_u = -1;
+    int my_d = -1, my_row = -1;
     if (lane < K) {
       const int64_t tk = static_cast<int64_t>(t) * K + lane;
       const int e = __ldg(idx + tk);
@@ -299,32 +208,20 @@ __global__ void __launch_bounds__(256)
         pos = __ldg(blk_base + static_cast<int64_t>(t / kRouteTokens) * E + e) +
               __ldg(local_rank + tk);
         const int d = e / El;
-        const int db = __ldg(dest_base + e);
-        const int64_t row = static_cast<int64_t>(db) + (pos - __ldg(offsets + e));
-        const int uo = d < world ? __ldg(tok_uord + static_cast<int64_t>(t) * world + d) : -1;
-        const int64_t u = static_cast<int64_t>(ubase[d < world ? d : 0]) + uo;
-        if (d < world && db >= 0 && row >= 0 && row < cap && uo >= 0 && u < ucap) {
+        const int64_t row = static_cast<int64_t>(__ldg(dest_base + e)) + (pos - __ldg(offsets + e));
+        if (d < world && __ldg(dest_base + e) >= 0 && row >= 0 && row < cap) {
           my_d = d;
-          my_u = static_cast<int>(u);
+          my_row = static_cast<int>(row);
           meta_of[d][row] = (rank << 24) | pos;
-          index_of[d][row] = my_u;
         }
       }
       slot_of[tk] = pos;
     }
-    int dd[K], uu[K];
+    int dd[K], rr[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) {
       dd[j] = __shfl_sync(0xffffffffu, my_d, j);
-      uu[j] = __shfl_sync(0xffffffffu, my_u, j);
-    }
-    // one copy per distinct destination rank: pick j sends unless an earlier pick has its rank
-    bool first[K];
-#pragma unroll
-    for (int j = 0; j < K; ++j) {
-      first[j] = dd[j] >= 0;
-#pragma unroll
-      for (int i = 0; i < j; ++i) first[j] = first[j] && dd[i] != dd[j];
+      rr[j] = __shfl_sync(0xffffffffu, my_row, j);
     }
     const uint4* src = x + static_cast<int64_t>(t) * H8;
     for (int c0 = 0; c0 < H8; c0 += 32 * 8) {
@@ -336,8 +233,8 @@ __global__ void __launch_bounds__(256)
       }
 #pragma unroll
       for (int j = 0; j < K; ++j) {
-        if (!first[j]) continue;
-        uint4* dst = urows_of[dd[j]] + static_cast<int64_t>(uu[j]) * H8;
+        if (dd[j] < 0) continue;
+        uint4* dst = rows_of[dd[j]] + static_cast<int64_t>(rr[j]) * H8;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int c = c0 + u * 32 + lane;
@@ -372,8 +269,6 @@ struct EPBuffers {
   int32_t* slot_of;
   int32_t* dest_base;
   int32_t* recv_off;
-  int32_t* tok_uord;    // [max_tokens, world]
-  int32_t* ubase_send;  // [kMaxRanks]
   float* router_part;
   void* h;   // bf16 [cap, I]
   void* sh;  // bf16 [max_tokens, Is]
@@ -394,8 +289,6 @@ size_t carve_ep(Carve& c, EPBuffers* b, int Tm, int H, int E, int K, int I, int 
   x.slot_of = c.take<int32_t>(S);
   x.dest_base = c.take<int32_t>(E);
   x.recv_off = c.take<int32_t>(E / world + 1);
-  x.tok_uord = c.take<int32_t>(static_cast<size_t>(Tm) * world);
-  x.ubase_send = c.take<int32_t>(kMaxRanks);
   x.router_part = c.take<float>(static_cast<size_t>(kRouterSplits) * Tm * kRouterPartCols);
   x.h = c.take<__nv_bfloat16>(static_cast<size_t>(L.cap) * I);
   x.sh = c.take<__nv_bfloat16>(Is > 0 ? static_cast<size_t>(Tm) * Is : 0);
@@ -558,10 +451,9 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
                                      b.w, nullptr, b.blk_hist, b.local_rank, s));
   }
   DS_TRY(mark(1));
-  ep::ep_plan_kernel<<<1, 1024, 0, s>>>(b.blk_hist, nblk, b.idx, T, K, E, El, rank, world, peers,
-                                        L.flags, L.counts, target, b.offsets, b.blk_base,
-                                        b.dest_base, b.recv_off, b.tok_uord, b.ubase_send, L.cap,
-                                        L.ucap, status, timeout_cycles);
+  ep::ep_plan_kernel<<<1, 1024, 0, s>>>(b.blk_hist, nblk, E, El, rank, world, peers, L.flags,
+                                        L.counts, target, b.offsets, b.blk_base, b.dest_base,
+                                        b.recv_off, L.cap, status, timeout_cycles);
   DS_LAUNCH_CHECK("ep_plan_kernel");
   DS_TRY(mark(2));
   {
@@ -569,8 +461,8 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
 #define DS_EP_SCATTER(KK)                                                                     \
   ep::ep_scatter_kernel<KK><<<grid, 256, 0, s>>>(                                             \
       static_cast<const uint4*>(x_bf16), T, H / 8, E, El, rank, world, b.idx, b.blk_base,     \
-      b.local_rank, b.offsets, b.dest_base, b.tok_uord, b.ubase_send, b.slot_of, peers,       \
-      L.flags, L.recv_meta, L.recv_index, L.urows, L.cap, L.ucap, status)
+      b.local_rank, b.offsets, b.dest_base, b.slot_of, peers, L.flags, L.recv_meta,           \
+      L.recv_rows, L.cap, status)
     switch (K) {
       case 1: DS_EP_SCATTER(1); break;
       case 2: DS_EP_SCATTER(2); break;
@@ -606,10 +498,8 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
     s1.epilogue = ds::gemm::kSwiGLU;
   }
   ds::gemm::Problem g1{};
-  g1.A = mine + L.urows;
-  g1.a_rows = L.ucap;
-  g1.a_gather = reinterpret_cast<const int32_t*>(mine + L.recv_index);
-  g1.m_rows = L.cap;
+  g1.A = mine + L.recv_rows;
+  g1.a_rows = L.cap;
   g1.K = H;
   g1.B = w1_local_bf16;
   g1.b_rows = static_cast<int64_t>(El) * 2 * I;

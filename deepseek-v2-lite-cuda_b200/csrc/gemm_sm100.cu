@@ -5,9 +5,8 @@
 // src/kernels/mla/kv_upproj.cu:77-119.
 //
 // Structure (one persistent CTA per SM, 192 threads):
-//   warp 0       producer: A tile 128x64 (one TMA box, or in gather mode rows picked by
-//                index, copied by the warp with cp.async) and B tile 256x64 (two 128-row
-//                TMA boxes) per k-block into a 4-stage shared-memory ring (128-byte swizzle).
+//   warp 0       TMA producer: A tile 128x64 and B tile 256x64 (two 128-row boxes) per
+//                k-block into a 4-stage shared-memory ring (128-byte swizzle).
 //   warp 1       MMA issuer: tcgen05.mma kind::f16, M=128 N=256 K=16, f32 accumulator in
 //                TMEM, two accumulator buffers (2 x 256 columns) so the epilogue of tile i
 //                overlaps the MMAs of tile i+1.
@@ -42,8 +41,7 @@ constexpr uint32_t STAGE_TX = A_BYTES + B_BYTES;
 constexpr int kMaxGroups = 512;
 constexpr int kMaxProblems = 2;
 constexpr uint32_t kTmemCols = 512;
-// barriers + tmem holder + flags + problem tile starts (256 B), gather row indices (512 B)
-constexpr uint32_t kTailBytes = 256 + 512;
+constexpr uint32_t kTailBytes = 256;  // barriers + tmem holder + flags + problem tile starts
 constexpr int kGroupStride = kMaxGroups + 1;
 // output staging: per epilogue warp one 32-row x 128-byte slab (swizzled as SWIZZLE_128B)
 constexpr uint32_t kSlabBytes = 32 * 128;
@@ -67,9 +65,6 @@ struct ProbParams {
   int ldo;
   const int32_t* out_row_map;
   int tma_out;        // contiguous output rows: full 32-row slabs leave by TMA store
-  const int32_t* a_gather;  // gather mode: A row of each tile row (slot -> token)
-  const void* a_ptr;        // gather mode: A base and row pitch in bytes
-  int64_t a_ld_bytes;
   int kb_per_split;   // router: k-blocks per K slice (the n-tile index is the slice)
   float* logits_out;  // router: partial accumulators
   // cross-GPU hooks (expert parallelism over peer memory)
@@ -107,12 +102,6 @@ struct TileInfo {
   int brow0;
   int nt;
 };
-
-__device__ __forceinline__ int ld_cg_i32(const int32_t* p) {
-  int v;
-  asm volatile("ld.global.cg.b32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
 
 __device__ __forceinline__ const ProbParams& prob_params(const Params& p, int pb) {
   return pb ? p.pr[1] : p.pr[0];
@@ -340,7 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* never_flag = abort_flag + 1;
   int* pstart = const_cast<int*>(reinterpret_cast<volatile int*>(never_flag + 1));  // [3]
-  int* gidx = reinterpret_cast<int*>(tail + 256);  // gather mode: A row of each tile row
   int* goff = reinterpret_cast<int*>(tail + kTailBytes);
   int* gtile = goff + kMaxProblems * kGroupStride;
 
@@ -354,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      ptx::mbar_init(full0 + 8u * s, 32);  // one arrival per producer lane
+      ptx::mbar_init(full0 + 8u * s, 1);
       ptx::mbar_init(empty0 + 8u * s, 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -405,110 +393,51 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // Lane 0 waits on the ring and loads B (and A as one 128-row box) by TMA; in gather mode
-    // the whole warp copies the tile's A rows, picked by row index, with cp.async.
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t used_mask = 0, phase_mask = 0;
-    bool ok = true;
-    uint32_t waited = 0;
-    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
-      const ProbParams& q = prob_params(p, ti.prob);
-      if (q.wait_flag != nullptr && !(waited & (1u << ti.prob))) {
-        int wok = 1;
-        if (lane == 0) {
-          wok = ptx::wait_flag_ge(q.wait_flag, q.wait_target, abort_flag, p.status,
-                                  p.timeout_cycles, DS_ERR_TIMEOUT)
-                    ? 1
-                    : 0;
-          // peers wrote this problem's A rows with generic stores; order them before TMA reads
-          if (wok) asm volatile("fence.proxy.async.global;" ::: "memory");
-        }
-        if (!__shfl_sync(0xffffffffu, wok, 0)) {
-          ok = false;
-          break;
-        }
-        __syncwarp();  // lane 0's acquire orders the other lanes' index loads too
-        waited |= 1u << ti.prob;
-      }
-      const CUtensorMap* tA = ti.prob ? &tmA1 : &tmA0;
-      const CUtensorMap* tB = ti.prob ? &tmB1 : &tmB0;
-      const bool gather = q.a_gather != nullptr;
-      // gather mode: lane l copies, for i = 0..31, the 16-byte chunk (l & 7) of tile row
-      // 4i + (l >> 3); roff[i] = byte offset of that row in A (32 bits: A < 4 GB)
-      uint32_t roff[32];
-      if (gather) {
-        // the tile's 128 A-row indices; rows past the tile's group repeat its last row (in
-        // range, never stored), clamped into A's rows so every copy stays in bounds.
-        // Coherent loads: with a wait flag the indices were written by other GPUs meanwhile.
-        const int last = ti.row0 + ti.rows - 1;
-        __syncwarp();  // the previous tile's offsets were read from gidx
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          gidx[lane * 4 + j] =
-              min(max(ld_cg_i32(q.a_gather + min(ti.row0 + lane * 4 + j, last)), 0), q.dense_rows - 1);
-        __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          roff[i] = static_cast<uint32_t>(gidx[i * 4 + (lane >> 3)]) * static_cast<uint32_t>(q.a_ld_bytes);
-      }
-      const int kb0 = EPI == kRouter ? ti.nt * q.kb_per_split : 0;
-      const int kb1 = EPI == kRouter ? min(q.k_blocks, kb0 + q.kb_per_split) : q.k_blocks;
-      for (int kb = kb0; kb < kb1; ++kb) {
-        int eok = 1;
-        if (lane == 0)
-          eok = ptx::mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag, p.status,
-                               p.timeout_cycles, DS_ERR_TIMEOUT)
-                    ? 1
-                    : 0;
-        if (!__shfl_sync(0xffffffffu, eok, 0)) {
-          ok = false;
-          break;
-        }
-        const uint32_t fb = full0 + 8u * stage;
-        const uint32_t a_dst = sA + stage * A_BYTES;
-        const uint32_t b_dst = sB + stage * B_BYTES;
-        if (!gather) {
-          // A and B by TMA; 32 arrivals: lane 0 with the byte count, the others plain
-          if (lane == 0) {
-            ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
-            ptx::tma_load_2d(a_dst, tA, fb, kb * BK, ti.row0);
-            ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
-            ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
-          } else {
-            ptx::mbar_arrive(fb);
-          }
-        } else {
-          // B by TMA; A gathered with cp.async: instruction i copies tile rows 4i..4i+3, 8
-          // lanes x 16 bytes per row, into the 128-byte swizzled slots the MMA expects; each
-          // lane's arrival fires when its copies have landed
-          if (lane == 0) {
-            ptx::mbar_expect_tx(fb, B_BYTES);
-            ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
-            ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
-          }
-          // row r = 4i + g (g = lane >> 3) lands at r*128 + ((chunk ^ (r & 7)) << 4), and
-          // r & 7 = g + 4 (i & 1): two lane constants, the rest is per-i immediates
-          const uint32_t ch = lane & 7, g = lane >> 3;
-          const uint32_t d_even = a_dst + g * 128u + ((ch ^ g) << 4);
-          const uint32_t d_odd = a_dst + g * 128u + ((ch ^ (g + 4u)) << 4);
-          const char* abase = static_cast<const char*>(q.a_ptr) + static_cast<int64_t>(kb) * BK * 2 + ch * 16;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            ptx::cp_async16((i & 1 ? d_odd : d_even) + static_cast<uint32_t>(i) * 512u, abase + roff[i]);
-          ptx::cp_async_arrive_noinc(fb);
-        }
-        used_mask |= 1u << stage;
-        phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-    }
-    // Every load issued here must land before the CTA may exit.
     if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t used_mask = 0, phase_mask = 0;
+      bool ok = true;
+      uint32_t waited = 0;
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+        const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
+        const ProbParams& q = prob_params(p, ti.prob);
+        if (q.wait_flag != nullptr && !(waited & (1u << ti.prob))) {
+          if (!ptx::wait_flag_ge(q.wait_flag, q.wait_target, abort_flag, p.status,
+                                 p.timeout_cycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          // peers wrote this problem's A rows with generic stores; order them before TMA reads
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          waited |= 1u << ti.prob;
+        }
+        const CUtensorMap* tA = ti.prob ? &tmA1 : &tmA0;
+        const CUtensorMap* tB = ti.prob ? &tmB1 : &tmB0;
+        const int kb0 = EPI == kRouter ? ti.nt * q.kb_per_split : 0;
+        const int kb1 = EPI == kRouter ? min(q.k_blocks, kb0 + q.kb_per_split) : q.k_blocks;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!ptx::mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag, p.status,
+                              p.timeout_cycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + 8u * stage;
+          ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
+          const uint32_t a_dst = sA + stage * A_BYTES;
+          const uint32_t b_dst = sB + stage * B_BYTES;
+          ptx::tma_load_2d(a_dst, tA, fb, kb * BK, ti.row0);
+          ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
+          ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
+          used_mask |= 1u << stage;
+          phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Every load issued here must land before the CTA may exit.
       for (int s = 0; s < STAGES; ++s) {
         if (used_mask & (1u << s))
           ptx::mbar_wait(full0 + 8u * s, (phase_mask >> s) & 1u, never_flag, p.status,
@@ -544,9 +473,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           ptx::tc_fence_after();
-          // A rows gathered by cp.async are generic-proxy writes: make them visible to the
-          // tensor core's (async-proxy) operand reads
-          if (q.a_gather != nullptr) ptx::fence_async_shared();
           const uint32_t a0 = sA + stage * A_BYTES;
           const uint32_t b0 = sB + stage * B_BYTES;
 #pragma unroll
@@ -738,9 +664,6 @@ int check_problem(const Problem& pr) {
   DS_REQUIRE(pr.a_rows < (1LL << 31) && pr.b_rows < (1LL << 31), "gemm: too many rows");
   DS_REQUIRE(pr.epilogue == kPlain || pr.epilogue == kSwiGLU || pr.epilogue == kRouter,
              "gemm: unknown epilogue %d", pr.epilogue);
-  DS_REQUIRE(pr.a_gather == nullptr ||
-                 (pr.offsets != nullptr && pr.m_rows > 0 && pr.m_rows < (1LL << 31) && !router),
-             "gemm: gather mode needs group offsets and m_rows");
   return DS_OK;
 }
 
@@ -760,9 +683,6 @@ ProbParams prob_params_of(const Problem& pr) {
   q.out_row_map = pr.out_row_map;
   q.kb_per_split = (q.k_blocks + pr.n_tiles - 1) / pr.n_tiles;
   q.logits_out = pr.logits_out;
-  q.a_gather = pr.a_gather;
-  q.a_ptr = pr.A;
-  q.a_ld_bytes = static_cast<int64_t>(pr.K) * 2;
   q.wait_flag = pr.wait_flag;
   q.wait_target = pr.wait_target;
   q.out_meta = pr.out_meta;
@@ -811,17 +731,15 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
   int cap = di.num_sms;
   for (int i = 0; i < nl; ++i) {
     const Problem& pr = *live[i];
-    const bool gather = pr.a_gather != nullptr;
-    const int64_t m_rows = gather ? pr.m_rows : pr.a_rows;  // rows of the tile space / output
-    DS_TRY(make_tmap(&tmA[i], pr.A, pr.a_rows, pr.K));  // unused in gather mode
+    DS_TRY(make_tmap(&tmA[i], pr.A, pr.a_rows, pr.K));
     DS_TRY(make_tmap(&tmB[i], pr.B, pr.b_rows, pr.K));
     p.pr[i] = prob_params_of(pr);
-    // output rows in tile-row order: stores leave through TMA (box = one warp's slab)
+    // output rows = A rows, in order: stores leave through TMA (box = one warp's slab)
     if (pr.epilogue != kRouter && pr.out_row_map == nullptr && pr.out_meta == nullptr) {
-      DS_TRY(make_tmap(&tmO[i], pr.out, m_rows, pr.ldo, 32u));
+      DS_TRY(make_tmap(&tmO[i], pr.out, pr.a_rows, pr.ldo, 32u));
       p.pr[i].tma_out = 1;
     }
-    max_tiles += ((m_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
+    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
     if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
     // a cross-GPU wait may legitimately hold the pipeline: every wait gets its bound
     if (pr.wait_timeout_cycles > p.timeout_cycles) p.timeout_cycles = pr.wait_timeout_cycles;
@@ -862,8 +780,7 @@ int grid_for(const Problem* const* probs, int n) {
   for (int i = 0; i < n; ++i) {
     if (probs[i] == nullptr || probs[i]->a_rows <= 0) continue;
     const Problem& pr = *probs[i];
-    const int64_t m_rows = pr.a_gather ? pr.m_rows : pr.a_rows;
-    max_tiles += ((m_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
+    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
     if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
   }
   return static_cast<int>(max_tiles < cap ? max_tiles : cap);

@@ -46,12 +46,6 @@ int launch_scatter(const void* x, int T, int H, int E, int K, const int32_t* idx
                    void* dispatched, int32_t* token_map, float* dispatched_weights,
                    int32_t* slot_of, int S, cudaStream_t s);
 
-// The slot bookkeeping of launch_scatter without the row copies: token_map [S], slot_of
-// [T, K] (for GEMMs that gather their A rows by token id).
-int launch_slot_index(int T, int E, int K, const int32_t* idx, const int32_t* blk_base,
-                      const int32_t* local_rank, int32_t* token_map, int32_t* slot_of, int S,
-                      cudaStream_t s);
-
 // out[t] = sum_j w[t,j] * eo[slot_of[t,j]] (+ shared[t]), slots in ascending order.  With
 // wait_flag, each CTA first waits (bounded by timeout_cycles) until *wait_flag >= wait_target
 // (rows of eo written by other GPUs) and reads eo through L2.
@@ -95,11 +89,6 @@ struct Problem {
   // expert parallelism over peer memory: wait until *wait_flag >= wait_target before reading
   // this problem's A; write output row i to out_peers[meta >> 24] + (meta & 0xFFFFFF) * ldo
   // with meta = out_meta[i] (out unused then)
-  // gather mode: A is a matrix of a_rows source rows and tile row i of the group space
-  // (m_rows rows, partitioned by offsets) reads A row a_gather[i] (cp.async gather); the
-  // output has m_rows rows
-  const int32_t* a_gather = nullptr;
-  int64_t m_rows = 0;
   const int* wait_flag = nullptr;
   int wait_target = 0;
   long long wait_timeout_cycles = 0;  // 0: the default bound of every wait in the kernel

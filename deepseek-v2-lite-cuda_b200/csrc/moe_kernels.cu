@@ -354,29 +354,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Dispatch without the row copy (the GEMM gathers A rows by token id): one thread per
-// (token, pick) resolves its slot, writes token_map[slot] = token and slot_of.
-template <int K>
-__global__ void __launch_bounds__(256)
-    slot_index_kernel(int T, int E, const int32_t* __restrict__ idx,
-                      const int32_t* __restrict__ blk_base, const int32_t* __restrict__ local_rank,
-                      int32_t* __restrict__ token_map, int32_t* __restrict__ slot_of, int S) {
-  const int64_t n = static_cast<int64_t>(T) * K;
-  for (int64_t tk = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; tk < n;
-       tk += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int t = static_cast<int>(tk / K);
-    const int e = __ldg(idx + tk);
-    int slot = -1;
-    if (e >= 0 && e < E) {
-      const int sl = __ldg(blk_base + static_cast<int64_t>(t / kRouteTokens) * E + e) +
-                     __ldg(local_rank + tk);
-      if (sl >= 0 && sl < S) slot = sl;
-    }
-    if (slot >= 0) token_map[slot] = t;
-    slot_of[tk] = slot;
-  }
-}
-
 __device__ __forceinline__ void acc_bf16x8(float (&a)[8], const uint4& v, float w) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
@@ -731,20 +708,6 @@ int launch_scatter(const void* x, int T, int H, int E, int K, const int32_t* idx
                        local_rank, static_cast<uint4*>(dispatched), token_map,
                        dispatched_weights, slot_of, S));
   DS_LAUNCH_CHECK("scatter_kernel");
-  return DS_OK;
-}
-
-int launch_slot_index(int T, int E, int K, const int32_t* idx, const int32_t* blk_base,
-                      const int32_t* local_rank, int32_t* token_map, int32_t* slot_of, int S,
-                      cudaStream_t s) {
-  if (T <= 0) return DS_OK;
-  DeviceInfo di;
-  DS_TRY(device_info(&di));
-  const int64_t n = static_cast<int64_t>(T) * K;
-  const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 8LL * di.num_sms));
-  DS_DISPATCH_K(K, slot_index_kernel<KK><<<grid, 256, 0, s>>>(T, E, idx, blk_base, local_rank,
-                                                               token_map, slot_of, S));
-  DS_LAUNCH_CHECK("slot_index_kernel");
   return DS_OK;
 }
 

@@ -1,6 +1,5 @@
-// Fused DeepSeek-V2-Lite MoE layer: routing -> plan -> dispatch (slot bookkeeping; GEMM1
-// gathers its A rows from the tokens by TMA) -> grouped GEMM1+SwiGLU -> grouped GEMM2 (the
-// shared expert inside both launches) -> combine, all on one stream with no host
+// Fused DeepSeek-V2-Lite MoE layer: routing -> plan -> dispatch -> grouped GEMM1+SwiGLU ->
+// grouped GEMM2 -> (shared expert GEMMs) -> combine, all on one stream with no host
 // synchronisation.  Mirrors the pipeline of src/kernels/moe_fused.py:118-154 and adds the
 // shared expert of src/reference/moe.py:72-74,106-107.
 #include "kernels.cuh"
@@ -17,6 +16,7 @@ struct LayerBuffers {
   int32_t* blk_base;
   int32_t* token_map;
   int32_t* slot_of;
+  void* dispatched;  // bf16 [S, H]
   void* h;           // bf16 [S, I]
   void* eo;          // bf16 [S, H]
   void* sh;          // bf16 [T, Is]
@@ -36,6 +36,7 @@ size_t carve_layer(Carve& c, LayerBuffers* b, int T, int H, int E, int K, int I,
   x.blk_base = c.take<int32_t>(nblk * E);
   x.token_map = c.take<int32_t>(S);
   x.slot_of = c.take<int32_t>(S);
+  x.dispatched = c.take<__nv_bfloat16>(S * H);
   x.h = c.take<__nv_bfloat16>(S * I);
   x.eo = c.take<__nv_bfloat16>(S * H);
   x.sh = c.take<__nv_bfloat16>(Is > 0 ? static_cast<size_t>(T) * Is : 0);
@@ -125,19 +126,16 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
   DS_TRY(mark(1));
   DS_TRY(ds::launch_plan(b.blk_hist, nblk, E, nullptr, nullptr, b.offsets, b.blk_base, s));
   DS_TRY(mark(2));
-  // dispatch = slot bookkeeping only: GEMM1 gathers each slot's token row straight from x
-  DS_TRY(ds::launch_slot_index(T, E, K, b.idx, b.blk_base, b.local_rank, b.token_map, b.slot_of,
-                               S, s));
+  DS_TRY(ds::launch_scatter(x_bf16, T, H, E, K, b.idx, b.w, b.blk_base, b.local_rank,
+                            b.dispatched, b.token_map, nullptr, b.slot_of, S, s));
   DS_TRY(mark(3));
 
   // GEMM1 (+ SwiGLU) of the routed experts and of the shared expert in one persistent launch,
   // then GEMM2 of both (the shared expert's long-K tiles first, so the short routed tiles
   // fill the end of the launch).
   ds::gemm::Problem g1{};
-  g1.A = x_bf16;
-  g1.a_rows = T;
-  g1.a_gather = b.token_map;
-  g1.m_rows = S;
+  g1.A = b.dispatched;
+  g1.a_rows = S;
   g1.K = H;
   g1.B = packed_w1_bf16;
   g1.b_rows = static_cast<int64_t>(E) * 2 * I;

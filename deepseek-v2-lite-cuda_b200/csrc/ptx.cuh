@@ -76,21 +76,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
-// ---- cp.async (16-byte global -> shared copies, per thread) ----------------------------
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-// one arrival on `bar` once all of this thread's earlier cp.async copies have landed (the
-// arrival is one of the barrier's expected arrivals: .noinc)
-__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-// add `bytes` to the barrier's expected transaction count without arriving
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-
 // 2-D tiled bulk-tensor store shared -> global (bulk-group completion).  x = innermost
 // coordinate (elements, a multiple of 16 bytes), y = row; both non-negative.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int x, int y) {
