@@ -1,5 +1,5 @@
-// Library-wide host state: error messages, per-device facts, the device status word, the
-// hello stub and the bounded-wait probe.
+// Library-wide host state: error messages, per-device facts and side streams, the device
+// status word, the hello stub and the bounded-wait probe.
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -37,6 +37,25 @@ int cuda_fail(cudaError_t e, const char* where) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", where, cudaGetErrorString(e),
            cudaGetErrorName(e));
   return DS_ERR_CUDA;
+}
+
+static SideStream g_side[kMaxDevices];
+static bool g_side_ready[kMaxDevices] = {};
+static std::mutex g_side_mutex;
+
+int side_stream(int dev, SideStream* out) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(DS_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  std::lock_guard<std::mutex> lock(g_side_mutex);
+  if (!g_side_ready[dev]) {
+    SideStream ss{};
+    DS_CUDA(cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking));
+    DS_CUDA(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming));
+    DS_CUDA(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming));
+    g_side[dev] = ss;
+    g_side_ready[dev] = true;
+  }
+  *out = g_side[dev];
+  return DS_OK;
 }
 
 int device_info(DeviceInfo* out) {

@@ -23,6 +23,16 @@ struct DeviceInfo {
 };
 int device_info(DeviceInfo* out);
 
+// A second stream per device (with a fork and a join event) for work that overlaps the
+// caller's stream inside one entry point: forked from and joined back into the caller's
+// stream, so the entry point stays stream-ordered.  Created on first use; entry points that
+// use it must not run concurrently on one device from several host threads.
+struct SideStream {
+  cudaStream_t stream;
+  cudaEvent_t fork, join;
+};
+int side_stream(int device, SideStream* out);
+
 // Device status word (one per device, lives in this library's module).
 int* device_status_ptr();
 

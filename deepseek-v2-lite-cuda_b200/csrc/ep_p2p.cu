@@ -61,6 +61,9 @@ SymLayout sym_layout(int max_tokens, int H, int E, int K, int world) {
   return L;
 }
 
+// SMs the shared-expert GEMM1 leaves to the dispatch kernel it overlaps
+constexpr int kDispatchSMs = 32;
+
 struct PeerTable {
   char* base[kMaxRanks];
 };
@@ -451,6 +454,34 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
                                      b.w, nullptr, b.blk_hist, b.local_rank, s));
   }
   DS_TRY(mark(1));
+  // the shared expert's GEMM1 (SwiGLU) needs only this rank's tokens: it runs on a side
+  // stream, capped below the SM count, while the plan and the dispatch kernel (which is
+  // bound by NVLink, not by SMs) run here; joined back before GEMM2
+  const bool side = has_shared && T > 0;
+  if (side) {
+    ds::SideStream ss;
+    DS_TRY(ds::side_stream(di.device, &ss));
+    ds::gemm::Problem s1{};
+    s1.A = x_bf16;
+    s1.a_rows = T;
+    s1.K = H;
+    s1.B = shared_w1_bf16;
+    s1.b_rows = 2 * static_cast<int64_t>(Is);
+    s1.groups = 1;
+    s1.n_tiles = Is / 128;
+    s1.b_rows_per_group = 2 * Is;
+    s1.b_tile_stride = 128;
+    s1.b_half1_off = Is;
+    s1.weight_group_mod = 1;
+    s1.out = b.sh;
+    s1.ldo = Is;
+    s1.epilogue = ds::gemm::kSwiGLU;
+    s1.max_ctas = di.num_sms > 2 * ep::kDispatchSMs ? di.num_sms - ep::kDispatchSMs : di.num_sms;
+    DS_CUDA(cudaEventRecord(ss.fork, s));
+    DS_CUDA(cudaStreamWaitEvent(ss.stream, ss.fork, 0));
+    DS_TRY(ds::gemm::launch(s1, ss.stream));
+    DS_CUDA(cudaEventRecord(ss.join, ss.stream));
+  }
   ep::ep_plan_kernel<<<1, 1024, 0, s>>>(b.blk_hist, nblk, E, El, rank, world, peers, L.flags,
                                         L.counts, target, b.offsets, b.blk_base, b.dest_base,
                                         b.recv_off, L.cap, status, timeout_cycles);
@@ -478,25 +509,7 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
   }
   DS_TRY(mark(3));
 
-  // GEMM1 (+ SwiGLU): shared expert on this rank's tokens first, then the routed rows of this
-  // rank's experts as they arrive from every rank.
-  ds::gemm::Problem s1{};
-  if (has_shared && T > 0) {
-    s1.A = x_bf16;
-    s1.a_rows = T;
-    s1.K = H;
-    s1.B = shared_w1_bf16;
-    s1.b_rows = 2 * static_cast<int64_t>(Is);
-    s1.groups = 1;
-    s1.n_tiles = Is / 128;
-    s1.b_rows_per_group = 2 * Is;
-    s1.b_tile_stride = 128;
-    s1.b_half1_off = Is;
-    s1.weight_group_mod = 1;
-    s1.out = b.sh;
-    s1.ldo = Is;
-    s1.epilogue = ds::gemm::kSwiGLU;
-  }
+  // GEMM1 (+ SwiGLU) of the routed rows of this rank's experts as they arrive from every rank
   ds::gemm::Problem g1{};
   g1.A = mine + L.recv_rows;
   g1.a_rows = L.cap;
@@ -516,11 +529,13 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
   g1.wait_flag = my_flags + ep::kFlagArrive;
   g1.wait_target = target;
   g1.wait_timeout_cycles = timeout_cycles;
-  {
-    const ds::gemm::Problem* probs[2] = {(has_shared && T > 0) ? &s1 : nullptr, &g1};
-    DS_TRY(ds::gemm::launch_multi(probs, 2, s));
-  }
+  DS_TRY(ds::gemm::launch(g1, s));
   DS_TRY(mark(4));
+  if (side) {
+    ds::SideStream ss;
+    DS_TRY(ds::side_stream(di.device, &ss));
+    DS_CUDA(cudaStreamWaitEvent(s, ss.join, 0));  // the shared expert's h for GEMM2
+  }
 
   // GEMM2: routed rows first (their outputs cross NVLink while the shared tiles run), each
   // row stored at its source rank's return slot; then the shared expert.  The launch's last

@@ -6,7 +6,8 @@ slot order, so the expert-parallel output must equal the single-GPU fused layer
 also checked against the oracle directly (max-abs 2e-2, rel-L2 1e-2).  Failure detection:
 a rank that stops taking part makes the other rank's bounded in-kernel wait run out; the
 device status reads DS_ERR_TIMEOUT and the context stays usable.  Multi-rank cases run one
-process per GPU (skipped with fewer than 2 GPUs), NVLS off, plain peer loads and stores.
+process per GPU (2, 4 and 8 ranks, each skipped without enough GPUs), NVLS off, plain peer
+loads and stores.
 """
 import datetime
 import os
@@ -180,9 +181,11 @@ def _run(world, mode):
     return sorted(res)
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks_equal_fused_layer():
-    for rank, ok, exc in _run(2, "exact"):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ranks_equal_fused_layer(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    for rank, ok, exc in _run(world, "exact"):
         assert exc is None, (rank, exc)
         assert all(ok), (rank, ok)
 
