@@ -522,6 +522,10 @@ def kernel_case(name, reps=2):
             disp, tm, dw = ds_kernels.moe_dispatch(x, idx, w, off)
             for _ in range(reps):
                 ds_kernels.moe_combine(disp, tm, dw, T)
+    elif name == "swiglu":
+        g1 = torch.randn(16384 * K // 2, 2 * I, device=dev).to(torch.bfloat16)  # as op_report
+        for _ in range(reps):
+            ds_kernels.swiglu(g1)
     elif name in ("rms_norm", "rope", "kv_upproj"):
         M = 4 * 4096
         lat = torch.randn(M, 512, device=dev).to(torch.bfloat16)
@@ -557,7 +561,7 @@ def main():
                     help="expert-parallel transport for --gpus > 1")
     ap.add_argument("--op-report", default=None)
     ap.add_argument("--kernel-case", default=None,
-                    choices=["layer", "gemm1", "gemm2", "dispatch", "routing", "router", "combine",
+                    choices=["layer", "gemm1", "gemm2", "dispatch", "routing", "router", "combine", "swiglu",
                              "rms_norm", "rope", "kv_upproj"],
                     help="run one kernel at its BASELINE size twice (profiling) and exit")
     args = ap.parse_args()

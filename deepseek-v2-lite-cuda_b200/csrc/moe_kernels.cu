@@ -266,40 +266,53 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-// Exclusive scan of n ints, one CTA: each thread owns a contiguous chunk.
+// Exclusive scan of n ints, one CTA: tiles of 1024 x 16 items, each thread's 16 items held
+// in registers (all loads of a tile issued together), a block scan of the thread totals,
+// and a carry from tile to tile.
+constexpr int kScanItems = 16;
 __global__ void __launch_bounds__(1024)
     exclusive_scan_kernel(const int32_t* __restrict__ in, int n, int32_t* __restrict__ out) {
   __shared__ int warp_tot[32];
+  __shared__ int carry_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int chunk = (n + 1023) / 1024;
-  const int64_t b0 = min(static_cast<int64_t>(n), static_cast<int64_t>(tid) * chunk);
-  const int64_t b1 = min(static_cast<int64_t>(n), b0 + chunk);
-  int s = 0;
-  for (int64_t i = b0; i < b1; ++i) s += __ldg(in + i);
-  int incl = s;
+  int carry = 0;
+  for (int64_t tile = 0; tile < n; tile += 1024 * kScanItems) {
+    const int64_t b0 = tile + static_cast<int64_t>(tid) * kScanItems;
+    int v[kScanItems];
 #pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, d);
-    if (lane >= d) incl += v;
-  }
-  if (lane == 31) warp_tot[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    int w = warp_tot[lane];
+    for (int j = 0; j < kScanItems; ++j) v[j] = b0 + j < n ? __ldg(in + b0 + j) : 0;
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) s += v[j];
+    int incl = s;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, w, d);
-      if (lane >= d) w += v;
+      const int y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
     }
-    warp_tot[lane] = w;  // inclusive over warps
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_tot[lane];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, d);
+        if (lane >= d) w += y;
+      }
+      warp_tot[lane] = w;  // inclusive over warps
+      if (lane == 31) carry_s = carry + w;
+    }
+    __syncthreads();
+    int run = carry + (incl - s) + (warp > 0 ? warp_tot[warp - 1] : 0);
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+      if (b0 + j < n) out[b0 + j] = run;
+      run += v[j];
+    }
+    carry = carry_s;
+    __syncthreads();  // warp_tot and carry_s are reused by the next tile
   }
-  __syncthreads();
-  int run = (incl - s) + (warp > 0 ? warp_tot[warp - 1] : 0);
-  for (int64_t i = b0; i < b1; ++i) {
-    out[i] = run;
-    run += __ldg(in + i);
-  }
-  if (tid == 1023) out[n] = warp_tot[31];
+  if (tid == 0) out[n] = carry;
 }
 
 // K3: one warp per token; lanes j < K resolve the K destination slots, then the warp reads
@@ -446,20 +459,32 @@ __global__ void __launch_bounds__(256)
         }
       }
     }
-    for (int c = lane; c < H8; c += 32) {
-      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint4 v[K];
+    // two columns per lane per iteration: 2K + 2 row loads in flight
+    for (int c0 = lane; c0 < H8; c0 += 64) {
+      uint4 v[2][K], sh[2];
 #pragma unroll
-      for (int j = 0; j < K; ++j) {
-        if (s[j] == INT_MAX) continue;
-        const uint4* src = eo + static_cast<int64_t>(s[j]) * H8 + c;
-        v[j] = wait_flag != nullptr ? ld_cg16(src) : __ldg(src);
+      for (int h = 0; h < 2; ++h) {
+        const int c = c0 + 32 * h;
+        if (c >= H8) continue;
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+          if (s[j] == INT_MAX) continue;
+          const uint4* src = eo + static_cast<int64_t>(s[j]) * H8 + c;
+          v[h][j] = wait_flag != nullptr ? ld_cg16(src) : __ldg(src);
+        }
+        if (shared_out != nullptr) sh[h] = __ldg(shared_out + static_cast<int64_t>(t) * H8 + c);
       }
 #pragma unroll
-      for (int j = 0; j < K; ++j)
-        if (s[j] != INT_MAX) acc_bf16x8(a, v[j], ww[j]);
-      if (shared_out != nullptr) add_bf16x8(a, __ldg(shared_out + static_cast<int64_t>(t) * H8 + c));
-      out[static_cast<int64_t>(t) * H8 + c] = pack_bf16x8(a);
+      for (int h = 0; h < 2; ++h) {
+        const int c = c0 + 32 * h;
+        if (c >= H8) continue;
+        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < K; ++j)
+          if (s[j] != INT_MAX) acc_bf16x8(a, v[h][j], ww[j]);
+        if (shared_out != nullptr) add_bf16x8(a, sh[h]);
+        out[static_cast<int64_t>(t) * H8 + c] = pack_bf16x8(a);
+      }
     }
   }
 }
