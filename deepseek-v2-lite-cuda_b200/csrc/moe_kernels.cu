@@ -617,17 +617,19 @@ __global__ void __launch_bounds__(256)
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
-// K5: 16-byte vectors; each thread handles 8 gate and 8 up values of one row.
+// K5: 16-byte vectors; each thread handles 8 gate and 8 up values of one row.  Index math
+// in 32 bits when the item count allows it (a 64-bit division per 16-byte item costs more
+// issue slots than the item's memory traffic).
+template <typename Idx>
 __global__ void __launch_bounds__(256)
-    swiglu_vec_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, int64_t rows,
-                      int I8) {
-  const int64_t total = rows * I8;
-  for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < total;
-       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = v / I8;
-    const int c = static_cast<int>(v - r * I8);
-    const uint4 g = __ldg(in + r * 2 * I8 + c);
-    const uint4 u = __ldg(in + r * 2 * I8 + I8 + c);
+    swiglu_vec_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, Idx rows, Idx I8) {
+  const Idx total = rows * I8;
+  for (Idx v = blockIdx.x * static_cast<Idx>(blockDim.x) + threadIdx.x; v < total;
+       v += static_cast<Idx>(gridDim.x) * blockDim.x) {
+    const Idx r = v / I8;
+    const Idx c = v - r * I8;
+    const uint4 g = __ldg(in + static_cast<int64_t>(r) * 2 * I8 + c);
+    const uint4 u = __ldg(in + static_cast<int64_t>(r) * 2 * I8 + I8 + c);
     const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&g);
     const __nv_bfloat162* uh = reinterpret_cast<const __nv_bfloat162*>(&u);
     float o[8];
@@ -757,8 +759,13 @@ int launch_swiglu(const void* in, void* out, int64_t rows, int I, cudaStream_t s
   DS_TRY(device_info(&di));
   if ((I % 8) == 0 && aligned16(in) && aligned16(out)) {
     const int grid = grid_for(rows * (I / 8), 256, di.num_sms, 8);
-    swiglu_vec_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(in), static_cast<uint4*>(out),
-                                           rows, I / 8);
+    if (rows * (I / 8) < (int64_t{1} << 31))
+      swiglu_vec_kernel<uint32_t><<<grid, 256, 0, s>>>(
+          static_cast<const uint4*>(in), static_cast<uint4*>(out), static_cast<uint32_t>(rows),
+          static_cast<uint32_t>(I / 8));
+    else
+      swiglu_vec_kernel<int64_t><<<grid, 256, 0, s>>>(static_cast<const uint4*>(in),
+                                                      static_cast<uint4*>(out), rows, I / 8);
   } else {
     const int grid = grid_for(rows * (I / 2), 256, di.num_sms, 8);
     swiglu_pair_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat162*>(in),
