@@ -266,9 +266,10 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-// Exclusive scan of n ints, one CTA: tiles of 1024 x 16 items, each thread's 16 items held
-// in registers (all loads of a tile issued together), a block scan of the thread totals,
-// and a carry from tile to tile.
+// Exclusive scan of n ints, one CTA, in tiles of 1024 x 16 items: warp w owns 512
+// consecutive items of a tile and reads them as 16 coalesced 128-byte runs (run j = items
+// 32j..32j+31 of its segment), scans each run with shuffles carrying the running sum, then a
+// scan of the 32 warp totals and a carry from tile to tile.
 constexpr int kScanItems = 16;
 __global__ void __launch_bounds__(1024)
     exclusive_scan_kernel(const int32_t* __restrict__ in, int n, int32_t* __restrict__ out) {
@@ -277,20 +278,27 @@ __global__ void __launch_bounds__(1024)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int carry = 0;
   for (int64_t tile = 0; tile < n; tile += 1024 * kScanItems) {
-    const int64_t b0 = tile + static_cast<int64_t>(tid) * kScanItems;
+    const int64_t seg = tile + static_cast<int64_t>(warp) * 32 * kScanItems;
     int v[kScanItems];
 #pragma unroll
-    for (int j = 0; j < kScanItems; ++j) v[j] = b0 + j < n ? __ldg(in + b0 + j) : 0;
-    int s = 0;
-#pragma unroll
-    for (int j = 0; j < kScanItems; ++j) s += v[j];
-    int incl = s;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += y;
+    for (int j = 0; j < kScanItems; ++j) {
+      const int64_t i = seg + 32 * j + lane;
+      v[j] = i < n ? __ldg(in + i) : 0;
     }
-    if (lane == 31) warp_tot[warp] = incl;
+    int wrun = 0;  // this warp's running sum over its runs
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+      int incl = v[j];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += y;
+      }
+      const int x = v[j];
+      v[j] = wrun + incl - x;  // exclusive prefix within the warp's segment
+      wrun += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) warp_tot[warp] = wrun;
     __syncthreads();
     if (warp == 0) {
       int w = warp_tot[lane];
@@ -303,11 +311,11 @@ __global__ void __launch_bounds__(1024)
       if (lane == 31) carry_s = carry + w;
     }
     __syncthreads();
-    int run = carry + (incl - s) + (warp > 0 ? warp_tot[warp - 1] : 0);
+    const int base = carry + (warp > 0 ? warp_tot[warp - 1] : 0);
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) {
-      if (b0 + j < n) out[b0 + j] = run;
-      run += v[j];
+      const int64_t i = seg + 32 * j + lane;
+      if (i < n) out[i] = base + v[j];
     }
     carry = carry_s;
     __syncthreads();  // warp_tot and carry_s are reused by the next tile
@@ -512,7 +520,8 @@ __global__ void csr_fill_kernel(const int32_t* __restrict__ tm, int S, int T,
 __global__ void __launch_bounds__(256)
     combine_csr8_kernel(const uint4* __restrict__ eo, const int32_t* __restrict__ row_ptr,
                         const int32_t* __restrict__ csr, const float* __restrict__ dw,
-                        uint4* __restrict__ out, int T, int H8) {
+                        uint4* __restrict__ out, int T, int H8, int32_t* __restrict__ over_list,
+                        int32_t* __restrict__ over_count) {
   __shared__ int sl[8][8];
   __shared__ float sw[8][8];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -520,7 +529,10 @@ __global__ void __launch_bounds__(256)
   for (int t = blockIdx.x * (blockDim.x >> 5) + wid; t < T; t += warps) {
     const int beg = __ldg(row_ptr + t);
     const int n = __ldg(row_ptr + t + 1) - beg;
-    if (n > 8) continue;  // combine_csr_kernel
+    if (n > 8) {  // left to combine_csr_kernel through the overflow list
+      if (lane == 0) over_list[atomicAdd(over_count, 1)] = t;
+      continue;
+    }
     const int sv = lane < n ? __ldg(csr + beg + lane) : INT_MAX;
     int rank = 0;
     for (int q = 0; q < n; ++q) rank += (__shfl_sync(0xffffffffu, sv, q) < sv);
@@ -544,21 +556,23 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Tokens with more than 8 slots: one warp per token visits the slots in ascending order in
-// batches of up to 32 (rank sort when the segment fits one batch, repeated warp-min
+// Tokens with more than 8 slots (the overflow list combine_csr8_kernel leaves): one warp
+// per token visits the slots in ascending order in batches of up to 32 (rank sort when the segment fits one batch, repeated warp-min
 // selection otherwise), columns 1024 at a time with f32 accumulators.
 __global__ void __launch_bounds__(256)
     combine_csr_kernel(const uint4* __restrict__ eo, const int32_t* __restrict__ row_ptr,
                        const int32_t* __restrict__ csr, const float* __restrict__ dw,
-                       uint4* __restrict__ out, int T, int H8) {
+                       uint4* __restrict__ out, int H8, const int32_t* __restrict__ over_list,
+                       const int32_t* __restrict__ over_count) {
   __shared__ int sl[8][32];
   __shared__ float sw[8][32];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int warps = gridDim.x * (blockDim.x >> 5);
-  for (int t = blockIdx.x * (blockDim.x >> 5) + wid; t < T; t += warps) {
+  const int n_over = __ldg(over_count);
+  for (int i = blockIdx.x * (blockDim.x >> 5) + wid; i < n_over; i += warps) {
+    const int t = __ldg(over_list + i);
     const int beg = __ldg(row_ptr + t);
     const int n = __ldg(row_ptr + t + 1) - beg;
-    if (n <= 8) continue;  // combine_csr8_kernel
     for (int col0 = 0; col0 < H8; col0 += 128) {
       float a[4][8];
 #pragma unroll
@@ -852,7 +866,7 @@ size_t ds_moe_combine_workspace_size(int total_slots, int num_tokens) {
   ds::Carve c(nullptr, 0);
   c.take<int32_t>(static_cast<size_t>(num_tokens));      // counts
   c.take<int32_t>(static_cast<size_t>(num_tokens) + 1);  // row_ptr
-  c.take<int32_t>(static_cast<size_t>(num_tokens));      // cursor
+  c.take<int32_t>(static_cast<size_t>(num_tokens) + 1);  // cursor + overflow count
   c.take<int32_t>(static_cast<size_t>(total_slots));     // csr
   return ds::align_up(c.used, 256);
 }
@@ -872,14 +886,18 @@ int ds_moe_combine(const void* expert_output_bf16, const int32_t* token_map,
   ds::Carve c(workspace, workspace_bytes);
   int32_t* cnt = c.take<int32_t>(num_tokens);
   int32_t* row_ptr = c.take<int32_t>(static_cast<size_t>(num_tokens) + 1);
-  int32_t* cursor = c.take<int32_t>(num_tokens);
+  int32_t* cursor = c.take<int32_t>(static_cast<size_t>(num_tokens) + 1);
   int32_t* csr = c.take<int32_t>(total_slots > 0 ? total_slots : 1);
+  // tokens with more than 8 slots: a list in cnt (free once the scan has read it), its
+  // length in cursor[num_tokens] (zeroed with the cursors)
+  int32_t* over_list = cnt;
+  int32_t* over_count = cursor + num_tokens;
   if (!c.ok()) return fail(DS_ERR_WORKSPACE, "moe_combine: workspace needs %zu bytes", c.used);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   ds::DeviceInfo di;
   DS_TRY(ds::device_info(&di));
   DS_CUDA(cudaMemsetAsync(cnt, 0, sizeof(int32_t) * num_tokens, s));
-  DS_CUDA(cudaMemsetAsync(cursor, 0, sizeof(int32_t) * num_tokens, s));
+  DS_CUDA(cudaMemsetAsync(cursor, 0, sizeof(int32_t) * (static_cast<size_t>(num_tokens) + 1), s));
   if (total_slots > 0) {
     DS_REQUIRE(token_map && dispatched_weights, "moe_combine: null pointer");
     const int g = ds::grid_for(total_slots, 256, di.num_sms, 8);
@@ -897,12 +915,11 @@ int ds_moe_combine(const void* expert_output_bf16, const int32_t* token_map,
   ds::combine_csr8_kernel<<<g, 256, 0, s>>>(static_cast<const uint4*>(expert_output_bf16),
                                             row_ptr, csr, dispatched_weights,
                                             static_cast<uint4*>(final_output_bf16), num_tokens,
-                                            hidden_size / 8);
+                                            hidden_size / 8, over_list, over_count);
   DS_LAUNCH_CHECK("combine_csr8_kernel");
-  ds::combine_csr_kernel<<<g, 256, 0, s>>>(static_cast<const uint4*>(expert_output_bf16),
-                                           row_ptr, csr, dispatched_weights,
-                                           static_cast<uint4*>(final_output_bf16), num_tokens,
-                                           hidden_size / 8);
+  ds::combine_csr_kernel<<<di.num_sms, 256, 0, s>>>(
+      static_cast<const uint4*>(expert_output_bf16), row_ptr, csr, dispatched_weights,
+      static_cast<uint4*>(final_output_bf16), hidden_size / 8, over_list, over_count);
   DS_LAUNCH_CHECK("combine_csr_kernel");
   return DS_OK;
 }

@@ -99,7 +99,7 @@ def test_scan_known_answers(golden_dir):
 
 def test_scan_large_and_random():
     g = torch.Generator().manual_seed(3)
-    for n in (2, 63, 64, 65, 1000, 1024, 1025, 5000):
+    for n in (2, 63, 64, 65, 1000, 1024, 1025, 5000, 16383, 16384, 16385, 40000):
         c = torch.randint(0, 1000, (n,), generator=g, dtype=torch.int32)
         out = ds().moe_scan(c.cuda())
         assert torch.equal(out.cpu(), oracle.expert_offsets(c)), n
@@ -197,6 +197,28 @@ def test_combine_heavy_token_and_empty_tokens():
     tm[::10] = 3
     dw = torch.rand(S, generator=g) / 50
     _check_combine(eo, tm, dw, T, 2e-2)
+
+
+def test_combine_many_long_segments():
+    # every token has 9-40 slots: all of them go through the overflow list to the batched
+    # long-segment kernel
+    g = torch.Generator().manual_seed(7)
+    T, S = 300, 7000
+    eo = torch.randn(S, H, generator=g).to(torch.bfloat16)
+    tm = torch.randint(0, T, (S,), generator=g, dtype=torch.int32)
+    dw = torch.rand(S, generator=g) / 20
+    _check_combine(eo, tm, dw, T, 2e-2)
+
+
+def test_combine_more_tokens_than_one_scan_tile():
+    # T > 16384: the single-CTA scan of the per-token counts carries over several tiles
+    g = torch.Generator().manual_seed(8)
+    T = 20000
+    S = T + 3000
+    eo = torch.randn(S, H, generator=g).to(torch.bfloat16)
+    tm = torch.cat([torch.arange(T, dtype=torch.int32),
+                    torch.randint(0, T, (S - T,), generator=g, dtype=torch.int32)])
+    _check_combine(eo, tm, torch.rand(S, generator=g), T, 2e-2)
 
 
 def test_combine_known_answer(golden_dir):
