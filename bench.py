@@ -390,35 +390,58 @@ def run_ours(args, rank, world, local_rank):
         op_report(args.op_report, dev)
 
 
-def _time(fn, iters=20, warm=3, reps=5):
-    """Device seconds per call: `iters` calls captured in one CUDA graph (so host launch
-    overhead is not measured), replayed `reps` times between CUDA events."""
+L2_BYTES = 126 * 2 ** 20
+
+
+def _copies(nbytes):
+    """Input sets to rotate through so that consecutive calls touch more than twice the L2:
+    no call finds its operands (or its predecessor's outputs) in L2."""
+    return max(1, -(-2 * L2_BYTES // int(nbytes)))
+
+
+def _time(fns, iters=20, warm=3, reps=10):
+    """Device time per call: `iters` calls cycling through `fns` (one per input copy),
+    captured in one CUDA graph (host launch overhead is not measured) with every output kept
+    alive (each call writes fresh memory), replayed `reps` times, each replay between CUDA
+    events.  Returns (median, p95) seconds per call over the replays."""
+    if callable(fns):
+        fns = [fns]
+    n = len(fns)
+    iters = max(iters, n)
+    iters = -(-iters // n) * n
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        for _ in range(warm):
-            fn()
+        for i in range(max(warm, n)):
+            fns[i % n]()
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
+    keep = []
     with torch.cuda.graph(g):
-        for _ in range(iters):
-            fn()
+        for i in range(iters):
+            keep.append(fns[i % n]())
     g.replay()
     torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
+    times = []
     for _ in range(reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
         g.replay()
-    b.record()
-    torch.cuda.synchronize()
-    return a.elapsed_time(b) / (iters * reps) / 1000.0
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) / iters / 1000.0)
+    del keep, g
+    torch.cuda.empty_cache()
+    times.sort()
+    return times[len(times) // 2], times[min(len(times) - 1, int(0.95 * len(times)))]
 
 
 def op_report(path, dev):
-    """Per-op device timings (CUDA-graph replay) and roofline fractions of the bandwidth
-    kernels at their BASELINE sizes (configs 1 and 3), appended as JSON lines to `path`."""
+    """Per-op device timings (CUDA-graph replay, median and p95 over >= 200 calls, inputs
+    rotated so no call hits L2) and roofline fractions of the bandwidth kernels at their
+    BASELINE sizes (configs 1 and 3), appended as JSON lines to `path`."""
     import ds_kernels
     import synthetic
     pk = peaks()
@@ -429,38 +452,53 @@ def op_report(path, dev):
     x = torch.randn(T, H, device=dev).to(torch.bfloat16)
     idx, w, counts = ds_kernels.moe_routing(logits, K)
     off = ds_kernels.moe_scan(counts)
-    t = _time(lambda: ds_kernels.moe_routing(logits, K))
-    out.append(("moe_routing cfg1", 4 * T * E + 8 * T * K + 4 * E, t))
-    t = _time(lambda: ds_kernels.moe_dispatch(x, idx, w, off))
-    out.append(("moe_dispatch cfg1", 2 * T * H + 2 * S * H + 16 * S, t))
+    nb = 4 * T * E + 8 * T * K + 4 * E
+    lg = [logits.clone() for _ in range(_copies(nb))]
+    out.append(("moe_routing cfg1", nb, _time([lambda l=l: ds_kernels.moe_routing(l, K) for l in lg])))
+    del lg
+    nb = 2 * T * H + 2 * S * H + 16 * S
+    out.append(("moe_dispatch cfg1", nb, _time(lambda: ds_kernels.moe_dispatch(x, idx, w, off))))
     disp, tm, dw = ds_kernels.moe_dispatch(x, idx, w, off)
     eo = torch.randn(S, H, device=dev).to(torch.bfloat16)
-    t = _time(lambda: ds_kernels.moe_combine(eo, tm, dw, T))
-    out.append(("moe_combine cfg1", 2 * S * H + 2 * T * H + 8 * S, t))
+    out.append(("moe_combine cfg1", 2 * S * H + 2 * T * H + 8 * S,
+                _time(lambda: ds_kernels.moe_combine(eo, tm, dw, T))))
+    del disp, eo
     g1 = torch.randn(T * K // 2, 2 * I, device=dev).to(torch.bfloat16)
-    t = _time(lambda: ds_kernels.swiglu(g1))
-    out.append(("swiglu [S/2, 2816]", g1.numel() * 2 + g1.numel(), t))
+    out.append(("swiglu [S/2, 2816]", g1.numel() * 2 + g1.numel(), _time(lambda: ds_kernels.swiglu(g1))))
+    del g1
     M = 4 * 4096
     lat = torch.randn(M, 512, device=dev).to(torch.bfloat16)
     wn = torch.rand(512, device=dev) + 0.5
-    t = _time(lambda: ds_kernels.rms_norm(lat, wn))
-    out.append(("rms_norm cfg3", 4 * M * 512, t))
+    nb = 4 * M * 512
+    lats = [lat.clone() for _ in range(_copies(nb))]
+    out.append(("rms_norm cfg3", nb, _time([lambda l=l: ds_kernels.rms_norm(l, wn) for l in lats])))
+    del lats
     q = torch.randn(4, 16, 4096, 64, device=dev).to(torch.bfloat16)
     k = torch.randn(4, 1, 4096, 64, device=dev).to(torch.bfloat16)
     cs = torch.randn(4, 1, 4096, 64, device=dev).to(torch.bfloat16)
-    t = _time(lambda: ds_kernels.rope(q, k, cs, cs))
-    out.append(("rope cfg3", 4 * (q.numel() + k.numel()) + 4 * cs.numel(), t))
+    nb = 4 * (q.numel() + k.numel()) + 4 * cs.numel()
+    sets = [(q.clone(), k.clone(), cs.clone(), cs.clone()) for _ in range(_copies(nb))]
+    out.append(("rope cfg3", nb, _time([lambda t=t: ds_kernels.rope(*t) for t in sets])))
+    del sets
+    # calibration: a plain device copy (read + write) of the same byte counts, same harness
+    for label, nbt in (("device copy, rms_norm cfg3 bytes", 4 * M * 512),
+                       ("device copy, rope cfg3 bytes", nb)):
+        srcs = [torch.empty(nbt // 4, dtype=torch.bfloat16, device=dev) for _ in range(_copies(nbt))]
+        out.append((label, nbt, _time([lambda x=x: x.clone() for x in srcs])))
+        del srcs
     wkv = (torch.randn(4096, 512, device=dev) * 0.02).to(torch.bfloat16)
-    t = _time(lambda: ds_kernels.kv_upproj(lat, wkv))
+    tk = _time(lambda: ds_kernels.kv_upproj(lat, wkv))
     with open(path, "a") as f:
-        for name, nbytes, sec in out:
+        for name, nbytes, (sec, p95) in out:
             gbs = nbytes / sec / 1e9
             f.write(json.dumps({"op": name, "bytes": nbytes, "us": round(sec * 1e6, 2),
-                                "GB/s": round(gbs, 1), "frac_hbm": round(gbs / pk["hbm_gbs"], 3)}) + "\n")
+                                "us_p95": round(p95 * 1e6, 2), "GB/s": round(gbs, 1),
+                                "frac_hbm": round(gbs / pk["hbm_gbs"], 3)}) + "\n")
         fl = 2.0 * M * 512 * 4096
-        f.write(json.dumps({"op": "kv_upproj cfg3", "flops": fl, "us": round(t * 1e6, 2),
-                            "TFLOP/s": round(fl / t / 1e12, 1),
-                            "frac_bf16": round(fl / t / 1e12 / pk["bf16"], 3)}) + "\n")
+        f.write(json.dumps({"op": "kv_upproj cfg3", "flops": fl, "us": round(tk[0] * 1e6, 2),
+                            "us_p95": round(tk[1] * 1e6, 2),
+                            "TFLOP/s": round(fl / tk[0] / 1e12, 1),
+                            "frac_bf16": round(fl / tk[0] / 1e12 / pk["bf16"], 3)}) + "\n")
 
 
 def kernel_case(name, reps=2):

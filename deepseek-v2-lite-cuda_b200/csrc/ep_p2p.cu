@@ -74,7 +74,7 @@ __device__ __forceinline__ int* flag_at(char* const base, size_t flags_off, int 
 
 // Plan + count exchange.  One CTA of 1024 threads = 16 partitions of the routing blocks x 64
 // experts (the local part is the single-GPU plan).
-__global__ void __launch_bounds__(1024)
+__global__ void __launch_bounds__(1024, 1)
     ep_plan_kernel(const int32_t* __restrict__ hist, int nblk, int E, int El, int rank,
                    int world, const __grid_constant__ PeerTable peers, size_t flags_off,
                    size_t counts_off, int target,
@@ -91,9 +91,22 @@ __global__ void __launch_bounds__(1024)
   const int p = threadIdx.x / kMaxExperts;
   const int chunk = (nblk + P - 1) / P;
   const int b0 = min(nblk, p * chunk), b1 = min(nblk, b0 + chunk);
+  // up to kPlanRegs histogram entries per thread stay in registers, loads issued together
+  constexpr int kPlanRegs = 16;
+  const bool in_regs = chunk <= kPlanRegs;
+  int hv[kPlanRegs];
   int s = 0;
-  if (e < E)
-    for (int b = b0; b < b1; ++b) s += __ldg(hist + static_cast<int64_t>(b) * E + e);
+  if (e < E) {
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < kPlanRegs; ++j)
+        hv[j] = b0 + j < b1 ? __ldg(hist + static_cast<int64_t>(b0 + j) * E + e) : 0;
+#pragma unroll
+      for (int j = 0; j < kPlanRegs; ++j) s += hv[j];
+    } else {
+      for (int b = b0; b < b1; ++b) s += __ldg(hist + static_cast<int64_t>(b) * E + e);
+    }
+  }
   part[p][e] = s;
   __syncthreads();
   if (threadIdx.x < E) {
@@ -117,9 +130,17 @@ __global__ void __launch_bounds__(1024)
   if (threadIdx.x <= E) offsets[threadIdx.x] = off[threadIdx.x];
   if (e < E) {
     int run = off[e] + pbase[p][e];
-    for (int b = b0; b < b1; ++b) {
-      blk_base[static_cast<int64_t>(b) * E + e] = run;
-      run += __ldg(hist + static_cast<int64_t>(b) * E + e);
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < kPlanRegs; ++j) {
+        if (b0 + j < b1) blk_base[static_cast<int64_t>(b0 + j) * E + e] = run;
+        run += hv[j];
+      }
+    } else {
+      for (int b = b0; b < b1; ++b) {
+        blk_base[static_cast<int64_t>(b) * E + e] = run;
+        run += __ldg(hist + static_cast<int64_t>(b) * E + e);
+      }
     }
   }
   // ---- count exchange: row `rank` of every rank's matrix, then one release per rank

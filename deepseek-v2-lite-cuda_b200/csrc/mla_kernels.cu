@@ -4,10 +4,131 @@
 // RMSNorm follows src/reference/mla.py:59-64 (f32 statistics) with the single rounding of
 // src/kernels/mla/rms_norm.cu:104-114; RoPE implements the interleave->half rotation of
 // src/reference/mla.py:183-206 in the per-element form of src/kernels/mla/rope.cu:23-26.
+#include <mutex>
+
 #include "kernels.cuh"
+#include "ptx.cuh"
 
 namespace ds {
 namespace {
+
+// Contiguous rows of at most 512 elements (the 512-d kv latent): a pipelined ring.  Each CTA
+// walks tiles of kNormTileRows rows; thread 0 keeps kNormStages tiles in flight with one bulk
+// copy each (global -> shared, no registers spent on the bytes in flight) while the 8 warps
+// normalise the oldest tile from shared memory (2 rows per warp, f32 statistics, weights held
+// in registers) and write it with 16-byte stores; the stage is refilled once every warp has
+// read it.  DRAM latency is paid once per CTA, not once per tile.  Every wait is bounded: on
+// expiry the CTA records DS_ERR_TIMEOUT, waits (bounded) for its copies in flight, returns.
+constexpr int kNormTileRows = 16;
+constexpr int kNormStages = 4;
+__global__ void __launch_bounds__(256)
+    rms_norm_ring_kernel(const __nv_bfloat16* __restrict__ in, const float4* __restrict__ weight,
+                         uint4* __restrict__ out, int rows, int H, float eps, int* status,
+                         long long timeout_cycles) {
+  extern __shared__ __align__(128) uint8_t ring[];  // kNormStages x kNormTileRows x H bf16
+  __shared__ __align__(8) uint64_t bars[kNormStages];
+  __shared__ int abort_flag;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ntiles = (rows + kNormTileRows - 1) / kNormTileRows;
+  const int mine = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const uint32_t stage_bytes = static_cast<uint32_t>(kNormTileRows) * H * 2;
+  const uint32_t ring0 = ptx::smem_u32(ring);
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int st = 0; st < kNormStages; ++st) ptx::mbar_init(ptx::smem_u32(&bars[st]), 1);
+    ptx::fence_barrier_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i) {  // thread 0: the CTA's i-th tile into stage i % kNormStages
+    const int tile = blockIdx.x + i * gridDim.x;
+    const int r0 = tile * kNormTileRows;
+    const uint32_t bytes = static_cast<uint32_t>(min(kNormTileRows, rows - r0)) * H * 2;
+    const uint32_t bar = ptx::smem_u32(&bars[i % kNormStages]);
+    ptx::mbar_arrive_expect_tx(bar, bytes);
+    ptx::bulk_load_1d(ring0 + (i % kNormStages) * stage_bytes, in + static_cast<int64_t>(r0) * H,
+                      bytes, bar);
+  };
+  int issued = 0;
+  if (threadIdx.x == 0)
+    for (; issued < min(mine, kNormStages); ++issued) issue(issued);
+  const int H8 = H >> 3;
+  float wv[2][8];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int c = u * 32 + lane;
+    if (c < H8) {
+      const float4 w0 = __ldg(weight + 2 * c), w1 = __ldg(weight + 2 * c + 1);
+      wv[u][0] = w0.x; wv[u][1] = w0.y; wv[u][2] = w0.z; wv[u][3] = w0.w;
+      wv[u][4] = w1.x; wv[u][5] = w1.y; wv[u][6] = w1.z; wv[u][7] = w1.w;
+    }
+  }
+  const float inv_h = 1.f / static_cast<float>(H);
+  int done = 0;
+  for (; done < mine; ++done) {
+    const int st = done % kNormStages;
+    if (!ptx::mbar_wait(ptx::smem_u32(&bars[st]), (done / kNormStages) & 1, &abort_flag, status,
+                        timeout_cycles, DS_ERR_TIMEOUT))
+      break;
+    const int r0 = (blockIdx.x + done * gridDim.x) * kNormTileRows;
+    const int nrows = min(kNormTileRows, rows - r0);
+    const uint4* t4 = reinterpret_cast<const uint4*>(ring + st * stage_bytes);
+    uint4 v[2][2];
+    float ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int r = warp * 2 + j;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = u * 32 + lane;
+        if (r < nrows && c < H8) {
+          v[j][u] = t4[r * H8 + c];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j][u]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h[i]);
+            ss[j] = fmaf(f.x, f.x, ss[j]);
+            ss[j] = fmaf(f.y, f.y, ss[j]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], d);
+      ss[1] += __shfl_xor_sync(0xffffffffu, ss[1], d);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int r = warp * 2 + j;
+      if (r >= nrows) continue;
+      const float scale = rsqrtf(ss[j] * inv_h + eps);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = u * 32 + lane;
+        if (c >= H8) continue;
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j][u]);
+        uint4 o;
+        uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          const __nv_bfloat162 bb =
+              __floats2bfloat162_rn(f.x * scale * wv[u][2 * i], f.y * scale * wv[u][2 * i + 1]);
+          ou[i] = *reinterpret_cast<const uint32_t*>(&bb);
+        }
+        out[static_cast<int64_t>(r0 + r) * H8 + c] = o;
+      }
+    }
+    __syncthreads();  // every warp has read the stage: refill it
+    if (threadIdx.x == 0 && issued < mine) issue(issued++);
+  }
+  if (done < mine && threadIdx.x == 0) {  // aborted: let the copies still in flight land
+    int never = 0;
+    for (int i = done; i < issued; ++i)
+      ptx::mbar_wait(ptx::smem_u32(&bars[i % kNormStages]), (i / kNormStages) & 1, &never,
+                     status, timeout_cycles, DS_ERR_TIMEOUT);
+  }
+}
 
 // Rows of at most 512 elements (the 512-d kv latent): one warp takes two rows at a time and
 // issues all four 16-byte loads per lane before the reductions, so twice the bytes are in
@@ -242,7 +363,7 @@ __device__ __forceinline__ uint4 f32x8_to_bf16(const float (&f)[8]) {
 // pairs k = 8c..8c+7 need cos/sin[k] and cos/sin[half + k] (one 16-byte load each), loaded
 // once per thread for 4 rows instead of once per row; the 4 rows' loads are issued together.
 constexpr int kRopeRows = 4;
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
     rope_heads_kernel(const uint4* __restrict__ q, const uint4* __restrict__ k,
                       const uint4* __restrict__ cos_t, const uint4* __restrict__ sin_t,
                       uint4* __restrict__ qo, uint4* __restrict__ ko, int64_t bs_rows,
@@ -258,11 +379,9 @@ __global__ void __launch_bounds__(256)
     const int64_t bs = t % bs_rows;  // b * seq + s
     const int g = static_cast<int>(t / bs_rows);
     const int64_t b = bs / seq, sp = bs - b * seq;
-    float cl[8], ch[8], sl[8], sh[8];
-    bf16x8_to_f32(__ldg(cos_t + bs * D8 + c), cl);
-    bf16x8_to_f32(__ldg(cos_t + bs * D8 + H8 + c), ch);
-    bf16x8_to_f32(__ldg(sin_t + bs * D8 + c), sl);
-    bf16x8_to_f32(__ldg(sin_t + bs * D8 + H8 + c), sh);
+    // the chunk's cos/sin stay packed (16 registers) and are widened per row
+    const uint4 cl4 = __ldg(cos_t + bs * D8 + c), ch4 = __ldg(cos_t + bs * D8 + H8 + c);
+    const uint4 sl4 = __ldg(sin_t + bs * D8 + c), sh4 = __ldg(sin_t + bs * D8 + H8 + c);
     uint4 xv[kRopeRows][2];
     int64_t rows[kRopeRows];
 #pragma unroll
@@ -278,9 +397,13 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < kRopeRows; ++j) {
       if (rows[j] < 0) continue;
-      float x0[8], x1[8];
+      float x0[8], x1[8], cl[8], ch[8], sl[8], sh[8];
       bf16x8_to_f32(xv[j][0], x0);
       bf16x8_to_f32(xv[j][1], x1);
+      bf16x8_to_f32(cl4, cl);
+      bf16x8_to_f32(ch4, ch);
+      bf16x8_to_f32(sl4, sl);
+      bf16x8_to_f32(sh4, sh);
       float lo[8], hi[8];
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
@@ -324,6 +447,19 @@ __global__ void rope_pair_kernel(const __nv_bfloat16* __restrict__ q,
   }
 }
 
+// Opt a kernel into `bytes` of dynamic shared memory once per device (above 48 KB).
+int smem_opt_in(const void* fn, int slot, int bytes, int device) {
+  static std::mutex mu;
+  static int done[1][64] = {};
+  if (device < 0 || device >= 64) return fail(DS_ERR_UNSUPPORTED, "device ordinal %d", device);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[slot][device] < bytes) {
+    DS_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[slot][device] = bytes;
+  }
+  return DS_OK;
+}
+
 int grid_cap(int64_t items, int per_block, int num_sms) {
   const int64_t need = (items + per_block - 1) / per_block;
   const int64_t cap = static_cast<int64_t>(num_sms) * 8;
@@ -352,6 +488,21 @@ int ds_rms_norm_strided(const void* input_bf16, int64_t in_stride, const float* 
                       ds::aligned16(weight))
                          ? 1
                          : 0;
+  if (vec_ok && hidden_size <= 512 && in_stride == hidden_size && out_stride == hidden_size) {
+    int* status = ds::device_status_ptr();
+    if (status == nullptr) return ds::fail(DS_ERR_CUDA, "device status word unavailable");
+    const int ntiles = (rows + ds::kNormTileRows - 1) / ds::kNormTileRows;
+    const int grid = ntiles < 2 * di.num_sms ? ntiles : 2 * di.num_sms;
+    const int smem = ds::kNormStages * ds::kNormTileRows * hidden_size * 2;
+    DS_TRY(ds::smem_opt_in(reinterpret_cast<const void*>(ds::rms_norm_ring_kernel), 0, smem,
+                           di.device));
+    ds::rms_norm_ring_kernel<<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16*>(input_bf16), reinterpret_cast<const float4*>(weight),
+        static_cast<uint4*>(output_bf16), rows, hidden_size, eps, status,
+        2000LL * di.clock_khz);
+    DS_LAUNCH_CHECK("rms_norm_ring_kernel");
+    return DS_OK;
+  }
   if (vec_ok && hidden_size <= 512) {
     const int grid = ds::grid_cap((static_cast<int64_t>(rows) + 1) / 2, 8, di.num_sms);
     ds::rms_norm_pair_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(

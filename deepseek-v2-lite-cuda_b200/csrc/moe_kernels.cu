@@ -228,9 +228,23 @@ __global__ void __launch_bounds__(1024)
   const int p = threadIdx.x / kMaxExperts;
   const int chunk = (nblk + P - 1) / P;
   const int b0 = min(nblk, p * chunk), b1 = min(nblk, b0 + chunk);
+  // up to kPlanRegs histogram entries per thread (T <= 16 * 64 * kPlanRegs tokens) stay in
+  // registers, their loads issued together; longer chunks are summed by a loop
+  constexpr int kPlanRegs = 16;
+  const bool in_regs = chunk <= kPlanRegs;
+  int hv[kPlanRegs];
   int s = 0;
-  if (e < E)
-    for (int b = b0; b < b1; ++b) s += __ldg(hist + static_cast<int64_t>(b) * E + e);
+  if (e < E) {
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < kPlanRegs; ++j)
+        hv[j] = b0 + j < b1 ? __ldg(hist + static_cast<int64_t>(b0 + j) * E + e) : 0;
+#pragma unroll
+      for (int j = 0; j < kPlanRegs; ++j) s += hv[j];
+    } else {
+      for (int b = b0; b < b1; ++b) s += __ldg(hist + static_cast<int64_t>(b) * E + e);
+    }
+  }
   part[p][e] = s;
   __syncthreads();
   if (threadIdx.x < E) {
@@ -259,9 +273,17 @@ __global__ void __launch_bounds__(1024)
   if (offsets != nullptr && threadIdx.x <= E) offsets[threadIdx.x] = off[threadIdx.x];
   if (blk_base != nullptr && e < E) {
     int run = off[e] + pbase[p][e];
-    for (int b = b0; b < b1; ++b) {
-      blk_base[static_cast<int64_t>(b) * E + e] = run;
-      run += __ldg(hist + static_cast<int64_t>(b) * E + e);
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < kPlanRegs; ++j) {
+        if (b0 + j < b1) blk_base[static_cast<int64_t>(b0 + j) * E + e] = run;
+        run += hv[j];
+      }
+    } else {
+      for (int b = b0; b < b1; ++b) {
+        blk_base[static_cast<int64_t>(b) * E + e] = run;
+        run += __ldg(hist + static_cast<int64_t>(b) * E + e);
+      }
     }
   }
 }

@@ -76,6 +76,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// 1-D bulk copy global -> shared (no tensor map): `bytes` a multiple of 16, both addresses
+// 16-byte aligned; completion counted on `bar` (complete_tx).
+__device__ __forceinline__ void bulk_load_1d(uint32_t dst, const void* src, uint32_t bytes,
+                                             uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // 2-D tiled bulk-tensor store shared -> global (bulk-group completion).  x = innermost
 // coordinate (elements, a multiple of 16 bytes), y = row; both non-negative.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int x, int y) {

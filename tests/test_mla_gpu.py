@@ -67,7 +67,8 @@ def _rope_inputs(bsz, seq, heads=16, seed=0, scaling=40.0):
 
 
 @pytest.mark.parametrize("bsz,seq,heads,scaling", [(1, 16, 16, 40.0), (2, 64, 16, 40.0),
-                                                   (1, 32, 16, 1.0), (3, 7, 4, 40.0)])
+                                                   (1, 32, 16, 1.0), (3, 7, 4, 40.0),
+                                                   (2, 100, 16, 40.0), (1, 20, 40, 1.0)])
 def test_rope(bsz, seq, heads, scaling):
     q, k, c, s = _rope_inputs(bsz, seq, heads, seed=seq, scaling=scaling)
     qr, kr = ds().rope(q.cuda(), k.cuda(), c.cuda(), s.cuda())
