@@ -10,11 +10,17 @@
 //   warp 1       MMA issuer: tcgen05.mma kind::f16, M=128 N=256 K=16, f32 accumulator in
 //                TMEM, two accumulator buffers (2 x 256 columns) so the epilogue of tile i
 //                overlaps the MMAs of tile i+1.
-//   warps 2-5    epilogue: tcgen05.ld 32x32b -> registers -> bf16 (optionally SwiGLU) ->
-//                global, one accumulator row per thread, rows masked at the group end.
-// Tiles are enumerated m-tile-major over a per-group tile prefix that every CTA builds
-// from the device-side group offsets (no host synchronisation); CTA c takes tiles
-// c, c + gridDim.x, ...  Every mbarrier wait is bounded (ptx::mbar_wait).
+//   warps 2-5    epilogue: tcgen05.ld 32x32b -> registers (one accumulator row per thread)
+//                -> bf16 (optionally SwiGLU) -> a 32-row x 64-column slab in shared memory
+//                -> one TMA bulk-tensor store (contiguous output rows), or a warp-wide
+//                copy-out of whole 128-byte row segments (mapped rows, another GPU's
+//                memory); rows past the group end go row by row, masked.
+// Up to two problems per launch (e.g. routed experts + shared expert).  Tiles are
+// enumerated m-tile-major over a per-group tile prefix that every CTA builds from the
+// device-side group offsets (no host synchronisation); CTA c takes tiles c, c + gridDim.x,
+// ...  Cross-GPU hooks: a problem may wait (bounded) on a flag another GPU raises before its
+// first tile, and a launch may raise flags on other GPUs when it completes.  Every wait is
+// bounded (ptx::mbar_wait, ptx::wait_flag_ge).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

@@ -3,7 +3,9 @@
 Same function names, argument names, defaults and return conventions as the reference
 binding (src/kernels/bindings.cu:186-301): `moe_routing`, `moe_scan`, `moe_dispatch`,
 `moe_combine`, `swiglu`, `moe_gemm1`, `moe_gemm2`, `rms_norm`, `kv_upproj`, `rope`,
-`run_hello`; plus the additive ops `moe_gemm1_swiglu` and `moe_layer_forward`.
+`run_hello`; plus the additive ops `moe_gemm1_swiglu`, `moe_layer_fused` /
+`moe_layer_forward` / `moe_layer_forward_from_x`, the layer stages and the expert-parallel
+entry points.
 
 Every op validates its tensors with the reference's messages (raising RuntimeError, as
 TORCH_CHECK does), allocates outputs with torch on the input's device, and calls the
@@ -721,6 +723,20 @@ def moe_layer_forward_from_x(x: torch.Tensor, router_w_split: torch.Tensor, num_
             _ptr(shared_w1), _ptr(shared_w2), _ptr(out), T, H, E, top_k, I, Is, _ptr(workspace),
             workspace.numel(), ev, _stream(x)), "moe_layer_forward_from_x")
     return out
+
+
+def moe_layer_fused(hidden_states: torch.Tensor, gate_weight: torch.Tensor,
+                    packed_w1: torch.Tensor, w2: torch.Tensor,
+                    shared_w1: Optional[torch.Tensor] = None,
+                    shared_w2: Optional[torch.Tensor] = None, top_k: int = 6) -> torch.Tensor:
+    """The whole MoE layer in one call from the router's gate weight (any float dtype,
+    [E, H]): the additive op of this surface for callers that hold the gate as a tensor.  It
+    splits the gate for the tensor-core router on every call; callers that run the layer
+    repeatedly keep the split (`router_weight_split`) and call `moe_layer_forward_from_x`,
+    as `moe_fused.FusedMoELayer` does."""
+    split = router_weight_split(gate_weight.float().contiguous())
+    return moe_layer_forward_from_x(hidden_states, split, gate_weight.shape[0], packed_w1, w2,
+                                    shared_w1, shared_w2, top_k=top_k)
 
 
 def dense_gemm1_swiglu(x: torch.Tensor, w1: torch.Tensor, max_ctas: int = 0) -> torch.Tensor:

@@ -129,6 +129,19 @@ def test_layer_from_x(T):
     torch.testing.assert_close(logits.cpu(), x.float() @ W.gate.t(), atol=1e-4, rtol=1e-4)
 
 
+def test_moe_layer_fused_equals_from_x():
+    import ds_kernels
+    W = weights(0, 2)
+    D = device_weights(W)
+    g = torch.Generator().manual_seed(901)
+    x = torch.randn(333, H, generator=g).to(torch.bfloat16).cuda()
+    a = ds_kernels.moe_layer_fused(x, D["gate"], D["w1"], D["w2"], D["sw1"], D["sw2"], top_k=K)
+    split = ds_kernels.router_weight_split(D["gate"])
+    b = ds_kernels.moe_layer_forward_from_x(x, split, E, D["w1"], D["w2"], D["sw1"], D["sw2"],
+                                            top_k=K)
+    assert torch.equal(a, b)
+
+
 def test_cfg2_full_size_from_x():
     W = weights(1, 2)
     D = device_weights(W)
