@@ -345,8 +345,34 @@ __global__ void __launch_bounds__(1024)
   if (tid == 0) out[n] = carry;
 }
 
-// K3: one warp per token; lanes j < K resolve the K destination slots, then the warp reads
-// the token row once (16-byte loads) and writes it to every destination.
+// K3: one warp per pair of tokens (t, t + warps): the warp issues both token rows' 16-byte
+// loads first (for H <= 2048 a row is 8 loads per lane), then lanes j < K resolve each
+// token's K destination slots, and the warp writes each row to every destination.
+template <int K>
+__device__ __forceinline__ int scatter_slot(int t, int lane, int E, const int32_t* __restrict__ idx,
+                                            const float* __restrict__ w,
+                                            const int32_t* __restrict__ blk_base,
+                                            const int32_t* __restrict__ local_rank,
+                                            int32_t* __restrict__ token_map, float* __restrict__ dw,
+                                            int32_t* __restrict__ slot_of, int S) {
+  int my_slot = -1;
+  if (lane < K) {
+    const int64_t tk = static_cast<int64_t>(t) * K + lane;
+    const int e = __ldg(idx + tk);
+    if (e >= 0 && e < E) {
+      const int s = __ldg(blk_base + static_cast<int64_t>(t / kRouteTokens) * E + e) +
+                    __ldg(local_rank + tk);
+      if (s >= 0 && s < S) my_slot = s;
+    }
+    if (my_slot >= 0) {
+      token_map[my_slot] = t;
+      if (dw != nullptr) dw[my_slot] = __ldg(w + tk);
+    }
+    if (slot_of != nullptr) slot_of[tk] = my_slot;
+  }
+  return my_slot;
+}
+
 template <int K>
 __global__ void __launch_bounds__(256)
     scatter_kernel(const uint4* __restrict__ x, int T, int H8, int E,
@@ -356,41 +382,65 @@ __global__ void __launch_bounds__(256)
                    float* __restrict__ dw, int32_t* __restrict__ slot_of, int S) {
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
-  for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
-    int my_slot = -1;
-    if (lane < K) {
-      const int64_t tk = static_cast<int64_t>(t) * K + lane;
-      const int e = __ldg(idx + tk);
-      if (e >= 0 && e < E) {
-        const int s = __ldg(blk_base + static_cast<int64_t>(t / kRouteTokens) * E + e) +
-                      __ldg(local_rank + tk);
-        if (s >= 0 && s < S) my_slot = s;
-      }
-      if (my_slot >= 0) {
-        token_map[my_slot] = t;
-        if (dw != nullptr) dw[my_slot] = __ldg(w + tk);
-      }
-      if (slot_of != nullptr) slot_of[tk] = my_slot;
-    }
-    int slots[K];
-#pragma unroll
-    for (int j = 0; j < K; ++j) slots[j] = __shfl_sync(0xffffffffu, my_slot, j);
-    const uint4* src = x + static_cast<int64_t>(t) * H8;
+  for (int t0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t0 < T; t0 += 2 * warps) {
+    const int t1 = t0 + warps;
+    const bool has1 = t1 < T;
+    const uint4* src0 = x + static_cast<int64_t>(t0) * H8;
+    const uint4* src1 = x + static_cast<int64_t>(has1 ? t1 : t0) * H8;
     for (int c0 = 0; c0 < H8; c0 += 32 * 8) {
-      uint4 v[8];
+      uint4 v0[8], v1[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int c = c0 + u * 32 + lane;
-        if (c < H8) v[u] = __ldg(src + c);
+        if (c < H8) {
+          v0[u] = __ldg(src0 + c);
+          if (has1) v1[u] = __ldg(src1 + c);
+        }
+      }
+      int m0 = -1, m1 = -1;
+      if (c0 == 0) {  // bookkeeping once per token, while the row loads are in flight
+        m0 = scatter_slot<K>(t0, lane, E, idx, w, blk_base, local_rank, token_map, dw, slot_of, S);
+        if (has1)
+          m1 = scatter_slot<K>(t1, lane, E, idx, w, blk_base, local_rank, token_map, dw, slot_of, S);
+      } else {  // rows longer than 2048 elements: the slots again, without the bookkeeping
+        if (lane < K) {
+          const int64_t tk0 = static_cast<int64_t>(t0) * K + lane;
+          const int e0 = __ldg(idx + tk0);
+          if (e0 >= 0 && e0 < E) {
+            const int s = __ldg(blk_base + static_cast<int64_t>(t0 / kRouteTokens) * E + e0) +
+                          __ldg(local_rank + tk0);
+            if (s >= 0 && s < S) m0 = s;
+          }
+          if (has1) {
+            const int64_t tk1 = static_cast<int64_t>(t1) * K + lane;
+            const int e1 = __ldg(idx + tk1);
+            if (e1 >= 0 && e1 < E) {
+              const int s = __ldg(blk_base + static_cast<int64_t>(t1 / kRouteTokens) * E + e1) +
+                            __ldg(local_rank + tk1);
+              if (s >= 0 && s < S) m1 = s;
+            }
+          }
+        }
       }
 #pragma unroll
       for (int j = 0; j < K; ++j) {
-        if (slots[j] < 0) continue;
-        uint4* dst = dispatched + static_cast<int64_t>(slots[j]) * H8;
+        const int s0 = __shfl_sync(0xffffffffu, m0, j);
+        const int s1 = __shfl_sync(0xffffffffu, m1, j);
+        if (s0 >= 0) {
+          uint4* dst = dispatched + static_cast<int64_t>(s0) * H8;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int c = c0 + u * 32 + lane;
-          if (c < H8) dst[c] = v[u];
+          for (int u = 0; u < 8; ++u) {
+            const int c = c0 + u * 32 + lane;
+            if (c < H8) dst[c] = v0[u];
+          }
+        }
+        if (has1 && s1 >= 0) {
+          uint4* dst = dispatched + static_cast<int64_t>(s1) * H8;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int c = c0 + u * 32 + lane;
+            if (c < H8) dst[c] = v1[u];
+          }
         }
       }
     }
