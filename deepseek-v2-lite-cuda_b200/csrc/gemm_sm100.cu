@@ -778,20 +778,6 @@ int launch(const Problem& pr, cudaStream_t s) {
   return launch_multi(one, 1, s, nullptr);
 }
 
-int grid_for(const Problem* const* probs, int n) {
-  DeviceInfo di;
-  if (device_info(&di) != DS_OK) return -1;
-  int64_t max_tiles = 0;
-  int cap = di.num_sms;
-  for (int i = 0; i < n; ++i) {
-    if (probs[i] == nullptr || probs[i]->a_rows <= 0) continue;
-    const Problem& pr = *probs[i];
-    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
-    if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
-  }
-  return static_cast<int>(max_tiles < cap ? max_tiles : cap);
-}
-
 int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,
                           cudaStream_t s) {
   if (S <= 0) return DS_OK;

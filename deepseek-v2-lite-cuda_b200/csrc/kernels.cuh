@@ -112,8 +112,6 @@ int launch(const Problem& pr, cudaStream_t s);
 int launch_multi(const Problem* const* probs, int n, cudaStream_t s,
                  const Signal* sig = nullptr);
 
-// Grid size launch_multi would use for these problems (-1 on error).
-int grid_for(const Problem* const* probs, int n);
 
 // Rows of out [S, ldo] outside [offsets[0], offsets[groups]) are set to zero.
 int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,

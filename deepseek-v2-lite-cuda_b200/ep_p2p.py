@@ -6,8 +6,9 @@ every rank allocates one symmetric segment (count matrix, per-forward flags, rec
 return rows), the segments are mapped into every rank's address space with CUDA IPC once at
 construction, and each forward is one C call (ds_ep_layer_forward):
 
-  route | plan + count exchange | dispatch straight into the owners' receive buffers |
-  GEMM1+SwiGLU (shared expert first, routed rows once all ranks' rows are in) |
+  route | plan + count exchange | dispatch straight into the owners' receive buffers,
+  with the shared expert's GEMM1+SwiGLU beside it on a side stream |
+  routed GEMM1+SwiGLU (once all ranks' rows are in) |
   GEMM2 (routed rows stored straight back to the token owners, then the shared expert) |
   combine (after all ranks returned their rows)
 

@@ -339,9 +339,11 @@ DS_API size_t ds_ep_layer_workspace_size(int max_tokens, int hidden_size, int nu
 /* One expert-parallel MoE layer forward of this rank's num_tokens (0 allowed; every rank
  * must call it for every forward, with epoch = 1, 2, 3, ...).  w1_local [El*2I, H] and
  * w2_local [El*H, I] hold experts [rank*El, (rank+1)*El) in the prepacked layout; router,
- * shared expert, logits_out and out as ds_moe_layer_forward_from_x.  events: NULL or
+ * shared expert, logits_out and out as ds_moe_layer_forward_from_x.  The shared expert's
+ * GEMM1 runs on an internal second stream beside the dispatch (forked from and joined back
+ * into `stream` with events; one forward at a time per device).  events: NULL or
  * DS_EP_NUM_EVENTS handles bracketing route | plan+count exchange | dispatch+send |
- * GEMM1 (+shared) | GEMM2 (+shared, return) | combine. */
+ * routed GEMM1 | GEMM2 (+shared, return) | combine. */
 DS_API int ds_ep_layer_forward(const void* x_bf16, int num_tokens,
                                const void* router_w_split_bf16, float* logits_out,
                                const void* w1_local_bf16, const void* w2_local_bf16,
