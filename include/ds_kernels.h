@@ -2,11 +2,12 @@
  * ds_kernels.h — C ABI of libds_kernels_sm100.so, the B200 (sm_100a) implementation of
  * DeepSeek-V2-Lite's MoE layer and MLA projection hot path.
  *
- * Every entry point takes raw device pointers, plain sizes and a CUDA stream passed as
- * `void*` (a cudaStream_t; NULL = legacy default stream).  No entry point allocates device
- * memory: scratch is passed in by the caller as (workspace, workspace_bytes), sized by the
- * matching *_workspace_size() query.  All launches are asynchronous on `stream`; nothing
- * synchronises with the host, so every entry point can be captured in a CUDA graph.
+ * Every compute entry point takes raw device pointers, plain sizes and a CUDA stream passed
+ * as `void*` (a cudaStream_t; NULL = legacy default stream) and allocates no device memory:
+ * scratch is passed in by the caller as (workspace, workspace_bytes), sized by the matching
+ * *_workspace_size() query.  (The one allocating call is ds_ep_alloc, which creates the
+ * expert-parallel segment once.)  All launches are asynchronous on `stream` and nothing in
+ * the compute entry points synchronises with the host.
  *
  * Return value: DS_OK (0) or a DS_ERR_* code.  ds_last_error() returns a message for the
  * last failure on the calling host thread.  Device-side failures (a bounded wait that ran
