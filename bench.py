@@ -480,6 +480,13 @@ def op_report(path, dev):
     sets = [(q.clone(), k.clone(), cs.clone(), cs.clone()) for _ in range(_copies(nb))]
     out.append(("rope cfg3", nb, _time([lambda t=t: ds_kernels.rope(*t) for t in sets])))
     del sets
+    # decoder glue around the layer: residual add + RMSNorm on H = 2048 (16384 rows)
+    xr = torch.randn(M, H, device=dev).to(torch.bfloat16)
+    rr = torch.randn(M, H, device=dev).to(torch.bfloat16)
+    wr = torch.rand(H, device=dev) + 0.5
+    out.append(("rms_norm_residual [16384, 2048]", 8 * M * H,
+                _time(lambda: ds_kernels.rms_norm_residual(xr, rr, wr))))
+    del xr, rr
     # calibration: a plain device copy (read + write) of the same byte counts, same harness
     for label, nbt in (("device copy, rms_norm cfg3 bytes", 4 * M * 512),
                        ("device copy, rope cfg3 bytes", nb)):

@@ -12,6 +12,27 @@
 namespace ds {
 namespace {
 
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 f32x8_to_bf16(const float (&f)[8]) {
+  uint4 r;
+  uint32_t* u = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    u[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  return r;
+}
+
 // Contiguous rows of at most 512 elements (the 512-d kv latent): a pipelined ring.  Each CTA
 // walks tiles of kNormTileRows rows; thread 0 keeps kNormStages tiles in flight with one bulk
 // copy each (global -> shared, no registers spent on the bytes in flight) while the 8 warps
@@ -127,6 +148,65 @@ __global__ void __launch_bounds__(256)
     for (int i = done; i < issued; ++i)
       ptx::mbar_wait(ptx::smem_u32(&bars[i % kNormStages]), (i / kNormStages) & 1, &never,
                      status, timeout_cycles, DS_ERR_TIMEOUT);
+  }
+}
+
+// Decoder-layer glue (src/reference/decoder_layer.py:123-139 around RMSNorm,
+// src/reference/mla.py:59-64): sum = bf16(residual + x), normed = bf16(w * sum * rsqrt(
+// mean(sum^2) + eps)) with f32 statistics over the rounded sum; both written.  One warp per
+// row of up to 2048 elements, both input rows' 16-byte loads issued before the math.
+__global__ void __launch_bounds__(256)
+    rms_norm_residual_kernel(const uint4* __restrict__ x, const uint4* __restrict__ res,
+                             const float4* __restrict__ weight, uint4* __restrict__ sum_out,
+                             uint4* __restrict__ normed, int rows, int H, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const int H8 = H >> 3;
+  const float inv_h = 1.f / static_cast<float>(H);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const int64_t base = static_cast<int64_t>(r) * H8;
+    uint4 a[8], b[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = u * 32 + lane;
+      if (c < H8) {
+        a[u] = __ldg(x + base + c);
+        b[u] = __ldg(res + base + c);
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = u * 32 + lane;
+      if (c >= H8) continue;
+      float fa[8], fb[8];
+      bf16x8_to_f32(a[u], fa);
+      bf16x8_to_f32(b[u], fb);
+      float sm[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sm[i] = fb[i] + fa[i];
+      a[u] = f32x8_to_bf16(sm);  // the rounded sum: written out and normalised
+      float fs[8];
+      bf16x8_to_f32(a[u], fs);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(fs[i], fs[i], ss);
+      sum_out[base + c] = a[u];
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+    const float scale = rsqrtf(ss * inv_h + eps);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = u * 32 + lane;
+      if (c >= H8) continue;
+      const float4 w0 = __ldg(weight + 2 * c), w1 = __ldg(weight + 2 * c + 1);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float fs[8], o[8];
+      bf16x8_to_f32(a[u], fs);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = fs[i] * scale * wv[i];
+      normed[base + c] = f32x8_to_bf16(o);
+    }
   }
 }
 
@@ -337,27 +417,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __bfloat1622float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
-
-__device__ __forceinline__ uint4 f32x8_to_bf16(const float (&f)[8]) {
-  uint4 r;
-  uint32_t* u = reinterpret_cast<uint32_t*>(&r);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-    u[i] = *reinterpret_cast<const uint32_t*>(&b);
-  }
-  return r;
-}
-
 // rope_dim % 16 == 0: one thread per (batch, position, 16-element chunk, group of 4 rows)
 // where the rows of a (batch, position) are the q heads and then k.  The chunk's 8 rotation
 // pairs k = 8c..8c+7 need cos/sin[k] and cos/sin[half + k] (one 16-byte load each), loaded
@@ -516,6 +575,29 @@ int ds_rms_norm_strided(const void* input_bf16, int64_t in_stride, const float* 
       static_cast<const __nv_bfloat16*>(input_bf16), in_stride, weight,
       static_cast<__nv_bfloat16*>(output_bf16), out_stride, rows, hidden_size, eps, vec_ok);
   DS_LAUNCH_CHECK("rms_norm_kernel");
+  return DS_OK;
+}
+
+int ds_rms_norm_residual(const void* input_bf16, const void* residual_bf16, const float* weight,
+                         void* sum_out_bf16, void* normed_out_bf16, int rows, int hidden_size,
+                         float eps, void* stream) {
+  DS_REQUIRE(rows >= 0, "rms_norm_residual: rows must be >= 0");
+  DS_REQUIRE(hidden_size > 0 && hidden_size % 8 == 0 && hidden_size <= 2048,
+             "rms_norm_residual: hidden_size must be a multiple of 8, at most 2048");
+  if (rows == 0) return DS_OK;
+  DS_REQUIRE(input_bf16 && residual_bf16 && weight && sum_out_bf16 && normed_out_bf16,
+             "rms_norm_residual: null pointer");
+  DS_REQUIRE(ds::aligned16(input_bf16) && ds::aligned16(residual_bf16) && ds::aligned16(weight) &&
+                 ds::aligned16(sum_out_bf16) && ds::aligned16(normed_out_bf16),
+             "rms_norm_residual: pointers must be 16-byte aligned");
+  ds::DeviceInfo di;
+  DS_TRY(ds::device_info(&di));
+  const int grid = ds::grid_cap(rows, 8, di.num_sms);
+  ds::rms_norm_residual_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(input_bf16), static_cast<const uint4*>(residual_bf16),
+      reinterpret_cast<const float4*>(weight), static_cast<uint4*>(sum_out_bf16),
+      static_cast<uint4*>(normed_out_bf16), rows, hidden_size, eps);
+  DS_LAUNCH_CHECK("rms_norm_residual_kernel");
   return DS_OK;
 }
 

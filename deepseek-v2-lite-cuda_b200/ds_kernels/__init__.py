@@ -60,6 +60,7 @@ SIGNATURES = {
     "ds_moe_gemm2": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "ds_rms_norm": (_i, [_vp, _vp, _vp, _i, _i, _f, _vp]),
     "ds_rms_norm_strided": (_i, [_vp, _i64, _vp, _vp, _i64, _i, _i, _f, _vp]),
+    "ds_rms_norm_residual": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp]),
     "ds_kv_upproj": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "ds_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "ds_moe_layer_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
@@ -390,6 +391,32 @@ def rms_norm(input: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> to
         _check(_lib.ds_rms_norm(_ptr(input), _ptr(weight), _ptr(out), rows, hidden, float(eps),
                                 _stream(input)), "rms_norm")
     return out
+
+
+def rms_norm_residual(input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                      eps: float = 1e-6) -> List[torch.Tensor]:
+    """Decoder-layer glue: returns [normed, sum] with sum = bf16(residual + input) (the next
+    residual) and normed = RMSNorm(sum) — the residual add and pre-norm around the attention
+    and MoE sub-layers of src/reference/decoder_layer.py:123-139, in one pass."""
+    _require(input.is_cuda and residual.is_cuda and weight.is_cuda,
+             "rms_norm_residual: all inputs must be CUDA tensors.")
+    _require(input.is_contiguous() and residual.is_contiguous(),
+             "rms_norm_residual: input and residual must be contiguous.")
+    _require(input.dtype == torch.bfloat16 and residual.dtype == torch.bfloat16,
+             "rms_norm_residual: input and residual must be bfloat16.")
+    _require(weight.dtype == torch.float32, "rms_norm_residual: weight must be float32.")
+    _require(tuple(input.shape) == tuple(residual.shape) and input.dim() >= 1,
+             "rms_norm_residual: input and residual must have the same shape.")
+    H = input.shape[-1]
+    _require(weight.numel() == H, "rms_norm_residual: weight size must match hidden_size.")
+    rows = input.numel() // H if H else 0
+    s = torch.empty_like(input)
+    n = torch.empty_like(input)
+    with _on_device(input):
+        _check(_lib.ds_rms_norm_residual(_ptr(input), _ptr(residual), _ptr(weight.contiguous()),
+                                         _ptr(s), _ptr(n), rows, H, float(eps), _stream(input)),
+               "rms_norm_residual")
+    return [n, s]
 
 
 def kv_upproj(normed_kv: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:

@@ -170,6 +170,16 @@ DS_API int ds_rms_norm_strided(const void* input_bf16, int64_t in_stride, const 
                         void* output_bf16, int64_t out_stride, int rows, int hidden_size,
                         float eps, void* stream);
 
+/* Decoder-layer glue around the MoE layer (additive op; the residual adds and pre-norms of
+ * src/reference/decoder_layer.py:123-139 with RMSNorm of src/reference/mla.py:59-64):
+ *   sum_out[r] = bf16(residual[r] + input[r]),
+ *   normed_out[r] = bf16( weight * sum_out[r] * rsqrt(mean(sum_out[r]^2) + eps) ),
+ * statistics in f32 over the rounded sum, one pass over both inputs.  Contiguous rows,
+ * hidden_size a multiple of 8 and at most 2048, 16-byte aligned pointers. */
+DS_API int ds_rms_norm_residual(const void* input_bf16, const void* residual_bf16,
+                                const float* weight, void* sum_out_bf16, void* normed_out_bf16,
+                                int rows, int hidden_size, float eps, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * K9 kv up-projection.  Replaces launch_kv_upproj (src/kernels/include/mla/kv_upproj.h:
  * 30-38, src/kernels/mla/kv_upproj.cu:77-119) and kv_upproj_forward (kv_upproj.cu:

@@ -2,6 +2,7 @@
 
 rms_norm   : src/reference/mla.py:59-64 (f32 statistics), one rounding at the end as in
              src/kernels/mla/rms_norm.cu:104-114.
+rms_norm_residual: the residual add + pre-norm of src/reference/decoder_layer.py:123-139.
 yarn_cos_sin: the YaRN tables of src/reference/mla.py:66-173 (correction range, linear ramp,
              frequency blend, mscale ratio), restated.
 rope       : src/reference/mla.py:176-206 (interleave -> half transform, then
@@ -22,6 +23,14 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.
     xf = x.to(F32)
     var = xf.pow(2).mean(-1, keepdim=True)
     return weight.to(F32) * (xf * torch.rsqrt(var + eps))
+
+
+def rms_norm_residual(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                      eps: float = 1e-6) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(normed, sum): sum = residual + x as bf16 tensors add (src/reference/decoder_layer.py:
+    130, 133-135), normed = rms_norm(sum) (src/reference/mla.py:59-64)."""
+    s = (residual.to(F32) + x.to(F32)).to(torch.bfloat16)
+    return rms_norm(s, weight, eps), s
 
 
 def _correction_dim(num_rot: float, dim: int, base: float, max_pos: int) -> float:

@@ -55,6 +55,18 @@ def test_rms_norm_cfg3_full():
     assert_bf16_close(out, oracle.rms_norm(x, w), 1e-2)
 
 
+@pytest.mark.parametrize("rows,H", [(1, 2048), (7, 2048), (1000, 2048), (33, 512), (5, 96)])
+def test_rms_norm_residual(rows, H):
+    g = torch.Generator().manual_seed(rows + H)
+    x = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    r = (torch.randn(rows, H, generator=g) * 2).to(torch.bfloat16)
+    w = torch.rand(H, generator=g) + 0.5
+    n, s = ds().rms_norm_residual(x.cuda(), r.cuda(), w.cuda())
+    rn, rs = oracle.rms_norm_residual(x, r, w)
+    assert torch.equal(s.cpu(), rs)  # the residual sum is bit-exact
+    assert_bf16_close(n, rn, 1e-2)
+
+
 def _rope_inputs(bsz, seq, heads=16, seed=0, scaling=40.0):
     g = torch.Generator().manual_seed(seed)
     q = (torch.randn(bsz, heads, seq, 64, generator=g) * 0.5).to(torch.bfloat16)
