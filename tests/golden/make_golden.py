@@ -3,7 +3,8 @@
     python tests/golden/make_golden.py [--reference /path/to/DeepSeek-V2-Lite-CUDA]
 
 Runs the reference's own PyTorch code (src/reference/moe.py, src/reference/mla.py, imported
-unmodified from the reference checkout) on small seeded inputs and writes the inputs and
+unmodified from the reference checkout; the decoder-layer residual add is restated around
+the reference's RMSNorm module) on small seeded inputs and writes the inputs and
 outputs to tests/golden/*.pt, together with the known answers that the reference's kernel
 tests assert (tests/test_moe_scan_kernel.py, tests/test_moe_combine_kernel.py,
 tests/test_moe_routing_kernel.py).  The reference is only needed to regenerate the files;
@@ -93,6 +94,23 @@ def mla_fixture(ref_mla, name, bsz, seq, seed, scaling_factor):
     print(f"wrote {name}.pt")
 
 
+def decoder_glue_fixture(ref_mla, name, rows, H, seed):
+    """The residual add + pre-norm of src/reference/decoder_layer.py:123-139 on bf16 hidden
+    states, with the reference's RMSNorm module (src/reference/mla.py:53-64)."""
+    torch.manual_seed(seed)
+    norm = ref_mla.RMSNorm(H, eps=1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(torch.rand(H) + 0.5)
+    x = torch.randn(rows, H).to(torch.bfloat16)
+    residual = (torch.randn(rows, H) * 2).to(torch.bfloat16)
+    with torch.no_grad():
+        summed = residual + x          # decoder_layer.py:130 / :138
+        normed = norm(summed)          # decoder_layer.py:133-134 (post_attention_layernorm)
+    torch.save({"x": x, "residual": residual, "weight": norm.weight.detach().clone(),
+                "sum": summed, "normed": normed}, os.path.join(HERE, f"{name}.pt"))
+    print(f"wrote {name}.pt")
+
+
 def known_answers():
     """Known-answer cases asserted by the reference's kernel tests."""
     ka = {}
@@ -142,6 +160,7 @@ def main():
                 w_std=0.1)
     mla_fixture(ref_mla, "mla_yarn40", bsz=2, seq=16, seed=3, scaling_factor=40.0)
     mla_fixture(ref_mla, "mla_plain", bsz=1, seq=32, seed=4, scaling_factor=1.0)
+    decoder_glue_fixture(ref_mla, "decoder_glue", rows=12, H=256, seed=5)
     known_answers()
 
 

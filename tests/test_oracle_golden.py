@@ -118,3 +118,13 @@ def test_mla_plain_rope_theta():
     inv = 1.0 / (10000.0 ** (torch.arange(0, 64, 2, dtype=torch.float32) / 64))
     ang = torch.outer(torch.arange(8, dtype=torch.float32), inv)
     torch.testing.assert_close(cos, torch.cat([ang, ang], -1).cos(), atol=1e-6, rtol=0)
+
+
+def test_decoder_glue_residual_rms_norm():
+    # the decoder layer's residual add + RMSNorm (reference module on bf16 hidden states)
+    fx = _load("decoder_glue.pt")
+    normed, summed = oracle.rms_norm_residual(fx["x"], fx["residual"], fx["weight"])
+    assert torch.equal(summed, fx["sum"])  # the bf16 residual sum, bit for bit
+    # the reference rounds the normalised row to bf16 before the f32 weight (mla.py:64); the
+    # oracle keeps it in f32 (one rounding, as the kernels do): within a bf16 half-ulp
+    torch.testing.assert_close(normed, fx["normed"].float(), atol=1e-6, rtol=2.0 ** -8)
