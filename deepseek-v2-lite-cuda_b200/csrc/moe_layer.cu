@@ -59,6 +59,24 @@ extern "C" size_t ds_moe_layer_workspace_size(int num_tokens, int hidden_size, i
                          intermediate_size, shared_intermediate_size);
 }
 
+extern "C" int ds_moe_layer_workspace_routing(int num_tokens, int hidden_size, int num_experts,
+                                              int top_k, int intermediate_size,
+                                              int shared_intermediate_size, size_t* idx_offset,
+                                              size_t* weights_offset, size_t* slot_of_offset) {
+  DS_REQUIRE(num_tokens >= 0 && top_k >= 1, "moe_layer_workspace_routing: bad shape");
+  DS_REQUIRE(idx_offset && weights_offset && slot_of_offset,
+             "moe_layer_workspace_routing: null pointer");
+  ds::Carve c(reinterpret_cast<void*>(uintptr_t{256}), ~size_t{0} >> 1);
+  ds::LayerBuffers b;
+  ds::carve_layer(c, &b, num_tokens, hidden_size, num_experts, top_k, intermediate_size,
+                  shared_intermediate_size);
+  const uintptr_t base = 256;
+  *idx_offset = reinterpret_cast<uintptr_t>(b.idx) - base;
+  *weights_offset = reinterpret_cast<uintptr_t>(b.w) - base;
+  *slot_of_offset = reinterpret_cast<uintptr_t>(b.slot_of) - base;
+  return DS_OK;
+}
+
 namespace {
 
 // One implementation for both entry points: routing from given f32 logits, or from x via the

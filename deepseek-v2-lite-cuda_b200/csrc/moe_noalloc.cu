@@ -23,6 +23,8 @@
 //   * The first call on each device looks up the array's device address (a one-time set-up
 //     that may load this library's device code); make that first call before any stream
 //     capture begins.
+//   * The address used is the current device's, so the stream must belong to the current
+//     device; a stream of another device is rejected with DS_ERR_UNSUPPORTED.
 #include <mutex>
 
 #include "kernels.cuh"
@@ -88,13 +90,23 @@ int ds_moe_dispatch_noalloc(const void* input_bf16, const int32_t* topk_indices,
              "moe_dispatch_noalloc: null pointer");
   DS_REQUIRE(ds::aligned16(input_bf16) && ds::aligned16(dispatched_bf16),
              "moe_dispatch_noalloc: input/dispatched must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (s != nullptr) {
+    int cur = 0, sdev = 0;
+    DS_CUDA(cudaGetDevice(&cur));
+    DS_CUDA(cudaStreamGetDevice(s, &sdev));
+    if (sdev != cur)
+      return ds::fail(DS_ERR_UNSUPPORTED,
+                      "moe_dispatch_noalloc: the stream belongs to device %d but device %d is "
+                      "current; make the stream's device current first",
+                      sdev, cur);
+  }
   int32_t* scratch = nullptr;
   DS_TRY(ds::scratch_for_current_device(&scratch));
   const int nblk = ds::route_blocks(num_tokens);
   int32_t* hist = scratch;
   int32_t* base = scratch + ds::kHistInts;
   int32_t* rank = scratch + 2 * ds::kHistInts;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   DS_TRY(ds::launch_rank(topk_indices, num_tokens, num_experts, top_k, hist, rank, s));
   DS_TRY(ds::launch_plan(hist, nblk, num_experts, expert_offsets, nullptr, nullptr, base, s));
   return ds::launch_scatter(input_bf16, num_tokens, hidden_size, num_experts, top_k,

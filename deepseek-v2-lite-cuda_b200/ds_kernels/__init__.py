@@ -64,6 +64,8 @@ SIGNATURES = {
     "ds_kv_upproj": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "ds_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "ds_moe_layer_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "ds_moe_layer_workspace_routing": (_i, [_i, _i, _i, _i, _i, _i, ctypes.POINTER(_sz),
+                                            ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
     "ds_moe_layer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
                                   _vp, _sz, _vp, _vp]),
     "ds_debug_wait_probe": (_i, [ctypes.c_longlong, _vp]),
@@ -486,6 +488,23 @@ def moe_layer_workspace_size(num_tokens: int, hidden_size: int, num_experts: int
                                                 intermediate_size, shared_intermediate_size))
 
 
+def moe_layer_workspace_routing(workspace: torch.Tensor, num_tokens: int, hidden_size: int,
+                                num_experts: int, top_k: int, intermediate_size: int,
+                                shared_intermediate_size: int):
+    """Views of the routing a layer forward left in `workspace`: (topk_indices int32 [T, k],
+    topk_weights f32 [T, k], slot_of int32 [T, k]); valid until the workspace is reused."""
+    a, b, c = _sz(0), _sz(0), _sz(0)
+    _check(_lib.ds_moe_layer_workspace_routing(num_tokens, hidden_size, num_experts, top_k,
+                                               intermediate_size, shared_intermediate_size,
+                                               ctypes.byref(a), ctypes.byref(b),
+                                               ctypes.byref(c)), "moe_layer_workspace_routing")
+    n = num_tokens * top_k
+
+    def view(off, dtype):
+        return workspace[off:off + 4 * n].view(dtype).view(num_tokens, top_k)
+    return view(a.value, torch.int32), view(b.value, torch.float32), view(c.value, torch.int32)
+
+
 def moe_layer_forward(router_logits: torch.Tensor, x: torch.Tensor, packed_w1: torch.Tensor,
                       w2: torch.Tensor, shared_w1: Optional[torch.Tensor] = None,
                       shared_w2: Optional[torch.Tensor] = None, top_k: int = 6,
@@ -882,3 +901,37 @@ def ep_layer_forward(x: torch.Tensor, router_w_split: torch.Tensor, num_experts:
             top_k, I, Is, rank, world, max_tokens, bases, epoch, timeout_ms, _ptr(workspace),
             workspace.numel(), ev, _stream(x)), "ep_layer_forward")
     return out
+
+
+# ---- torch custom operators ----------------------------------------------------------------
+# Every drop-in op is also registered as torch.ops.ds_kernels.<name> (torch_ops.py) with a
+# fake kernel, so torch.compile / torch.export / FakeTensor propagation see through it.  The
+# module-level functions stay direct C-ABI calls in eager mode and route through the
+# registered operator while torch.compile traces them.
+import functools as _functools  # noqa: E402
+
+_eager = {}
+
+
+def _traced(name):
+    eager = globals()[name]
+    _eager[name] = eager
+
+    @_functools.wraps(eager)
+    def op(*args, **kwargs):
+        if torch.compiler.is_compiling():
+            r = getattr(torch.ops.ds_kernels, name)(*args, **kwargs)
+            return list(r) if isinstance(r, tuple) else r
+        return eager(*args, **kwargs)
+
+    return op
+
+
+_TRACED_OPS = ("moe_routing", "moe_scan", "moe_dispatch", "moe_combine", "swiglu", "moe_gemm1",
+               "moe_gemm2", "rms_norm", "kv_upproj", "rope", "moe_gemm1_swiglu",
+               "rms_norm_residual", "moe_layer_fused")
+for _n in _TRACED_OPS:
+    globals()[_n] = _traced(_n)
+del _n
+
+from . import torch_ops  # noqa: E402,F401  (registers torch.ops.ds_kernels.*)

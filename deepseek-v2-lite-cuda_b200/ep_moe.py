@@ -41,9 +41,10 @@ class CudaOps:
     def prepare_router(self, gate_weight):
         return self.k.router_weight_split(gate_weight)
 
-    def route(self, x, router_state, num_experts, top_k):
-        """-> (topk_indices, topk_weights): tensor-core router with f32-accurate logits."""
-        return self.k.moe_router(x, router_state, num_experts, top_k)
+    def route(self, x, router_state, num_experts, top_k, logits_out=None):
+        """-> (topk_indices, topk_weights): tensor-core router with f32-accurate logits
+        (written to `logits_out` f32 [T, E] when given)."""
+        return self.k.moe_router(x, router_state, num_experts, top_k, logits_out=logits_out)
 
     def dispatch(self, idx, w, x, num_experts):
         """-> (expert_offsets, slot_of, token_map, dispatched)."""
@@ -114,9 +115,11 @@ class EPMoELayer(torch.nn.Module):
     PHASES = ("route_dispatch", "exchange_counts", "exchange_rows", "expert_mlp",
               "exchange_back", "combine")
 
-    def forward(self, x: torch.Tensor, events=None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, events=None,
+                logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """events: optional list of len(PHASES)+1 CUDA events recorded on the current stream
-        at the phase boundaries (for timing)."""
+        at the phase boundaries (for timing); logits_out (f32 [T, E]) receives the router
+        logits."""
         ops, N, El, k = self.ops, self.world, self.local_experts, self.top_k
 
         def mark(i):
@@ -128,7 +131,10 @@ class EPMoELayer(torch.nn.Module):
         cap = max(1, ops.num_sms(x.device) - self.nccl_reserve_sms) if x.is_cuda else 0
 
         mark(0)
-        idx, w = ops.route(x, self.router_state, self.num_experts, k)
+        if logits_out is None:
+            idx, w = ops.route(x, self.router_state, self.num_experts, k)
+        else:
+            idx, w = ops.route(x, self.router_state, self.num_experts, k, logits_out=logits_out)
         offsets, slot_of, token_map, disp = ops.dispatch(idx, w, x, self.num_experts)
         mark(1)
         counts = (offsets[1:] - offsets[:-1]).to(torch.int32).view(N, El).contiguous()

@@ -98,6 +98,15 @@ class FusedMoELayer(nn.Module):
         self._ws = _Workspace()
         return self
 
+    def last_routing(self, num_tokens: int):
+        """(topk_indices int32 [T, k], topk_weights f32 [T, k]) of the last forward over
+        `num_tokens` tokens, read from the layer's workspace (valid until the next forward)."""
+        Is = 0 if self.shared_w1 is None else self.shared_w1.shape[0] // 2
+        idx, w, _ = ds_kernels.moe_layer_workspace_routing(
+            self._ws.buf, num_tokens, self.packed_w1.shape[2], self.num_experts, self.top_k,
+            self.packed_w1.shape[1] // 2, Is)
+        return idx, w
+
     def forward(self, hidden_states: torch.Tensor, events=None,
                 logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """hidden_states bf16 [T, H] -> bf16 [T, H].  `logits_out` (f32 [T, E]) receives the

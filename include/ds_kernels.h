@@ -103,7 +103,8 @@ DS_API int ds_moe_dispatch(const void* input_bf16, const int32_t* topk_indices,
  * num_experts <= 64, top_k <= 8.  All calls on a device share that array: calls that may
  * overlap on the GPU (unordered streams, several host threads) race and corrupt each
  * other's results, so order them on one stream.  The first call on each device looks up
- * the array's address (one-time set-up); make it before any stream capture begins. */
+ * the array's address (one-time set-up); make it before any stream capture begins.  The
+ * stream must belong to the current device (another device's stream: DS_ERR_UNSUPPORTED). */
 #define DS_NOALLOC_MAX_TOKENS 65536
 DS_API int ds_moe_dispatch_noalloc(const void* input_bf16, const int32_t* topk_indices,
                                    const float* topk_weights, const int32_t* expert_offsets,
@@ -213,6 +214,15 @@ DS_API int ds_rope(const void* q_pe_bf16, const void* k_pe_bf16, const void* cos
 DS_API size_t ds_moe_layer_workspace_size(int num_tokens, int hidden_size, int num_experts,
                                    int top_k, int intermediate_size,
                                    int shared_intermediate_size);
+/* Where a layer forward leaves its routing inside the workspace (new, additive; the
+ * reference pipeline returns it from moe_routing, src/kernels/moe_fused.py:131-134): byte
+ * offsets of topk_indices int32 [T, k], topk_weights f32 [T, k] and slot_of int32 [T, k]
+ * (the dispatch slot of each (token, pick)), valid after the forward until the next call
+ * that uses the same workspace. */
+DS_API int ds_moe_layer_workspace_routing(int num_tokens, int hidden_size, int num_experts,
+                                          int top_k, int intermediate_size,
+                                          int shared_intermediate_size, size_t* idx_offset,
+                                          size_t* weights_offset, size_t* slot_of_offset);
 DS_API int ds_moe_layer_forward(const float* router_logits, const void* x_bf16,
                          const void* packed_w1_bf16, const void* w2_bf16,
                          const void* shared_w1_bf16, const void* shared_w2_bf16,

@@ -147,8 +147,11 @@ def known_answers():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("DS_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("DS_REFERENCE"),
+                    help="root of a checkout of the reference project (or set DS_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference PATH (or set DS_REFERENCE) to the reference checkout")
     ref_moe, ref_mla = _import_reference(a.reference)
     torch.set_num_threads(4)
     # Reduced-width blocks keep the fixtures small; the algorithm is width-independent.

@@ -143,12 +143,26 @@ def test_moe_layer_fused_equals_from_x():
 
 
 def test_cfg2_full_size_from_x():
+    # The layer's own routing (router GEMM partials -> route kernel, inside the one C call) is
+    # read back from its workspace and must equal the oracle's routing of the device logits
+    # index for index at the full config-2 size; weights at 1e-6; then the output bound.
+    import ds_kernels
+    from moe_fused import FusedMoELayer
     W = weights(1, 2)
     D = device_weights(W)
     g = torch.Generator().manual_seed(1002)
     x = torch.randn(8192, H, generator=g).to(torch.bfloat16)
-    out, ref, logits = run_layer_from_x(W, D, x)
+    layer = FusedMoELayer.from_packed(D["gate"], D["w1"], D["w2"], D["sw1"], D["sw2"], top_k=K)
+    logits = torch.empty(8192, E, device="cuda")
+    out = layer(x.cuda(), logits_out=logits)
+    idx, w = layer.last_routing(8192)
+    ridx, rw = oracle.route(logits.cpu(), K)
+    assert torch.equal(idx.cpu(), ridx)
+    torch.testing.assert_close(w.cpu(), rw, atol=1e-6, rtol=0)
+    ref = oracle.moe_forward(x, W, K, logits=logits.cpu())
     check(out, ref)
+    out2, _, _ = run_layer_from_x(W, D, x)
+    assert torch.equal(out, out2)
 
 
 def test_layer_deterministic():

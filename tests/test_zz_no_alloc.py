@@ -51,7 +51,11 @@ def _noalloc(lib, x, idx, w, offsets):
 
 def test_noalloc_matches_workspace_dispatch_on_consecutive_calls():
     ds_kernels, lib = _lib()
-    for T, seed in ((4096, 1), (777, 2)):  # second call smaller: stale scratch must not leak
+    # The first call fills the whole scratch (exactly the largest accepted size: every
+    # per-block histogram and every rank entry); the next ones are smaller and take the plan
+    # kernel's looped path (more than 16 routing blocks) and then its short path, so stale
+    # entries of a larger call must not leak into their results.
+    for T, seed in ((65536, 1), (20000, 2), (777, 3)):
         x, idx, w, offsets = _inputs(T, seed)
         ref_disp, ref_tmap, ref_dw = ds_kernels.moe_dispatch(x, idx, w, offsets)
         disp, tmap, dw = _noalloc(lib, x, idx, w, offsets)
@@ -64,8 +68,28 @@ def test_noalloc_matches_workspace_dispatch_on_consecutive_calls():
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
     ds_kernels, lib = _lib()
-    limit = 65536
+    limit = 65536  # DS_NOALLOC_MAX_TOKENS
     st = lib.ds_moe_dispatch_noalloc(None, None, None, None, None, None, None, limit + 1, H, E, K,
                                      None)
     assert st == ds_kernels.DS_ERR_UNSUPPORTED
     assert "exceeds" in lib.ds_last_error().decode()
+
+
+def test_noalloc_rejects_a_stream_of_another_device():
+    """The scratch address is the current device's; a stream that belongs to another GPU is
+    refused before anything is launched (needs two GPUs)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ds_kernels, lib = _lib()
+    x, idx, w, offsets = _inputs(64, 4)
+    other = torch.cuda.Stream(device=1)
+    S = 64 * K
+    disp = torch.empty((S, H), dtype=torch.bfloat16, device="cuda")
+    tmap = torch.empty((S,), dtype=torch.int32, device="cuda")
+    dw = torch.empty((S,), dtype=torch.float32, device="cuda")
+    with torch.cuda.device(0):
+        st = lib.ds_moe_dispatch_noalloc(x.data_ptr(), idx.data_ptr(), w.data_ptr(),
+                                         offsets.data_ptr(), disp.data_ptr(), tmap.data_ptr(),
+                                         dw.data_ptr(), 64, H, E, K, other.cuda_stream)
+    assert st == ds_kernels.DS_ERR_UNSUPPORTED
+    assert "stream" in lib.ds_last_error().decode()
