@@ -67,6 +67,8 @@ struct ProbParams {
   int b_tile_stride;
   int b_half1_off;
   int weight_group_mod;
+  int seg_cols;       // output columns of a segment: the last n-tile may hold fewer than 128
+  int paired;         // the two B halves index two segments (gate | up) of seg_cols each
   __nv_bfloat16* out;
   int ldo;
   const int32_t* out_row_map;
@@ -107,6 +109,8 @@ struct TileInfo {
   int rows;
   int brow0;
   int nt;
+  int v0, v1;  // valid output columns of the two 128-column halves (<= 0: none)
+  bool full;   // both halves hold 128 valid columns
 };
 
 __device__ __forceinline__ const ProbParams& prob_params(const Params& p, int pb) {
@@ -134,12 +138,18 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const Params& p, const in
   ti.row0 = go[lo] + (mtg - gt[lo]) * BM;
   ti.rows = min(BM, go[lo + 1] - ti.row0);
   ti.brow0 = (lo % q.weight_group_mod) * q.b_rows_per_group + ti.nt * q.b_tile_stride;
+  const int c0 = ti.nt * q.b_tile_stride;
+  ti.v0 = min(BM, q.seg_cols - c0);
+  ti.v1 = q.paired ? ti.v0 : min(BM, q.seg_cols - c0 - q.b_half1_off);
+  ti.full = ti.v0 == BM && ti.v1 == BM;
   return ti;
 }
 
 // ---- epilogues: one accumulator row per thread, all lanes execute the TMEM loads ----------
-// SwiGLU: accumulator columns [0,128) gate, [128,256) up of the same 128 intermediate units.
-__device__ __forceinline__ void epilogue_swiglu(uint32_t tb, bool valid, __nv_bfloat16* dst) {
+// SwiGLU: accumulator columns [0,128) gate, [128,256) up of the same 128 intermediate units;
+// the first `ncols` (a multiple of 8) of the 128 outputs are stored.
+__device__ __forceinline__ void epilogue_swiglu(uint32_t tb, bool valid, __nv_bfloat16* dst,
+                                                int ncols) {
 #pragma unroll 1
   for (int cc = 0; cc < 4; ++cc) {
     uint32_t g[32], u[32];
@@ -155,25 +165,29 @@ __device__ __forceinline__ void epilogue_swiglu(uint32_t tb, bool valid, __nv_bf
       uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        if (cc * 32 + i * 8 < ncols)
+          d4[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
     }
   }
 }
 
-// Plain: 256 accumulator columns -> bf16, half h of the tile to column base + h*half1_off.
+// Plain: 256 accumulator columns -> bf16, half h of the tile to column base + h*half1_off;
+// the first v0 / v1 (multiples of 8) columns of the two halves are stored.
 __device__ __forceinline__ void epilogue_plain(uint32_t tb, bool valid, __nv_bfloat16* row,
-                                               int col0, int half1_off) {
+                                               int col0, int half1_off, int v0, int v1) {
 #pragma unroll 1
   for (int cc = 0; cc < 8; ++cc) {
     uint32_t v[32];
     ptx::tmem_ld32(tb + cc * 32, v);
     ptx::tmem_wait_ld(v);
-    if (valid) {
+    const int lim = (cc >> 2) ? v1 : v0;
+    if (valid && (cc & 3) * 32 < lim) {
       const int col = col0 + (cc >> 2) * half1_off + (cc & 3) * 32;
       uint4* d4 = reinterpret_cast<uint4*>(row + col);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        d4[i] = make_uint4(pack2(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
+        if ((cc & 3) * 32 + i * 8 < lim)
+          d4[i] = make_uint4(pack2(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
                            pack2(__uint_as_float(v[8 * i + 2]), __uint_as_float(v[8 * i + 3])),
                            pack2(__uint_as_float(v[8 * i + 4]), __uint_as_float(v[8 * i + 5])),
                            pack2(__uint_as_float(v[8 * i + 6]), __uint_as_float(v[8 * i + 7])));
@@ -236,7 +250,8 @@ __device__ __forceinline__ void epilogue_plain_staged(uint32_t tb, const CUtenso
 // 128-byte row segments (whole NVLink / L2 lines) instead of 32 scattered 16-byte pieces.
 // dst: this lane's output row (nullptr = row not written).
 __device__ __forceinline__ void epilogue_plain_mapped(uint32_t tb, uint32_t slab, int lane,
-                                                      __nv_bfloat16* dst, int col0, int half1_off) {
+                                                      __nv_bfloat16* dst, int col0, int half1_off,
+                                                      int v0, int v1) {
   const unsigned long long my = reinterpret_cast<unsigned long long>(dst);
 #pragma unroll 1
   for (int c = 0; c < 4; ++c) {
@@ -253,7 +268,9 @@ __device__ __forceinline__ void epilogue_plain_mapped(uint32_t tb, uint32_t slab
     slab_acquire(lane);  // the previous chunk's copy-out (or TMA store) has read the slab
     slab_put_row(slab, lane, w);
     __syncwarp();
-    const int col = col0 + (c >> 1) * half1_off + (c & 1) * 64 + (lane & 7) * 8;
+    const int in_half = (c & 1) * 64 + (lane & 7) * 8;
+    const int col = col0 + (c >> 1) * half1_off + in_half;
+    const bool col_ok = in_half < ((c >> 1) ? v1 : v0);
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const int rr = it * 4 + (lane >> 3);
@@ -264,7 +281,8 @@ __device__ __forceinline__ void epilogue_plain_mapped(uint32_t tb, uint32_t slab
       asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                    : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                    : "r"(addr));
-      if (d != 0ull) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d) + col) = v;
+      if (d != 0ull && col_ok)
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d) + col) = v;
     }
   }
 }
@@ -540,14 +558,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // a warp whose 32 rows are all in the tile's group, with contiguous output rows,
       // stores through its shared-memory slab and TMA
-      const bool staged = qp.tma_out && q * 32 + 32 <= ti.rows;
+      const bool staged = qp.tma_out && ti.full && q * 32 + 32 <= ti.rows;
       const CUtensorMap* tO = ti.prob ? &tmO1 : &tmO0;
       const uint32_t slab = sOut + static_cast<uint32_t>(warp - 2) * kSlabBytes;
       if constexpr (EPI == kSwiGLU) {
         if (staged)
           epilogue_swiglu_staged(tb, tO, slab, lane, ti.row0 + q * 32, ti.nt * 128);
         else
-          epilogue_swiglu(tb, valid, obase + orow * qp.ldo + ti.nt * 128);
+          epilogue_swiglu(tb, valid, obase + orow * qp.ldo + ti.nt * 128, ti.v0);
       } else if constexpr (EPI == kRouter) {
         epilogue_router_partials(
             tb, valid, qp.logits_out + (static_cast<int64_t>(ti.nt) * qp.dense_rows + orow) * 192);
@@ -557,10 +575,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 qp.b_half1_off);
         else if (!qp.tma_out)
           epilogue_plain_mapped(tb, slab, lane, valid ? obase + orow * qp.ldo : nullptr,
-                                ti.nt * qp.b_tile_stride, qp.b_half1_off);
+                                ti.nt * qp.b_tile_stride, qp.b_half1_off, ti.v0, ti.v1);
         else
           epilogue_plain(tb, valid, obase + orow * qp.ldo, ti.nt * qp.b_tile_stride,
-                         qp.b_half1_off);
+                         qp.b_half1_off, ti.v0, ti.v1);
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -667,6 +685,7 @@ int check_problem(const Problem& pr) {
   DS_REQUIRE(pr.groups >= 1 && pr.groups <= kMaxGroups, "gemm: groups=%d outside [1, %d]",
              pr.groups, kMaxGroups);
   DS_REQUIRE(pr.n_tiles >= 1 && pr.weight_group_mod >= 1, "gemm: bad tiling");
+  DS_REQUIRE(pr.seg_cols >= 0 && pr.seg_cols % 8 == 0, "gemm: seg_cols must be a multiple of 8");
   DS_REQUIRE(pr.a_rows < (1LL << 31) && pr.b_rows < (1LL << 31), "gemm: too many rows");
   DS_REQUIRE(pr.epilogue == kPlain || pr.epilogue == kSwiGLU || pr.epilogue == kRouter,
              "gemm: unknown epilogue %d", pr.epilogue);
@@ -684,6 +703,10 @@ ProbParams prob_params_of(const Problem& pr) {
   q.b_tile_stride = pr.b_tile_stride;
   q.b_half1_off = pr.b_half1_off;
   q.weight_group_mod = pr.weight_group_mod;
+  q.paired = pr.epilogue != kRouter && pr.b_tile_stride == 128;
+  q.seg_cols = pr.seg_cols > 0 ? pr.seg_cols
+               : q.paired      ? pr.b_half1_off
+                               : pr.n_tiles * 256;
   q.out = static_cast<__nv_bfloat16*>(pr.out);
   q.ldo = pr.ldo;
   q.out_row_map = pr.out_row_map;
@@ -801,7 +824,7 @@ int moe_gemm1_impl(const void* dispatched, const void* packed_w1, const int32_t*
                    void* out, int S, int E, int H, int twoI, int epilogue, void* stream,
                    int max_ctas = 0) {
   DS_REQUIRE(S >= 0 && E >= 1 && H > 0 && twoI > 0, "gemm1: bad shape");
-  DS_REQUIRE(twoI % 256 == 0, "gemm1: 2*intermediate_size=%d must be a multiple of 256", twoI);
+  DS_REQUIRE(twoI % 16 == 0, "gemm1: 2*intermediate_size=%d must be a multiple of 16", twoI);
   DS_REQUIRE(H % 8 == 0, "gemm1: hidden_size must be a multiple of 8");
   if (S == 0) return DS_OK;
   DS_REQUIRE(offsets != nullptr, "gemm1: expert_offsets is null");
@@ -815,7 +838,8 @@ int moe_gemm1_impl(const void* dispatched, const void* packed_w1, const int32_t*
   pr.b_rows = static_cast<int64_t>(E) * twoI;
   pr.offsets = offsets;
   pr.groups = E;
-  pr.n_tiles = I / 128;
+  pr.n_tiles = (I + 127) / 128;
+  pr.seg_cols = I;
   pr.b_rows_per_group = twoI;
   pr.b_tile_stride = 128;
   pr.b_half1_off = I;
@@ -835,7 +859,7 @@ int moe_gemm2_impl(const void* swiglu_out_bf16, const void* w2_bf16,
                    void* stream) {
   DS_REQUIRE(total_slots >= 0 && num_experts >= 1 && intermediate_size > 0 && hidden_size > 0,
              "gemm2: bad shape");
-  DS_REQUIRE(hidden_size % 256 == 0, "gemm2: hidden_size=%d must be a multiple of 256",
+  DS_REQUIRE(hidden_size % 8 == 0, "gemm2: hidden_size=%d must be a multiple of 8",
              hidden_size);
   DS_REQUIRE(intermediate_size % 8 == 0, "gemm2: intermediate_size must be a multiple of 8");
   if (total_slots == 0) return DS_OK;
@@ -849,7 +873,8 @@ int moe_gemm2_impl(const void* swiglu_out_bf16, const void* w2_bf16,
   pr.b_rows = static_cast<int64_t>(num_experts) * hidden_size;
   pr.offsets = expert_offsets;
   pr.groups = num_experts;
-  pr.n_tiles = hidden_size / 256;
+  pr.n_tiles = (hidden_size + 255) / 256;
+  pr.seg_cols = hidden_size;
   pr.b_rows_per_group = hidden_size;
   pr.b_tile_stride = 256;
   pr.b_half1_off = 128;
@@ -895,7 +920,7 @@ int ds_moe_gemm2(const void* swiglu_out_bf16, const void* w2_bf16,
 int ds_kv_upproj(const void* normed_kv_bf16, const void* weight_bf16, void* kv_up_bf16,
                  int rows, int kv_lora_rank, int out_dim, void* stream) {
   DS_REQUIRE(rows >= 0 && kv_lora_rank > 0 && out_dim > 0, "kv_upproj: bad shape");
-  DS_REQUIRE(out_dim % 256 == 0, "kv_upproj: out_dim=%d must be a multiple of 256", out_dim);
+  DS_REQUIRE(out_dim % 8 == 0, "kv_upproj: out_dim=%d must be a multiple of 8", out_dim);
   DS_REQUIRE(kv_lora_rank % 8 == 0, "kv_upproj: kv_lora_rank must be a multiple of 8");
   if (rows == 0) return DS_OK;
   ds::gemm::Problem pr{};
@@ -906,7 +931,8 @@ int ds_kv_upproj(const void* normed_kv_bf16, const void* weight_bf16, void* kv_u
   pr.b_rows = out_dim;
   pr.offsets = nullptr;
   pr.groups = 1;
-  pr.n_tiles = out_dim / 256;
+  pr.n_tiles = (out_dim + 255) / 256;
+  pr.seg_cols = out_dim;
   pr.b_rows_per_group = out_dim;
   pr.b_tile_stride = 256;
   pr.b_half1_off = 128;

@@ -82,6 +82,10 @@ struct Problem {
   int epilogue;
   const int32_t* out_row_map;  // optional: destination row for each A row
   int max_ctas = 0;            // grid cap (0 = one CTA per SM), leaves SMs to concurrent work
+  // output columns per segment when the last n-tile is partial (0: every tile is full).
+  // Paired layout (b_tile_stride 128: gate | up halves) = I; contiguous (256) = N.  A
+  // multiple of 8; columns past it are computed but not stored.
+  int seg_cols = 0;
   // router epilogue (epilogue == kRouter): B = split gate [256, K]; n_tiles = number of K
   // slices; slice s writes its raw accumulator columns [0, 192) as f32 to
   // logits_out + (s * a_rows + row) * 192

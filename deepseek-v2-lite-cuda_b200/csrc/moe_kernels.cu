@@ -701,7 +701,12 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
+// The drop-in op's arithmetic is the reference model's bf16 forward, F.silu(gate) * up
+// (src/reference/moe.py:19 on bf16 tensors, and the oracle of the reference's swiglu test):
+// silu in f32 rounded to bf16, then the product in f32 rounded to bf16.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __bfloat162float(__float2bfloat16_rn(g / (1.f + expf(-g)))) * u;
+}
 
 // K5: 16-byte vectors; each thread handles 8 gate and 8 up values of one row.  Index math
 // in 32 bits when the item count allows it (a 64-bit division per 16-byte item costs more

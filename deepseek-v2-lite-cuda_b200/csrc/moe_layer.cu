@@ -94,10 +94,10 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
   DS_REQUIRE(T >= 0, "moe_layer: num_tokens must be >= 0");
   DS_REQUIRE(E >= 1 && E <= ds::kMaxExperts, "moe_layer: num_experts must be in [1, 64]");
   DS_REQUIRE(K >= 1 && K <= ds::kMaxTopK && K <= E, "moe_layer: bad top_k");
-  DS_REQUIRE(H % 256 == 0, "moe_layer: hidden_size must be a multiple of 256");
-  DS_REQUIRE(I % 128 == 0, "moe_layer: intermediate_size must be a multiple of 128");
-  DS_REQUIRE(!has_shared || (Is % 128 == 0 && Is > 0),
-             "moe_layer: shared intermediate size must be a positive multiple of 128");
+  DS_REQUIRE(H > 0 && H % 8 == 0, "moe_layer: hidden_size must be a positive multiple of 8");
+  DS_REQUIRE(I > 0 && I % 8 == 0, "moe_layer: intermediate_size must be a positive multiple of 8");
+  DS_REQUIRE(!has_shared || (Is % 8 == 0 && Is > 0),
+             "moe_layer: shared intermediate size must be a positive multiple of 8");
   DS_REQUIRE((shared_w1_bf16 == nullptr) == (shared_w2_bf16 == nullptr),
              "moe_layer: give both shared expert weights or neither");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -159,7 +159,8 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
   g1.b_rows = static_cast<int64_t>(E) * 2 * I;
   g1.offsets = b.offsets;
   g1.groups = E;
-  g1.n_tiles = I / 128;
+  g1.n_tiles = (I + 127) / 128;
+  g1.seg_cols = I;
   g1.b_rows_per_group = 2 * I;
   g1.b_tile_stride = 128;
   g1.b_half1_off = I;
@@ -177,7 +178,8 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
     s1.b_rows = 2 * static_cast<int64_t>(Is);
     s1.offsets = nullptr;
     s1.groups = 1;
-    s1.n_tiles = Is / 128;
+    s1.n_tiles = (Is + 127) / 128;
+    s1.seg_cols = Is;
     s1.b_rows_per_group = 2 * Is;
     s1.b_tile_stride = 128;
     s1.b_half1_off = Is;
@@ -200,7 +202,8 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
   g2.b_rows = static_cast<int64_t>(E) * H;
   g2.offsets = b.offsets;
   g2.groups = E;
-  g2.n_tiles = H / 256;
+  g2.n_tiles = (H + 255) / 256;
+  g2.seg_cols = H;
   g2.b_rows_per_group = H;
   g2.b_tile_stride = 256;
   g2.b_half1_off = 128;
@@ -218,7 +221,8 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
     s2.b_rows = H;
     s2.offsets = nullptr;
     s2.groups = 1;
-    s2.n_tiles = H / 256;
+    s2.n_tiles = (H + 255) / 256;
+    s2.seg_cols = H;
     s2.b_rows_per_group = H;
     s2.b_tile_stride = 256;
     s2.b_half1_off = 128;

@@ -110,7 +110,8 @@ gemm::Problem mlp_gemm1(const void* A, int64_t rows, int H, const void* w1, int6
   p.b_rows = w1_rows;
   p.offsets = offsets;
   p.groups = groups;
-  p.n_tiles = I / 128;
+  p.n_tiles = (I + 127) / 128;
+  p.seg_cols = I;
   p.b_rows_per_group = 2 * I;
   p.b_tile_stride = 128;
   p.b_half1_off = I;
@@ -133,7 +134,8 @@ gemm::Problem mlp_gemm2(const void* h, int64_t rows, int I, const void* w2, int6
   p.b_rows = w2_rows;
   p.offsets = offsets;
   p.groups = groups;
-  p.n_tiles = H / 256;
+  p.n_tiles = (H + 255) / 256;
+  p.seg_cols = H;
   p.b_rows_per_group = H;
   p.b_tile_stride = 256;
   p.b_half1_off = 128;
@@ -198,8 +200,8 @@ int ds_moe_expert_mlp(const void* rows_bf16, int num_rows, const int32_t* group_
                       const int32_t* out_row_map, int max_ctas, void* stream) {
   const int H = hidden_size, I = intermediate_size;
   DS_REQUIRE(num_rows >= 0 && num_groups >= 1, "expert_mlp: bad shape");
-  DS_REQUIRE(H % 256 == 0 && I % 128 == 0,
-             "expert_mlp: hidden_size %% 256 and intermediate_size %% 128 must be 0");
+  DS_REQUIRE(H > 0 && I > 0 && H % 8 == 0 && I % 8 == 0,
+             "expert_mlp: hidden_size and intermediate_size must be positive multiples of 8");
   if (num_rows == 0) return DS_OK;
   DS_REQUIRE(rows_bf16 && group_offsets && packed_w1_bf16 && w2_bf16 && h_bf16 && out_bf16,
              "expert_mlp: null pointer");
@@ -220,8 +222,8 @@ int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16, const vo
                  int max_ctas, void* stream) {
   const int H = hidden_size, I = intermediate_size;
   DS_REQUIRE(num_rows >= 0, "dense_mlp: bad shape");
-  DS_REQUIRE(H % 256 == 0 && I % 128 == 0,
-             "dense_mlp: hidden_size %% 256 and intermediate_size %% 128 must be 0");
+  DS_REQUIRE(H > 0 && I > 0 && H % 8 == 0 && I % 8 == 0,
+             "dense_mlp: hidden_size and intermediate_size must be positive multiples of 8");
   if (num_rows == 0) return DS_OK;
   DS_REQUIRE(x_bf16 && w1_bf16 && w2_bf16 && h_bf16 && out_bf16, "dense_mlp: null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -238,7 +240,7 @@ int ds_dense_gemm1_swiglu(const void* x_bf16, int num_rows, const void* w1_bf16,
                           int hidden_size, int intermediate_size, void* h_bf16, int max_ctas,
                           void* stream) {
   DS_REQUIRE(num_rows >= 0 && hidden_size > 0 && hidden_size % 8 == 0 &&
-                 intermediate_size % 128 == 0 && intermediate_size > 0,
+                 intermediate_size % 8 == 0 && intermediate_size > 0,
              "dense_gemm1_swiglu: bad shape");
   if (num_rows == 0) return DS_OK;
   DS_REQUIRE(x_bf16 && w1_bf16 && h_bf16, "dense_gemm1_swiglu: null pointer");
@@ -252,7 +254,7 @@ int ds_dense_gemm1_swiglu(const void* x_bf16, int num_rows, const void* w1_bf16,
 int ds_dense_gemm2(const void* h_bf16, int num_rows, const void* w2_bf16, int intermediate_size,
                    int hidden_size, void* out_bf16, int max_ctas, void* stream) {
   DS_REQUIRE(num_rows >= 0 && intermediate_size > 0 && intermediate_size % 8 == 0 &&
-                 hidden_size % 256 == 0 && hidden_size > 0,
+                 hidden_size % 8 == 0 && hidden_size > 0,
              "dense_gemm2: bad shape");
   if (num_rows == 0) return DS_OK;
   DS_REQUIRE(h_bf16 && w2_bf16 && out_bf16, "dense_gemm2: null pointer");

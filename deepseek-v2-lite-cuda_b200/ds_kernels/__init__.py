@@ -455,10 +455,13 @@ def rope(q_pe: torch.Tensor, k_pe: torch.Tensor, cos: torch.Tensor,
 
     Mirrors rope_forward (src/kernels/mla/rope.cu:139-207) in a single launch; cos/sin are
     broadcast over heads by index instead of being expanded.  Returns [q_rot, k_rot].
+    Strided inputs (e.g. the q_pe slice of the q projection) are accepted and made
+    contiguous first; the reference rejects them.
     """
     for t in (q_pe, k_pe, cos, sin):
-        _require(t.is_cuda and t.is_contiguous(), "rope: all inputs must be contiguous CUDA tensors.")
+        _require(t.is_cuda, "rope: all inputs must be contiguous CUDA tensors.")
         _require(t.dtype == torch.bfloat16, "rope: all inputs must be bfloat16.")
+    q_pe, k_pe, cos, sin = (t.contiguous() for t in (q_pe, k_pe, cos, sin))
     _require(q_pe.dim() == 4, "rope: q_pe must be 4-D [bsz, heads, seq, rope_dim].")
     _require(k_pe.dim() == 4, "rope: k_pe must be 4-D [bsz, 1, seq, rope_dim].")
     _require(cos.dim() == 4, "rope: cos must be 4-D [bsz, 1, seq, rope_dim].")

@@ -128,7 +128,9 @@ DS_API int ds_moe_combine(const void* expert_output_bf16, const int32_t* token_m
 /* ---------------------------------------------------------------------------------------
  * K5 swiglu.  Replaces launch_swiglu (src/kernels/include/moe/swiglu.h:26-32,
  * src/kernels/moe/swiglu.cu:114-130) and swiglu_forward (swiglu.cu:142-170).
- * out[r, j] = bf16( silu(f32 in[r, j]) * f32 in[r, j + I] ).  I even. */
+ * out[r, j] = bf16( f32(bf16(silu(f32 in[r, j]))) * f32 in[r, j + I] ): the rounding
+ * sequence of the reference model's bf16 F.silu(gate) * up (src/reference/moe.py:19); the
+ * reference kernel rounds once (swiglu.cu:96-104), at most one bf16 ulp apart.  I even. */
 DS_API int ds_swiglu(const void* input_bf16, void* output_bf16, int total_tokens,
               int intermediate_size, void* stream);
 

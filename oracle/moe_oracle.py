@@ -158,6 +158,14 @@ def _mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
     return (g / (1.0 + torch.exp(-g)) * u) @ w2.t()
 
 
+def dense_mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor) -> torch.Tensor:
+    """Dense SwiGLU FFN in f32: down(silu(gate x) * up x), w1 = [gate; up] [2I, H], w2 [H, I].
+
+    The geometry of ExpertMLP (src/reference/moe.py:6-19); DeepSeek-V2-Lite's layer 0 uses it
+    with I = 10944 in place of the MoE block (src/reference/decoder_layer.py:8-9)."""
+    return _mlp(x.to(F32), w1.to(F32), w2.to(F32))
+
+
 def moe_forward(x: torch.Tensor, W: MoEWeights, top_k: int,
                 logits: Optional[torch.Tensor] = None, return_aux: bool = False):
     """f32 restatement of DeepSeekMoE.forward (src/reference/moe.py:77-109).

@@ -147,3 +147,62 @@ def test_kv_upproj_3d():
     out = ds().kv_upproj(x.cuda(), w.cuda())
     assert out.shape == (2, 32, 4096)
     _check(out.view(-1, 4096), oracle.kv_upproj(x.view(-1, 512), w))
+
+
+# ---- output widths that are not a multiple of the 256-column tile -------------------------
+# The last n-tile of a problem then holds fewer valid columns (the gate | up halves of GEMM1
+# each end at I; a plain tile ends at N).  Columns past the end are computed but never
+# stored: the values on both sides of the gate | up boundary and a guard region after the
+# output are checked.
+
+@pytest.mark.parametrize("I_", [72, 200, 1000])
+def test_gemm1_partial_last_n_tile(I_):
+    E_, H_ = 8, 256
+    g = torch.Generator().manual_seed(I_)
+    S = 777
+    a = (torch.rand(S, H_, generator=g) * 2 - 1).to(torch.bfloat16)
+    w1 = (torch.rand(E_, 2 * I_, H_, generator=g) * 0.1).to(torch.bfloat16)
+    off = round_robin_offsets(S, E_)
+    out = ds().moe_gemm1(a.cuda(), w1.cuda(), off.cuda())
+    assert out.shape == (S, 2 * I_)
+    ref = oracle.grouped_linear(a, w1, off)
+    _check(out, ref)
+    fused = ds().moe_gemm1_swiglu(a.cuda(), w1.cuda(), off.cuda())
+    assert fused.shape == (S, I_)
+    _check(fused, oracle.swiglu(ref))
+
+
+def _guarded_out(rows, cols):
+    """bf16 buffer of rows*cols elements followed by 4096 guard elements set to a sentinel."""
+    buf = torch.full((rows * cols + 4096,), 7.0, dtype=torch.bfloat16, device="cuda")
+    return buf
+
+
+@pytest.mark.parametrize("H_", [1000, 2056])
+def test_gemm2_partial_last_n_tile_stays_in_bounds(H_):
+    E_, I_ = 8, 200
+    g = torch.Generator().manual_seed(H_)
+    S = 555
+    a = (torch.rand(S, I_, generator=g) * 2 - 1).to(torch.bfloat16)
+    w2 = (torch.rand(E_, H_, I_, generator=g) * 0.1).to(torch.bfloat16)
+    off = round_robin_offsets(S, E_)
+    k = ds()
+    buf = _guarded_out(S, H_)
+    ad, wd, od = a.cuda(), w2.cuda(), off.cuda()
+    st = k.library().ds_moe_gemm2(ad.data_ptr(), wd.data_ptr(), od.data_ptr(), buf.data_ptr(), S,
+                                  E_, I_, H_, torch.cuda.current_stream().cuda_stream)
+    assert st == 0, k.library().ds_last_error().decode()
+    torch.cuda.synchronize()
+    assert torch.all(buf[S * H_:] == 7.0)
+    _check(buf[:S * H_].view(S, H_), oracle.grouped_linear(a, w2, off))
+
+
+@pytest.mark.parametrize("out_dim", [1000, 4104])
+def test_kv_upproj_any_width(out_dim):
+    g = torch.Generator().manual_seed(out_dim)
+    rows = 300
+    x = (torch.randn(rows, 512, generator=g) * 0.1).to(torch.bfloat16)
+    w = (torch.randn(out_dim, 512, generator=g) * 0.02).to(torch.bfloat16)
+    out = ds().kv_upproj(x.cuda(), w.cuda())
+    assert out.shape == (rows, out_dim)
+    _check(out, oracle.kv_upproj(x, w))

@@ -270,6 +270,19 @@ def test_swiglu(rows):
     assert_bf16_close(out, ref, 1e-2)
 
 
+@pytest.mark.parametrize("rows", [1, 256, 4099])
+def test_swiglu_equals_the_bf16_torch_expression(rows):
+    # The drop-in rounds silu(gate) to bf16 before the product, as F.silu(gate) * up does on
+    # bf16 tensors (the reference model's expert, src/reference/moe.py:19, and its swiglu
+    # test's oracle, tests/test_swiglu_kernel.py): bit for bit.
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(rows)
+    x = (torch.rand(rows, 2 * 1408, generator=g) * 4 - 2).to(torch.bfloat16).cuda()
+    out = ds().swiglu(x)
+    ref = F.silu(x[:, :1408]) * x[:, 1408:]
+    assert torch.equal(out, ref)
+
+
 def test_swiglu_odd_width_and_empty():
     x = (torch.rand(5, 2 * 6) * 4 - 2).to(torch.bfloat16)
     out = ds().swiglu(x.cuda())
