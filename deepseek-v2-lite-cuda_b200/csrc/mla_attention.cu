@@ -1,0 +1,673 @@
+// MLA attention core of DeepSeek-V2-Lite prefill (the causal scaled-dot-product attention of
+// src/reference/mla.py:355-378 with 192-wide q/k heads = 128 nope + 64 RoPE, 128-wide v
+// heads), and the whole MLA forward around it (src/reference/mla.py:295-393):
+//
+//   qkv   = x @ [W_q; W_kv_a]^T            one tcgen05 GEMM: [M, heads*192 + 512 + 64]
+//   lat   = RMSNorm(qkv[:, heads*192 : +512])
+//   kv    = lat @ W_kv_b^T                  [M, heads*(128 + 128)]  (k_nope | v per head)
+//   RoPE in place on the 64-wide q_pe of every head and on k_pe inside qkv
+//   V^T   = transpose of the v halves       [(b*heads + h)*128 + d, S]
+//   o     = causal softmax(q k^T * scale) v  (this file's attention kernel), [M, heads*128]
+//   out   = o @ W_o^T                        [M, hidden]
+//
+// Attention kernel (one CTA per (batch, head, 128-row q tile), 192 threads):
+//   warp 0       TMA producer: the Q tile once (3 boxes of 128 rows x 64 columns: nope,
+//                nope, rope, straight out of qkv), then per 128-row kv block the K tile
+//                (k_nope 2 boxes from kv, k_pe 1 box from qkv, shared by the heads) and the
+//                V^T tile (2 boxes), into a 2-stage ring (128-byte swizzle).
+//   warp 1       MMA issuer (one thread): S_j = Q K_j^T (M=128, N=128, K=192) into one of two
+//                TMEM buffers, then O += P_{j-1} V_{j-1} (M=128, N=128, K=128) with P read
+//                from TMEM (the softmax warps write it over S) and V^T from shared memory.
+//   warps 2-5    softmax, one q row per thread: row max of S_j (log2 domain), P_j =
+//                2^(s - m) rounded to bf16 into the S buffer's first 64 columns, running sum,
+//                and the rescale of the O accumulator in TMEM by 2^(m_old - m_new) (after
+//                the previous P V has landed; skipped by a warp whose rows kept their max);
+//                at the end O / l -> bf16 -> out.
+// Blocks are ordered longest first (the last q tiles see the most kv blocks).  Every wait is
+// bounded; a wait that runs out sets the device status and the kernel drains and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace ds {
+namespace attn {
+namespace {
+
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int kThreads = 192;
+constexpr uint32_t CHUNK = 128 * 64 * 2;  // one 128-row x 64-column bf16 box: 16 KiB
+constexpr uint32_t Q_BYTES = 3 * CHUNK;
+constexpr uint32_t K_BYTES = 3 * CHUNK;
+constexpr uint32_t V_BYTES = 2 * CHUNK;
+constexpr int STAGES = 2;
+constexpr uint32_t kTileBytes = Q_BYTES + STAGES * (K_BYTES + V_BYTES);  // 208 KiB
+constexpr uint32_t kTailBytes = 256;
+constexpr size_t kSmemBytes = 1024 + kTileBytes + kTailBytes;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSCol0 = 0, kSCol1 = 128, kOCol = 256;
+constexpr long long kTimeoutCycles = 4000000000LL;
+
+struct Params {
+  int batch, seq, heads;
+  int krope_col;        // column of k_pe in qkv
+  float scale_log2;     // softmax scale * log2(e)
+  __nv_bfloat16* out;   // [batch*seq, heads*128]
+  int ldo;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b, float& ra, float& rb) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 f = __bfloat1622float2(h);
+  ra = f.x;
+  rb = f.y;
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    mla_attention_kernel(const __grid_constant__ CUtensorMap tmQ,   // qkv [B*S, ldq]
+                         const __grid_constant__ CUtensorMap tmKV,  // kv [B*S, heads*256]
+                         const __grid_constant__ CUtensorMap tmVt,  // V^T [B*heads*128, S]
+                         const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sQ = ptx::smem_u32(smem);
+  const uint32_t sK = sQ + Q_BYTES;
+  const uint32_t sV = sK + STAGES * K_BYTES;
+  uint8_t* tail = smem + kTileBytes;
+  const uint32_t bar0 = ptx::smem_u32(tail);
+  // barriers (8 bytes each): q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2],
+  // p_ready, o_done, drain
+  const uint32_t q_full = bar0;
+  const uint32_t k_full0 = bar0 + 8, k_empty0 = bar0 + 24;
+  const uint32_t v_full0 = bar0 + 40, v_empty0 = bar0 + 56;
+  const uint32_t s_full0 = bar0 + 72;
+  const uint32_t p_ready = bar0 + 88, o_done = bar0 + 96, drain_bar = bar0 + 104;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 112);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 116);
+  volatile int* never_flag = reinterpret_cast<volatile int*>(tail + 120);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ntq = (p.seq + BQ - 1) / BQ;
+  const int BH = p.batch * p.heads;
+  const int qt = ntq - 1 - static_cast<int>(blockIdx.x) / BH;  // longest tiles first
+  const int bh = static_cast<int>(blockIdx.x) % BH;
+  const int b = bh / p.heads, h = bh - (bh / p.heads) * p.heads;
+  const int q0 = qt * BQ;
+  const int nblk = qt + 1;  // causal: kv blocks 0..qt
+  const int row0 = b * p.seq;
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(k_full0 + 8u * s, 1);
+      ptx::mbar_init(k_empty0 + 8u * s, 1);
+      ptx::mbar_init(v_full0 + 8u * s, 1);
+      ptx::mbar_init(v_empty0 + 8u * s, 1);
+      ptx::mbar_init(s_full0 + 8u * s, 1);
+    }
+    ptx::mbar_init(p_ready, 4);
+    ptx::mbar_init(o_done, 1);
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    *never_flag = 0;
+    ptx::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmQ);
+    ptx::prefetch_tmap(&tmKV);
+    ptx::prefetch_tmap(&tmVt);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      ptx::mbar_arrive_expect_tx(q_full, Q_BYTES);
+      for (int c = 0; c < 3; ++c)
+        ptx::tma_load_2d(sQ + c * CHUNK, &tmQ, q_full, h * 192 + c * 64, row0 + q0);
+      int issued = 0;
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!ptx::mbar_wait(k_empty0 + 8u * st, ph ^ 1u, abort_flag, p.status, kTimeoutCycles,
+                            DS_ERR_TIMEOUT))
+          break;
+        const uint32_t kf = k_full0 + 8u * st;
+        ptx::mbar_arrive_expect_tx(kf, K_BYTES);
+        const uint32_t kd = sK + st * K_BYTES;
+        ptx::tma_load_2d(kd, &tmKV, kf, h * 256, row0 + j * BKV);
+        ptx::tma_load_2d(kd + CHUNK, &tmKV, kf, h * 256 + 64, row0 + j * BKV);
+        ptx::tma_load_2d(kd + 2 * CHUNK, &tmQ, kf, p.krope_col, row0 + j * BKV);
+        if (!ptx::mbar_wait(v_empty0 + 8u * st, ph ^ 1u, abort_flag, p.status, kTimeoutCycles,
+                            DS_ERR_TIMEOUT)) {
+          issued = 2 * j + 1;
+          break;
+        }
+        const uint32_t vf = v_full0 + 8u * st;
+        ptx::mbar_arrive_expect_tx(vf, V_BYTES);
+        const uint32_t vd = sV + st * V_BYTES;
+        ptx::tma_load_2d(vd, &tmVt, vf, j * BKV, bh * 128);
+        ptx::tma_load_2d(vd + CHUNK, &tmVt, vf, j * BKV + 64, bh * 128);
+        issued = 2 * j + 2;
+      }
+      // every load issued here lands before the CTA exits: the last phase of each barrier
+      ptx::mbar_wait(q_full, 0, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
+      for (int n = issued - 1; n >= 0 && n >= issued - 4; --n) {
+        const int j = n >> 1;
+        const uint32_t bar = (n & 1) ? v_full0 + 8u * (j & 1) : k_full0 + 8u * (j & 1);
+        ptx::mbar_wait(bar, (j >> 1) & 1, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_bf16_f32(128, 128);
+      bool ok = ptx::mbar_wait(q_full, 0, abort_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
+      ptx::tc_fence_after();
+      for (int j = 0; ok && j <= nblk; ++j) {
+        if (j < nblk) {
+          const int st = j & 1;
+          if (!ptx::mbar_wait(k_full0 + 8u * st, (j >> 1) & 1, abort_flag, p.status,
+                              kTimeoutCycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t d = tmem + (st ? kSCol1 : kSCol0);
+          const uint32_t kb = sK + st * K_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 12; ++kk) {
+            const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+            ptx::umma_f16(d, ptx::sw128_kmajor_desc(sQ + off), ptx::sw128_kmajor_desc(kb + off),
+                          idesc, kk > 0 ? 1u : 0u);
+          }
+          ptx::umma_commit(k_empty0 + 8u * st);
+          ptx::umma_commit(s_full0 + 8u * st);
+        }
+        if (j >= 1) {
+          const int jp = j - 1;
+          const int st = jp & 1;
+          if (!ptx::mbar_wait(p_ready, jp & 1, abort_flag, p.status, kTimeoutCycles,
+                              DS_ERR_TIMEOUT) ||
+              !ptx::mbar_wait(v_full0 + 8u * st, (jp >> 1) & 1, abort_flag, p.status,
+                              kTimeoutCycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t pa = tmem + (st ? kSCol1 : kSCol0);
+          const uint32_t vb = sV + st * V_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+            ptx::umma_f16_ts(tmem + kOCol, pa + kk * 8, ptx::sw128_kmajor_desc(vb + off), idesc,
+                             (jp > 0 || kk > 0) ? 1u : 0u);
+          }
+          ptx::umma_commit(v_empty0 + 8u * st);
+          ptx::umma_commit(o_done);
+        }
+      }
+      // no MMA may still be running when TMEM is released
+      ptx::umma_commit(drain_bar);
+      ptx::mbar_wait(drain_bar, 0, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (warps 2-5)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // q row within the tile (= TMEM lane)
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t ob = tmem + lane_off + kOCol;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int st = j & 1;
+      int w_ok = 1;
+      if (lane == 0)
+        w_ok = ptx::mbar_wait(s_full0 + 8u * st, (j >> 1) & 1, abort_flag, p.status,
+                              kTimeoutCycles, DS_ERR_TIMEOUT)
+                   ? 1
+                   : 0;
+      if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const uint32_t sb = tmem + lane_off + (st ? kSCol1 : kSCol0);
+      const bool diag = j == qt;
+      // pass 1: row max in the log2 domain (masked columns: kv > q on the diagonal block)
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        ptx::tmem_ld32(sb + c * 32, v);
+        ptx::tmem_wait_ld(v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float s = __uint_as_float(v[i]) * p.scale_log2;
+          if (!(diag && c * 32 + i > r)) mx = fmaxf(mx, s);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = (m == m_new) ? 1.f : ptx::ex2(m - m_new);
+      // pass 2: P = 2^(s - m_new) as bf16 into the first 64 columns of this S buffer (chunk c
+      // of S is read before chunk c of P overwrites columns that were already consumed)
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        ptx::tmem_ld32(sb + c * 32, v);
+        ptx::tmem_wait_ld(v);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = c * 32 + 2 * i;
+          const float s0 = __uint_as_float(v[2 * i]) * p.scale_log2;
+          const float s1 = __uint_as_float(v[2 * i + 1]) * p.scale_log2;
+          const float p0 = (diag && col > r) ? 0.f : ptx::ex2(s0 - m_new);
+          const float p1 = (diag && col + 1 > r) ? 0.f : ptx::ex2(s1 - m_new);
+          float r0, r1;
+          w[i] = pack_bf16(p0, p1, r0, r1);
+          sum += r0 + r1;
+        }
+        ptx::tmem_st16(sb + c * 16, w);
+      }
+      l = l * alpha + sum;
+      // O *= alpha once the previous P V has landed; a warp whose rows all kept their max
+      // leaves O alone (the P V of block j cannot start before this warp's p_ready arrival,
+      // so o_done is at most one phase ahead of the phase waited for here)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        int o_ok = 1;
+        if (lane == 0)
+          o_ok = ptx::mbar_wait(o_done, (j - 1) & 1, abort_flag, p.status, kTimeoutCycles,
+                                DS_ERR_TIMEOUT)
+                     ? 1
+                     : 0;
+        if (!__shfl_sync(0xffffffffu, o_ok, 0)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          ptx::tmem_ld32(ob + c * 32, v);
+          ptx::tmem_wait_ld(v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          ptx::tmem_st32(ob + c * 32, v);
+        }
+      }
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(p_ready);
+      m = m_new;
+    }
+    if (ok) {
+      int o_ok = 1;
+      if (lane == 0)
+        o_ok = ptx::mbar_wait(o_done, (nblk - 1) & 1, abort_flag, p.status, kTimeoutCycles,
+                              DS_ERR_TIMEOUT)
+                   ? 1
+                   : 0;
+      if (__shfl_sync(0xffffffffu, o_ok, 0)) {
+        ptx::tc_fence_after();
+        const float inv = 1.f / l;
+        const bool valid = q0 + r < p.seq;
+        __nv_bfloat16* dst =
+            p.out + static_cast<int64_t>(row0 + q0 + r) * p.ldo + static_cast<int64_t>(h) * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          ptx::tmem_ld32(ob + c * 32, v);
+          ptx::tmem_wait_ld(v);
+          if (valid) {
+            uint32_t w[16];
+            float r0, r1;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              w[i] = pack_bf16(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv,
+                               r0, r1);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// V^T: kv [B*S, heads*256] (per head 128 k_nope then 128 v) -> vt [(b*heads + h)*128 + d, S].
+// A block moves a 64-token x 64-dim tile through shared memory: 16-byte loads along d,
+// 16-byte stores along the sequence.
+__global__ void __launch_bounds__(256)
+    v_transpose_kernel(const __nv_bfloat16* __restrict__ kv, int ldkv,
+                       __nv_bfloat16* __restrict__ vt, int seq, int heads) {
+  __shared__ __nv_bfloat16 tile[64][64 + 8];
+  const int s0 = blockIdx.x * 64;
+  const int d0 = blockIdx.y * 64;
+  const int bh = blockIdx.z;
+  const int b = bh / heads, h = bh - b * heads;
+  const int t = threadIdx.x;
+  // load: 64 tokens x 8 uint4 (64 dims)
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int idx = it * 256 + t;
+    const int ts = idx >> 3, c = idx & 7;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (s0 + ts < seq)
+      v = __ldg(reinterpret_cast<const uint4*>(
+          kv + static_cast<int64_t>(b * seq + s0 + ts) * ldkv + h * 256 + 128 + d0 + c * 8));
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tile[c * 8 + k][ts] = e[k];
+  }
+  __syncthreads();
+  // store: 64 dims x 8 uint4 (64 tokens)
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int idx = it * 256 + t;
+    const int dd = idx >> 3, c = idx & 7;
+    if (s0 + c * 8 < seq) {
+      uint4 v;
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) e[k] = tile[dd][c * 8 + k];
+      *reinterpret_cast<uint4*>(vt + (static_cast<int64_t>(bh) * 128 + d0 + dd) * seq + s0 + c * 8) = v;
+    }
+  }
+}
+
+// RoPE in place on qkv [rows, ld]: the 64-wide q_pe of each head (columns h*192 + 128 ..) and
+// k_pe (columns kcol ..), one thread per (token, head or k), all 64 elements of its row (so
+// the in-place update never races): the interleave -> half transform and the rotation of
+// src/reference/mla.py:176-206, out[k] = x[2k] cos[k] - x[2k+1] sin[k],
+// out[32+k] = x[2k+1] cos[32+k] + x[2k] sin[32+k], one bf16 rounding.  cos/sin: bf16
+// [positions, 64] tables at position pos[row] (or row % seq when pos is null).
+__global__ void __launch_bounds__(256)
+    mla_rope_inplace_kernel(__nv_bfloat16* __restrict__ qkv, int ld, int64_t rows, int seq,
+                            int heads, int kcol, const __nv_bfloat16* __restrict__ cos_t,
+                            const __nv_bfloat16* __restrict__ sin_t,
+                            const int32_t* __restrict__ pos) {
+  const int per_row = heads + 1;
+  const int64_t total = rows * per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / per_row;
+    const int hh = static_cast<int>(i - row * per_row);
+    const int col = hh < heads ? hh * 192 + 128 : kcol;
+    uint4* x4 = reinterpret_cast<uint4*>(qkv + row * ld + col);
+    const int64_t pr = pos != nullptr ? __ldg(pos + row) : row % seq;
+    const uint4* c4 = reinterpret_cast<const uint4*>(cos_t + pr * 64);
+    const uint4* s4 = reinterpret_cast<const uint4*>(sin_t + pr * 64);
+    uint4 xv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) xv[k] = x4[k];
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(xv);
+    uint4 ov[8];
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(ov);
+#pragma unroll
+    for (int k8 = 0; k8 < 4; ++k8) {
+      const uint4 cl = __ldg(c4 + k8), ch = __ldg(c4 + 4 + k8);
+      const uint4 sl = __ldg(s4 + k8), sh = __ldg(s4 + 4 + k8);
+      const __nv_bfloat16* clp = reinterpret_cast<const __nv_bfloat16*>(&cl);
+      const __nv_bfloat16* chp = reinterpret_cast<const __nv_bfloat16*>(&ch);
+      const __nv_bfloat16* slp = reinterpret_cast<const __nv_bfloat16*>(&sl);
+      const __nv_bfloat16* shp = reinterpret_cast<const __nv_bfloat16*>(&sh);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int k = k8 * 8 + q;
+        const float a = __bfloat162float(xe[2 * k]), bb = __bfloat162float(xe[2 * k + 1]);
+        oe[k] = __float2bfloat16_rn(a * __bfloat162float(clp[q]) - bb * __bfloat162float(slp[q]));
+        oe[32 + k] =
+            __float2bfloat16_rn(bb * __bfloat162float(chp[q]) + a * __bfloat162float(shp[q]));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x4[k] = ov[k];
+  }
+}
+
+// ---- host ------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+bool g_attr_set[64] = {};
+std::mutex g_attr_mutex;
+
+int tmap_2d(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld) {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  if (g_encode == nullptr) return fail(DS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64u, 128u};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld", (int)r,
+                (long long)rows, (long long)cols);
+  return DS_OK;
+}
+
+}  // namespace
+
+// Attention over qkv (RoPE already applied in place) and kv; vt = V^T scratch
+// [batch*heads*128, seq]; out [batch*seq, heads*128].
+int launch_attention(const void* qkv, int ldq, const void* kv, void* vt, void* out, int batch,
+                     int seq, int heads, float softmax_scale, cudaStream_t s) {
+  DS_REQUIRE(batch >= 1 && seq >= 1 && heads >= 1, "mla_attention: bad shape");
+  DS_REQUIRE(seq % 8 == 0, "mla_attention: seq_len must be a multiple of 8");
+  DS_REQUIRE(ldq % 8 == 0 && ldq >= heads * 192 + 512 + 64, "mla_attention: bad qkv stride");
+  DS_REQUIRE(aligned16(qkv) && aligned16(kv) && aligned16(vt) && aligned16(out),
+             "mla_attention: buffers must be 16-byte aligned");
+  DeviceInfo di;
+  DS_TRY(device_info(&di));
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (!g_attr_set[di.device]) {
+      DS_CUDA(cudaFuncSetAttribute(mla_attention_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(kSmemBytes)));
+      g_attr_set[di.device] = true;
+    }
+  }
+  const int64_t M = static_cast<int64_t>(batch) * seq;
+  {
+    dim3 grid((seq + 63) / 64, 2, batch * heads);
+    v_transpose_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(kv), heads * 256,
+                                            static_cast<__nv_bfloat16*>(vt), seq, heads);
+    DS_LAUNCH_CHECK("v_transpose_kernel");
+  }
+  CUtensorMap tq, tkv, tvt;
+  DS_TRY(tmap_2d(&tq, qkv, M, ldq, ldq));
+  DS_TRY(tmap_2d(&tkv, kv, M, static_cast<int64_t>(heads) * 256, static_cast<int64_t>(heads) * 256));
+  DS_TRY(tmap_2d(&tvt, vt, static_cast<int64_t>(batch) * heads * 128, seq, seq));
+  Params p{};
+  p.batch = batch;
+  p.seq = seq;
+  p.heads = heads;
+  p.krope_col = heads * 192 + 512;
+  p.scale_log2 = static_cast<float>(static_cast<double>(softmax_scale) * 1.4426950408889634);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = heads * 128;
+  p.status = device_status_ptr();
+  if (p.status == nullptr) return fail(DS_ERR_CUDA, "device status word unavailable");
+  const int ntq = (seq + BQ - 1) / BQ;
+  mla_attention_kernel<<<ntq * batch * heads, kThreads, kSmemBytes, s>>>(tq, tkv, tvt, p);
+  DS_LAUNCH_CHECK("mla_attention_kernel");
+  return DS_OK;
+}
+
+int launch_mla_rope(void* qkv, int ldq, int64_t rows, int seq, int heads, const void* cos_t,
+                    const void* sin_t, const int32_t* pos, cudaStream_t s) {
+  DeviceInfo di;
+  DS_TRY(device_info(&di));
+  const int64_t items = rows * (heads + 1);
+  int64_t grid = (items + 255) / 256;
+  if (grid > di.num_sms * 16) grid = di.num_sms * 16;
+  mla_rope_inplace_kernel<<<static_cast<int>(grid > 0 ? grid : 1), 256, 0, s>>>(
+      static_cast<__nv_bfloat16*>(qkv), ldq, rows, seq, heads, heads * 192 + 512,
+      static_cast<const __nv_bfloat16*>(cos_t), static_cast<const __nv_bfloat16*>(sin_t), pos);
+  DS_LAUNCH_CHECK("mla_rope_inplace_kernel");
+  return DS_OK;
+}
+
+}  // namespace attn
+}  // namespace ds
+
+// ---- C ABI ------------------------------------------------------------------------------------
+namespace {
+
+struct MlaBuffers {
+  void* qkv;  // bf16 [M, ldq]
+  void* lat;  // bf16 [M, 512]
+  void* kv;   // bf16 [M, heads*256]
+  void* vt;   // bf16 [batch*heads*128, seq]
+  void* o;    // bf16 [M, heads*128]
+};
+
+constexpr int kLatent = 512;
+
+int mla_ldq(int heads) { return heads * 192 + kLatent + 64; }
+
+size_t carve_mla(ds::Carve& c, MlaBuffers* b, int batch, int seq, int heads) {
+  const size_t M = static_cast<size_t>(batch) * seq;
+  MlaBuffers x{};
+  x.qkv = c.take<__nv_bfloat16>(M * mla_ldq(heads));
+  x.lat = c.take<__nv_bfloat16>(M * kLatent);
+  x.kv = c.take<__nv_bfloat16>(M * heads * 256);
+  x.vt = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * heads * 128 * seq);
+  x.o = c.take<__nv_bfloat16>(M * heads * 128);
+  if (b) *b = x;
+  return ds::align_up(c.used, 256);
+}
+
+ds::gemm::Problem dense_problem(const void* A, int64_t rows, int K, const void* B, int N,
+                                void* out) {
+  ds::gemm::Problem p{};
+  p.A = A;
+  p.a_rows = rows;
+  p.K = K;
+  p.B = B;
+  p.b_rows = N;
+  p.offsets = nullptr;
+  p.groups = 1;
+  p.n_tiles = (N + 255) / 256;
+  p.seg_cols = N;
+  p.b_rows_per_group = N;
+  p.b_tile_stride = 256;
+  p.b_half1_off = 128;
+  p.weight_group_mod = 1;
+  p.out = out;
+  p.ldo = N;
+  p.epilogue = ds::gemm::kPlain;
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ds_mla_attention_workspace_size(int batch, int seq, int heads) {
+  return ds::align_up(static_cast<size_t>(batch) * heads * 128 * seq * 2, 256);
+}
+
+int ds_mla_attention(const void* qkv_bf16, int qkv_ld, const void* kv_bf16, void* out_bf16,
+                     int batch, int seq, int heads, float softmax_scale, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  DS_REQUIRE(batch >= 0 && seq >= 0 && heads >= 1, "mla_attention: bad shape");
+  if (batch == 0 || seq == 0) return DS_OK;
+  DS_REQUIRE(qkv_bf16 && kv_bf16 && out_bf16 && workspace, "mla_attention: null pointer");
+  DS_REQUIRE(workspace_bytes >= ds_mla_attention_workspace_size(batch, seq, heads),
+             "mla_attention: workspace needs %zu bytes",
+             ds_mla_attention_workspace_size(batch, seq, heads));
+  return ds::attn::launch_attention(qkv_bf16, qkv_ld, kv_bf16, workspace, out_bf16, batch, seq,
+                                    heads, softmax_scale, static_cast<cudaStream_t>(stream));
+}
+
+size_t ds_mla_forward_workspace_size(int batch, int seq, int hidden, int heads) {
+  (void)hidden;
+  ds::Carve c(nullptr, 0);
+  return carve_mla(c, nullptr, batch, seq, heads);
+}
+
+int ds_mla_forward(const void* x_bf16, const void* w_qkv_a_bf16, const float* kv_norm_weight,
+                   const void* w_kv_b_bf16, const void* w_o_bf16, const void* cos_bf16,
+                   const void* sin_bf16, const int32_t* positions, void* out_bf16, int batch,
+                   int seq, int hidden, int heads, float eps, float softmax_scale,
+                   void* workspace, size_t workspace_bytes, void** events, void* stream) {
+  DS_REQUIRE(batch >= 0 && seq >= 0 && heads >= 1 && hidden > 0, "mla_forward: bad shape");
+  DS_REQUIRE(hidden % 8 == 0, "mla_forward: hidden_size must be a multiple of 8");
+  DS_REQUIRE(seq % 8 == 0 || batch * seq == 0, "mla_forward: seq_len must be a multiple of 8");
+  if (batch == 0 || seq == 0) return DS_OK;
+  DS_REQUIRE(x_bf16 && w_qkv_a_bf16 && kv_norm_weight && w_kv_b_bf16 && w_o_bf16 && cos_bf16 &&
+                 sin_bf16 && out_bf16,
+             "mla_forward: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto mark = [&](int i) -> int {
+    if (events != nullptr && events[i] != nullptr)
+      DS_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s));
+    return DS_OK;
+  };
+  ds::Carve c(workspace, workspace_bytes);
+  MlaBuffers b;
+  carve_mla(c, &b, batch, seq, heads);
+  if (!c.ok()) return ds::fail(DS_ERR_WORKSPACE, "mla_forward: workspace needs %zu bytes", c.used);
+  const int64_t M = static_cast<int64_t>(batch) * seq;
+  const int ldq = mla_ldq(heads);
+  DS_TRY(mark(0));
+  // q_proj | kv_a_proj_with_mqa in one GEMM: [M, heads*192 + 512 + 64]
+  DS_TRY(ds::gemm::launch(dense_problem(x_bf16, M, hidden, w_qkv_a_bf16, ldq, b.qkv), s));
+  DS_TRY(mark(1));
+  DS_TRY(ds_rms_norm_strided(static_cast<const __nv_bfloat16*>(b.qkv) + heads * 192, ldq,
+                             kv_norm_weight, b.lat, kLatent, static_cast<int>(M), kLatent, eps,
+                             stream));
+  DS_TRY(mark(2));
+  DS_TRY(ds::gemm::launch(dense_problem(b.lat, M, kLatent, w_kv_b_bf16, heads * 256, b.kv), s));
+  DS_TRY(mark(3));
+  DS_TRY(ds::attn::launch_mla_rope(b.qkv, ldq, M, seq, heads, cos_bf16, sin_bf16, positions, s));
+  DS_TRY(mark(4));
+  DS_TRY(ds::attn::launch_attention(b.qkv, ldq, b.kv, b.vt, b.o, batch, seq, heads,
+                                    softmax_scale, s));
+  DS_TRY(mark(5));
+  DS_TRY(ds::gemm::launch(dense_problem(b.o, M, heads * 128, w_o_bf16, hidden, out_bf16), s));
+  DS_TRY(mark(6));
+  return DS_OK;
+}
+
+}  // extern "C"

@@ -31,6 +31,7 @@ DS_ERR_CUDA = 3
 DS_ERR_TIMEOUT = 4
 DS_ERR_WORKSPACE = 5
 LAYER_NUM_EVENTS = 9
+MLA_NUM_EVENTS = 7
 EP_NUM_EVENTS = 7
 EP_IPC_HANDLE_BYTES = 64
 
@@ -64,6 +65,11 @@ SIGNATURES = {
     "ds_kv_upproj": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "ds_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "ds_moe_layer_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "ds_mla_attention_workspace_size": (_sz, [_i, _i, _i]),
+    "ds_mla_attention": (_i, [_vp, _i, _vp, _vp, _i, _i, _i, _f, _vp, _sz, _vp]),
+    "ds_mla_forward_workspace_size": (_sz, [_i, _i, _i, _i]),
+    "ds_mla_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _f,
+                            _vp, _sz, _vp, _vp]),
     "ds_moe_layer_workspace_routing": (_i, [_i, _i, _i, _i, _i, _i, ctypes.POINTER(_sz),
                                             ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
     "ds_moe_layer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
@@ -560,6 +566,89 @@ def moe_layer_forward(router_logits: torch.Tensor, x: torch.Tensor, packed_w1: t
                                          _ptr(shared_w1), _ptr(shared_w2), _ptr(out), T, H, E,
                                          top_k, I, Is, _ptr(workspace), workspace.numel(), ev,
                                          _stream(x)), "moe_layer_forward")
+    return out
+
+
+def mla_attention(qkv: torch.Tensor, kv: torch.Tensor, batch: int, seq: int, heads: int,
+                  softmax_scale: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal MLA attention core (src/reference/mla.py:355-378) on the tcgen05 tensor cores.
+
+    qkv bf16 [batch*seq, ld]: per token the heads' q (192 each: 128 nope, then 64 already
+    RoPE-rotated), the 512-wide latent, then the rotated 64-wide k_pe; kv bf16
+    [batch*seq, heads*256]: per head 128 k_nope then 128 v.  Returns bf16
+    [batch*seq, heads*128] (head h in columns h*128 ..)."""
+    _check_tensor(qkv, "qkv", torch.bfloat16, "bfloat16", 2, "[batch*seq, ld]")
+    _check_tensor(kv, "kv", torch.bfloat16, "bfloat16", 2, "[batch*seq, heads*256]")
+    _require(qkv.shape[0] == batch * seq and kv.shape[0] == batch * seq,
+             "mla_attention: qkv and kv must hold batch*seq rows")
+    _require(kv.shape[1] == heads * 256, "mla_attention: kv must be [batch*seq, heads*256]")
+    if out is None:
+        out = torch.empty((batch * seq, heads * 128), dtype=torch.bfloat16, device=qkv.device)
+    if batch * seq == 0:
+        return out
+    need = int(_lib.ds_mla_attention_workspace_size(batch, seq, heads))
+    ws = _workspace(need, qkv.device)
+    with _on_device(qkv):
+        _check(_lib.ds_mla_attention(_ptr(qkv), qkv.shape[1], _ptr(kv), _ptr(out), batch, seq,
+                                     heads, float(softmax_scale), _ptr(ws), need, _stream(qkv)),
+               "mla_attention")
+    return out
+
+
+def mla_forward_workspace_size(batch: int, seq: int, hidden: int, heads: int) -> int:
+    return int(_lib.ds_mla_forward_workspace_size(batch, seq, hidden, heads))
+
+
+def mla_forward(hidden_states: torch.Tensor, w_qkv_a: torch.Tensor,
+                kv_norm_weight: torch.Tensor, w_kv_b: torch.Tensor, w_o: torch.Tensor,
+                cos: torch.Tensor, sin: torch.Tensor, softmax_scale: float, heads: int,
+                position_ids: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                workspace: Optional[torch.Tensor] = None,
+                events: Optional[Sequence[torch.cuda.Event]] = None) -> torch.Tensor:
+    """The whole MLA forward of DeepSeekMLA (src/reference/mla.py:295-393) in one C call:
+    hidden_states bf16 [batch, seq, hidden] -> bf16 [batch, seq, hidden].  w_qkv_a =
+    cat(q_proj.weight, kv_a_proj_with_mqa.weight) bf16 [heads*192 + 576, hidden];
+    kv_norm_weight f32 [512]; w_kv_b bf16 [heads*256, 512]; w_o bf16 [hidden, heads*128];
+    cos/sin bf16 [positions, 64]; position_ids int [batch, seq] or None (0..seq-1)."""
+    _require(hidden_states.is_cuda and hidden_states.dtype == torch.bfloat16
+             and hidden_states.dim() == 3, "mla_forward: hidden_states must be CUDA bf16 [b, s, h]")
+    x = hidden_states.contiguous()
+    B, S, Hd = x.shape
+    for t, name in ((w_qkv_a, "w_qkv_a"), (w_kv_b, "w_kv_b"), (w_o, "w_o"), (cos, "cos"),
+                    (sin, "sin")):
+        _require(t.is_cuda and t.is_contiguous() and t.dtype == torch.bfloat16,
+                 f"mla_forward: {name} must be a contiguous CUDA bf16 tensor")
+    _require(tuple(w_qkv_a.shape) == (heads * 192 + 576, Hd), "mla_forward: w_qkv_a shape")
+    _require(tuple(w_kv_b.shape) == (heads * 256, 512), "mla_forward: w_kv_b shape")
+    _require(tuple(w_o.shape) == (Hd, heads * 128), "mla_forward: w_o shape")
+    _require(cos.dim() == 2 and cos.shape[1] == 64 and tuple(sin.shape) == tuple(cos.shape),
+             "mla_forward: cos/sin must be [positions, 64]")
+    nw = kv_norm_weight.detach().float().contiguous()
+    pos = None
+    if position_ids is not None:
+        pos = position_ids.to(device=x.device, dtype=torch.int32).expand(B, S).contiguous()
+        _require(int(pos.max()) < cos.shape[0] and int(pos.min()) >= 0,
+                 "mla_forward: position_ids outside the cos/sin tables")
+    else:
+        _require(S <= cos.shape[0], "mla_forward: seq_len exceeds the cos/sin tables")
+    out = torch.empty((B, S, Hd), dtype=torch.bfloat16, device=x.device)
+    if B * S == 0:
+        return out
+    need = mla_forward_workspace_size(B, S, Hd, heads)
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(need, x.device)
+    ev = None
+    if events is not None:
+        _require(len(events) == MLA_NUM_EVENTS, f"events must hold {MLA_NUM_EVENTS} events")
+        st = torch.cuda.current_stream(x.device)
+        for e in events:
+            e.record(st)
+        ev = (ctypes.c_void_p * MLA_NUM_EVENTS)(*[e.cuda_event for e in events])
+    with _on_device(x):
+        _check(_lib.ds_mla_forward(_ptr(x), _ptr(w_qkv_a), _ptr(nw), _ptr(w_kv_b), _ptr(w_o),
+                                   _ptr(cos), _ptr(sin), _ptr(pos), _ptr(out), B, S, Hd, heads,
+                                   float(eps), float(softmax_scale), _ptr(workspace),
+                                   workspace.numel(), ev, _stream(x)), "mla_forward")
     return out
 
 

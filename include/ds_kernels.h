@@ -204,6 +204,39 @@ DS_API int ds_rope(const void* q_pe_bf16, const void* k_pe_bf16, const void* cos
             int seq, int rope_dim, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * MLA attention (config 3): the causal attention core and the whole MLA forward of
+ * DeepSeekMLA (src/reference/mla.py:295-393: q_proj, kv_a_proj_with_mqa, kv_a_layernorm,
+ * kv_b_proj, YaRN/plain RoPE on the 64-wide parts, softmax(q k^T * scale) v with 192-wide
+ * q/k and 128-wide v heads, o_proj).  The reference has no kernel for this part (its
+ * src/kernels/mla/ covers rms_norm, kv_upproj and rope only).
+ *
+ * ds_mla_attention: qkv bf16 [batch*seq, qkv_ld] holds per token the heads' q (192 each:
+ * 128 nope then 64 RoPE-rotated), then the 512-wide latent, then the 64-wide rotated k_pe;
+ * kv bf16 [batch*seq, heads*256] holds per head 128 k_nope then 128 v; out bf16
+ * [batch*seq, heads*128] (head h in columns h*128 ..).  Causal; seq % 8 == 0; workspace =
+ * ds_mla_attention_workspace_size (the transposed v). */
+DS_API size_t ds_mla_attention_workspace_size(int batch, int seq, int heads);
+DS_API int ds_mla_attention(const void* qkv_bf16, int qkv_ld, const void* kv_bf16,
+                            void* out_bf16, int batch, int seq, int heads, float softmax_scale,
+                            void* workspace, size_t workspace_bytes, void* stream);
+/* ds_mla_forward: x bf16 [batch*seq, hidden]; w_qkv_a bf16 [heads*192 + 576, hidden] =
+ * q_proj.weight rows then kv_a_proj_with_mqa.weight rows; kv_norm_weight f32 [512];
+ * w_kv_b bf16 [heads*256, 512]; w_o bf16 [hidden, heads*128]; cos/sin bf16 [positions, 64]
+ * tables (the module's cos_cached/sin_cached); positions int32 [batch*seq] or NULL
+ * (position = index within the sequence); out bf16 [batch*seq, hidden].  `events`: NULL or
+ * DS_MLA_NUM_EVENTS handles recorded before the first kernel and after each phase (qkv
+ * projection, latent RMSNorm, kv_b projection, RoPE, attention, o_proj). */
+#define DS_MLA_NUM_EVENTS 7
+DS_API size_t ds_mla_forward_workspace_size(int batch, int seq, int hidden, int heads);
+DS_API int ds_mla_forward(const void* x_bf16, const void* w_qkv_a_bf16,
+                          const float* kv_norm_weight, const void* w_kv_b_bf16,
+                          const void* w_o_bf16, const void* cos_bf16, const void* sin_bf16,
+                          const int32_t* positions, void* out_bf16, int batch, int seq,
+                          int hidden, int heads, float eps, float softmax_scale,
+                          void* workspace, size_t workspace_bytes, void** events,
+                          void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Fused MoE layer (new, additive; the pipeline of src/kernels/moe_fused.py:118-154 plus the
  * shared expert of src/reference/moe.py:72-74,106-107 that the reference pipeline drops).
  * router_logits f32 [T, E] (x @ gate^T in f32), x bf16 [T, H], packed_w1 bf16 [E, 2I, H],

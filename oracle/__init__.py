@@ -14,4 +14,7 @@ from .moe_oracle import (  # noqa: F401
     route, expert_counts, expert_offsets, dispatch, combine, swiglu, grouped_linear,
     moe_forward, MoEWeights, make_moe_weights, zipf_logits, dense_mlp,
 )
-from .mla_oracle import rms_norm, rms_norm_residual, rope, yarn_cos_sin, kv_upproj  # noqa: F401
+from .mla_oracle import (  # noqa: F401
+    rms_norm, rms_norm_residual, rope, yarn_cos_sin, kv_upproj, mla_attention, mla_forward,
+    mla_forward_rows,
+)

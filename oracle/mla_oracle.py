@@ -8,6 +8,10 @@ yarn_cos_sin: the YaRN tables of src/reference/mla.py:66-173 (correction range, 
 rope       : src/reference/mla.py:176-206 (interleave -> half transform, then
              q*cos + rotate_half(q)*sin).
 kv_upproj  : F.linear(normed, W) in f32 (src/kernels/mla/kv_upproj.cu:77-119).
+mla_attention: the causal scaled-dot-product step of src/reference/mla.py:355-378.
+mla_forward: the whole DeepSeekMLA.forward of src/reference/mla.py:295-393 in f32 (q_proj,
+             kv_a_proj_with_mqa, kv_a_layernorm, kv_b_proj, RoPE on the 64-wide parts,
+             causal attention over 192-wide q/k and 128-wide v, o_proj).
 """
 from __future__ import annotations
 
@@ -78,3 +82,76 @@ def rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor,
 
 def kv_upproj(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return x.to(F32) @ w.to(F32).t()
+
+
+def mla_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                  softmax_scale: float) -> torch.Tensor:
+    """q, k [b, h, s, dqk], v [b, h, s, dv] -> [b, h, s, dv] in f32: causal softmax(q k^T *
+    scale) v with the upper triangle masked to -inf (src/reference/mla.py:355-378)."""
+    qf, kf, vf = q.to(F32), k.to(F32), v.to(F32)
+    s_len = qf.shape[2]
+    w = torch.matmul(qf, kf.transpose(2, 3)) * softmax_scale
+    mask = torch.triu(torch.full((s_len, s_len), float("-inf")), diagonal=1)
+    w = torch.softmax(w + mask, dim=-1)
+    return torch.matmul(w, vf)
+
+
+def mla_forward(x: torch.Tensor, w_q: torch.Tensor, w_kva: torch.Tensor, norm_w: torch.Tensor,
+                w_kvb: torch.Tensor, w_o: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                softmax_scale: float, heads: int, eps: float = 1e-6,
+                return_aux: bool = False):
+    """DeepSeekMLA.forward (src/reference/mla.py:295-393) in f32 with positions 0..s-1.
+
+    x [b, s, hidden]; w_q [heads*192, hidden]; w_kva [512+64, hidden]; norm_w [512];
+    w_kvb [heads*(128+128), 512]; w_o [hidden, heads*128]; cos/sin [>= s, 64]."""
+    b, s_len, _ = x.shape
+    xf = x.to(F32)
+    q = (xf @ w_q.to(F32).t()).view(b, s_len, heads, 192).transpose(1, 2)
+    q_nope, q_pe = q[..., :128], q[..., 128:]
+    ckv = xf @ w_kva.to(F32).t()
+    latent, k_pe = ckv[..., :512], ckv[..., 512:]
+    k_pe = k_pe.view(b, s_len, 1, 64).transpose(1, 2)
+    kv = (rms_norm(latent, norm_w, eps) @ w_kvb.to(F32).t()).view(b, s_len, heads, 256)
+    kv = kv.transpose(1, 2)
+    k_nope, v = kv[..., :128], kv[..., 128:]
+    c = cos[:s_len].to(F32)[None, None]
+    sn = sin[:s_len].to(F32)[None, None]
+    q_pe, k_pe = rope(q_pe, k_pe, c, sn)
+    qs = torch.cat([q_nope, q_pe], dim=-1)
+    ks = torch.cat([k_nope, k_pe.expand(b, heads, s_len, 64)], dim=-1)
+    o = mla_attention(qs, ks, v, softmax_scale)
+    attn = o.transpose(1, 2).reshape(b, s_len, heads * 128)
+    out = attn @ w_o.to(F32).t()
+    if return_aux:
+        return out, {"query_states": qs, "key_states": ks, "value": v, "attn": attn}
+    return out
+
+
+def mla_forward_rows(x: torch.Tensor, w_q: torch.Tensor, w_kva: torch.Tensor,
+                     norm_w: torch.Tensor, w_kvb: torch.Tensor, w_o: torch.Tensor,
+                     cos: torch.Tensor, sin: torch.Tensor, softmax_scale: float, heads: int,
+                     rows: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """mla_forward restricted to the output rows `rows` (token indices, the same for every
+    sequence): keys and values of every token, queries and attention only for those rows, so
+    full-length sequences stay cheap to check.  Returns f32 [b, len(rows), hidden]."""
+    b, s_len, _ = x.shape
+    xf = x.to(F32)
+    rows = rows.to(torch.long)
+    R = rows.numel()
+    q = (xf[:, rows] @ w_q.to(F32).t()).view(b, R, heads, 192).transpose(1, 2)
+    q_nope, q_pe = q[..., :128], q[..., 128:]
+    ckv = xf @ w_kva.to(F32).t()
+    latent, k_pe = ckv[..., :512], ckv[..., 512:]
+    k_pe = k_pe.view(b, s_len, 1, 64).transpose(1, 2)
+    kv = (rms_norm(latent, norm_w, eps) @ w_kvb.to(F32).t()).view(b, s_len, heads, 256)
+    kv = kv.transpose(1, 2)
+    k_nope, v = kv[..., :128], kv[..., 128:]
+    _, k_pe = rope(k_pe, k_pe, cos[:s_len].to(F32)[None, None], sin[:s_len].to(F32)[None, None])
+    q_pe, _ = rope(q_pe, q_pe[:, :1], cos[rows].to(F32)[None, None], sin[rows].to(F32)[None, None])
+    qs = torch.cat([q_nope, q_pe], dim=-1)
+    ks = torch.cat([k_nope, k_pe.expand(b, heads, s_len, 64)], dim=-1)
+    w = torch.matmul(qs, ks.transpose(2, 3)) * softmax_scale
+    masked = torch.arange(s_len)[None, :] > rows[:, None]
+    w = torch.softmax(w.masked_fill(masked[None, None], float("-inf")), dim=-1)
+    attn = torch.matmul(w, v).transpose(1, 2).reshape(b, R, heads * 128)
+    return attn @ w_o.to(F32).t()

@@ -94,6 +94,36 @@ def mla_fixture(ref_mla, name, bsz, seq, seed, scaling_factor):
     print(f"wrote {name}.pt")
 
 
+def mla_forward_fixture(ref_mla, name, bsz, seq, hidden, heads, seed, scaling_factor,
+                        w_std=0.05):
+    """The whole DeepSeekMLA.forward (src/reference/mla.py:295-393) at reduced width (the
+    per-head sizes are the real 128 + 64 / 128 and the 512-wide latent), f32 on the CPU."""
+    torch.manual_seed(seed)
+    m = ref_mla.DeepSeekMLA(hidden_size=hidden, num_heads=heads,
+                            rope_scaling_factor=scaling_factor).float().eval()
+    with torch.no_grad():
+        for name_, p in m.named_parameters():
+            if "layernorm" in name_:
+                p.copy_(torch.rand_like(p) + 0.5)
+            else:
+                p.normal_(0.0, w_std)
+    x = torch.randn(bsz, seq, hidden)
+    with torch.no_grad():
+        out = m(x)
+        cos, sin = m.rotary_emb(x, seq_len=seq)
+    torch.save({
+        "bsz": bsz, "seq": seq, "hidden": hidden, "heads": heads,
+        "scaling_factor": scaling_factor, "softmax_scale": float(m.softmax_scale),
+        "x": x, "out": out, "cos": cos.clone(), "sin": sin.clone(),
+        "w_q": m.q_proj.weight.detach().clone(),
+        "w_kva": m.kv_a_proj_with_mqa.weight.detach().clone(),
+        "norm_w": m.kv_a_layernorm.weight.detach().clone(),
+        "w_kvb": m.kv_b_proj.weight.detach().clone(),
+        "w_o": m.o_proj.weight.detach().clone(),
+    }, os.path.join(HERE, f"{name}.pt"))
+    print(f"wrote {name}.pt  out[0,0,:4]={out[0, 0, :4].tolist()}")
+
+
 def decoder_glue_fixture(ref_mla, name, rows, H, seed):
     """The residual add + pre-norm of src/reference/decoder_layer.py:123-139 on bf16 hidden
     states, with the reference's RMSNorm module (src/reference/mla.py:53-64)."""
@@ -164,6 +194,10 @@ def main():
     mla_fixture(ref_mla, "mla_yarn40", bsz=2, seq=16, seed=3, scaling_factor=40.0)
     mla_fixture(ref_mla, "mla_plain", bsz=1, seq=32, seed=4, scaling_factor=1.0)
     decoder_glue_fixture(ref_mla, "decoder_glue", rows=12, H=256, seed=5)
+    mla_forward_fixture(ref_mla, "mla_forward_yarn40", bsz=2, seq=40, hidden=128, heads=2,
+                        seed=6, scaling_factor=40.0)
+    mla_forward_fixture(ref_mla, "mla_forward_plain", bsz=1, seq=48, hidden=128, heads=3,
+                        seed=7, scaling_factor=1.0)
     known_answers()
 
 

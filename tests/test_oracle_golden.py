@@ -2,6 +2,7 @@
 tests/golden/make_golden.py produced by running the reference's own PyTorch code, and the
 known answers of the reference's kernel tests.  CPU only."""
 import os
+import pytest
 
 import torch
 
@@ -128,3 +129,26 @@ def test_decoder_glue_residual_rms_norm():
     # the reference rounds the normalised row to bf16 before the f32 weight (mla.py:64); the
     # oracle keeps it in f32 (one rounding, as the kernels do): within a bf16 half-ulp
     torch.testing.assert_close(normed, fx["normed"].float(), atol=1e-6, rtol=2.0 ** -8)
+
+
+@pytest.mark.parametrize("name", ["mla_forward_yarn40.pt", "mla_forward_plain.pt"])
+def test_mla_forward_matches_the_reference_module(name):
+    # the whole DeepSeekMLA.forward (projections, latent RMSNorm, RoPE, causal attention with
+    # 192-wide q/k and 128-wide v, o_proj), reference module run in f32 on the CPU
+    fx = _load(name)
+    cos, sin = oracle.yarn_cos_sin(fx["seq"], scaling_factor=fx["scaling_factor"])
+    torch.testing.assert_close(cos, fx["cos"], atol=1e-6, rtol=0)
+    out = oracle.mla_forward(fx["x"], fx["w_q"], fx["w_kva"], fx["norm_w"], fx["w_kvb"],
+                             fx["w_o"], fx["cos"], fx["sin"], fx["softmax_scale"], fx["heads"])
+    torch.testing.assert_close(out, fx["out"], atol=2e-5, rtol=2e-5)
+
+
+def test_mla_forward_rows_agrees_with_the_full_forward():
+    # the row-restricted oracle used to check full-length sequences on the GPU
+    fx = _load("mla_forward_yarn40.pt")
+    args = (fx["x"], fx["w_q"], fx["w_kva"], fx["norm_w"], fx["w_kvb"], fx["w_o"], fx["cos"],
+            fx["sin"], fx["softmax_scale"], fx["heads"])
+    full = oracle.mla_forward(*args)
+    rows = torch.tensor([0, 1, 7, 20, 39])
+    torch.testing.assert_close(oracle.mla_forward_rows(*args, rows), full[:, rows],
+                               atol=1e-5, rtol=1e-5)
