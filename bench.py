@@ -538,11 +538,71 @@ def run_ours(args, rank, world, local_rank):
                         "phases_ms": {k: round(v, 4) for k, v in weak[1].items()}}
     if base is not None:
         line["cpu_baseline"] = base
+    if world == 1 and not args.no_cfg3:
+        line["cfg3_mla"] = mla_cfg3(dev)
     print(json.dumps(line), flush=True)
     if not par.get("ok", True):
         raise SystemExit("parity check failed: " + json.dumps(par))
     if args.op_report and world == 1:
         op_report(args.op_report, dev)
+
+
+def mla_cfg3(dev, steps=10, warmup=3):
+    """BASELINE config 3 (MLA prefill: batch 4, seq 4096, hidden 2048, 16 heads, plain RoPE
+    theta 10000) through ds_mla_forward, with CUDA events at the phase boundaries; seeded
+    N(0,1) activations and N(0, 0.02^2) weights.  Returns the per-phase times and the
+    attention kernel's and whole forward's throughput (causal flops: the lower triangle)."""
+    import ds_kernels
+    B, S, Hd, heads = 4, 4096, 2048, 16
+    M = B * S
+    g = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn(B, S, Hd, generator=g, device=dev).to(torch.bfloat16)
+
+    def w(*shape):
+        return (torch.randn(*shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+    w_qkv_a = w(heads * 192 + 576, Hd)
+    norm_w = torch.rand(512, generator=g, device=dev) + 0.5
+    w_kvb, w_o = w(heads * 256, 512), w(Hd, heads * 128)
+    t = torch.arange(S, dtype=torch.float32, device=dev)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, 64, 2, dtype=torch.float32, device=dev) / 64))
+    ang = torch.outer(t, inv)
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    scale = 192 ** -0.5
+    ws = torch.empty(ds_kernels.mla_forward_workspace_size(B, S, Hd, heads), dtype=torch.uint8,
+                     device=dev)
+    names = ["qkv_a_proj", "kv_norm", "kv_b_proj", "rope", "attention", "o_proj"]
+
+    def step(events=None):
+        return ds_kernels.mla_forward(x, w_qkv_a, norm_w, w_kvb, w_o, cos, sin, scale, heads,
+                                      workspace=ws, events=events)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+          for _ in range(steps)]
+    for i in range(steps):
+        step(ev[i])
+    torch.cuda.synchronize()
+    ph = {n: sum(ev[i][k].elapsed_time(ev[i][k + 1]) for i in range(steps)) / steps
+          for k, n in enumerate(names)}
+    total = sum(ph.values())
+    pk = peaks()
+    attn_fl = float(B * heads) * S * S * (192 + 128)  # 2 * (S^2 / 2) * (192 + 128) per head
+    fl = {"qkv_a_proj": 2.0 * M * Hd * (heads * 192 + 576), "kv_b_proj": 2.0 * M * 512 * heads * 256,
+          "attention": attn_fl, "o_proj": 2.0 * M * heads * 128 * Hd}
+    kern = {n: {"us": round(ph[n] * 1e3, 1), "TFLOP/s": round(f / (ph[n] / 1e3) / 1e12, 1),
+                "frac": round(f / (ph[n] / 1e3) / 1e12 / pk["bf16"], 4)} for n, f in fl.items()}
+    for n, nb in (("kv_norm", 4 * M * 512), ("rope", 4 * M * (heads + 1) * 64)):
+        kern[n] = {"us": round(ph[n] * 1e3, 1), "GB/s": round(nb / (ph[n] / 1e3) / 1e9, 1),
+                   "frac": round(nb / (ph[n] / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
+    return {"workload": "cfg3: MLA prefill, batch 4 x seq 4096, hidden 2048, 16 heads, causal",
+            "ms_per_forward": round(total, 4),
+            "tokens_per_s": round(M / (total / 1e3), 1),
+            "TFLOP/s": round(sum(fl.values()) / (total / 1e3) / 1e12, 1),
+            "attention_note": "flops of the causal lower triangle: B*heads*S^2*(192+128)",
+            "kernels": kern, "peak_source": f"{pk['source']} bf16 burst / HBM copy"}
 
 
 L2_BYTES = 126 * 2 ** 20
@@ -726,6 +786,10 @@ def kernel_case(name, reps=2):
         g1 = torch.randn(16384 * K // 2, 2 * I, device=dev).to(torch.bfloat16)  # as op_report
         for _ in range(reps):
             ds_kernels.swiglu(g1)
+    elif name == "mla":
+        # config 3 MLA forward: forward 1 warms up, the next ones can be captured
+        for _ in range(reps + 1):
+            mla_cfg3(dev, steps=1, warmup=0)
     elif name in ("rms_norm", "rope", "kv_upproj"):
         M = 4 * 4096
         lat = torch.randn(M, 512, device=dev).to(torch.bfloat16)
@@ -757,12 +821,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--no-cfg3", action="store_true",
+                    help="skip the config-3 MLA forward measurement (cfg3_mla key)")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel transport for --gpus > 1")
     ap.add_argument("--op-report", default=None)
     ap.add_argument("--kernel-case", default=None,
                     choices=["layer", "gemm1", "gemm2", "dispatch", "routing", "router", "combine", "swiglu",
-                             "rms_norm", "rope", "kv_upproj"],
+                             "rms_norm", "rope", "kv_upproj", "mla"],
                     help="run one kernel at its BASELINE size twice (profiling) and exit")
     args = ap.parse_args()
     if args.kernel_case:

@@ -11,19 +11,23 @@
 //   out   = o @ W_o^T                        [M, hidden]
 //
 // Attention kernel (one CTA per (batch, head, 128-row q tile), 192 threads):
-//   warp 0       TMA producer: the Q tile once (3 boxes of 128 rows x 64 columns: nope,
-//                nope, rope, straight out of qkv), then per 128-row kv block the K tile
-//                (k_nope 2 boxes from kv, k_pe 1 box from qkv, shared by the heads) and the
-//                V^T tile (2 boxes), into a 2-stage ring (128-byte swizzle).
+//   warp 0       TMA producer of Q and K: the Q tile once (3 boxes of 128 rows x 64
+//                columns: nope, nope, rope, straight out of qkv), then per 128-row kv block
+//                the K tile (k_nope 2 boxes from kv, k_pe 1 box from qkv, shared by the
+//                heads) into a 2-stage ring (128-byte swizzle).
+//   warp 10      TMA producer of the V^T tiles (2 boxes per block, 2-stage ring), so a K
+//                load never waits behind a V stage.
 //   warp 1       MMA issuer (one thread): S_j = Q K_j^T (M=128, N=128, K=192) into one of two
 //                TMEM buffers, then O += P_{j-1} V_{j-1} (M=128, N=128, K=128) with P read
 //                from TMEM (the softmax warps write it over S) and V^T from shared memory.
-//   warps 2-5    softmax, one q row per thread: row max of S_j (log2 domain), P_j =
-//                2^(s - m) rounded to bf16 into the S buffer's first 64 columns, running sum,
-//                and the rescale of the O accumulator in TMEM by 2^(m_old - m_new) (after
-//                the previous P V has landed; skipped by a warp whose rows kept their max);
-//                at the end O / l -> bf16 -> out.
-// Blocks are ordered longest first (the last q tiles see the most kv blocks).  Every wait is
+//   warps 2-9    softmax, two warps per 32-row TMEM quarter, each thread one row's 64 of the
+//                128 S values of a block (the pair exchanges row maxima through shared
+//                memory): row max (log2 domain), P_j = 2^(s*scale - m) rounded to bf16 into
+//                the S buffer's first 64 columns, running sum; m is raised (and the O
+//                accumulator in TMEM rescaled by 2^(m_old - m_new)) only when the row max
+//                grows by more than 2^8, so most blocks leave O alone; at the end O / l ->
+//                bf16 -> out.
+// CTAs are ordered (batch, head)-major, longest q tile first within a head.  Every wait is
 // bounded; a wait that runs out sets the device status and the kernel drains and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -41,14 +45,14 @@ namespace {
 
 constexpr int BQ = 128;
 constexpr int BKV = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;  // K producer, MMA, 8 softmax warps, V producer
 constexpr uint32_t CHUNK = 128 * 64 * 2;  // one 128-row x 64-column bf16 box: 16 KiB
 constexpr uint32_t Q_BYTES = 3 * CHUNK;
 constexpr uint32_t K_BYTES = 3 * CHUNK;
 constexpr uint32_t V_BYTES = 2 * CHUNK;
 constexpr int STAGES = 2;
 constexpr uint32_t kTileBytes = Q_BYTES + STAGES * (K_BYTES + V_BYTES);  // 208 KiB
-constexpr uint32_t kTailBytes = 256;
+constexpr uint32_t kTailBytes = 256 + 6 * 128 * 4;  // barriers, then the softmax pairs' exchange
 constexpr size_t kSmemBytes = 1024 + kTileBytes + kTailBytes;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSCol0 = 0, kSCol1 = 128, kOCol = 256;
@@ -85,22 +89,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* tail = smem + kTileBytes;
   const uint32_t bar0 = ptx::smem_u32(tail);
   // barriers (8 bytes each): q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2],
-  // p_ready, o_done, drain
+  // p_ready[2], o_done, drain.  p_ready alternates by block: the softmax warps may finish
+  // block j+1 before the MMA thread has seen block j's phase, and a barrier that moved two
+  // phases past its waiter would read as not yet complete.
   const uint32_t q_full = bar0;
   const uint32_t k_full0 = bar0 + 8, k_empty0 = bar0 + 24;
   const uint32_t v_full0 = bar0 + 40, v_empty0 = bar0 + 56;
   const uint32_t s_full0 = bar0 + 72;
-  const uint32_t p_ready = bar0 + 88, o_done = bar0 + 96, drain_bar = bar0 + 104;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 112);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 116);
-  volatile int* never_flag = reinterpret_cast<volatile int*>(tail + 120);
+  const uint32_t p_ready0 = bar0 + 88, o_done = bar0 + 104, drain_bar = bar0 + 112;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 120);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 124);
+  volatile int* never_flag = reinterpret_cast<volatile int*>(tail + 128);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int ntq = (p.seq + BQ - 1) / BQ;
-  const int BH = p.batch * p.heads;
-  const int qt = ntq - 1 - static_cast<int>(blockIdx.x) / BH;  // longest tiles first
-  const int bh = static_cast<int>(blockIdx.x) % BH;
+  // (batch, head)-major: the q tiles of one head run together and share its K / V tiles
+  // through L2; within a head the longest tiles (most kv blocks) start first
+  const int bh = static_cast<int>(blockIdx.x) / ntq;
+  const int qt = ntq - 1 - (static_cast<int>(blockIdx.x) - bh * ntq);
   const int b = bh / p.heads, h = bh - (bh / p.heads) * p.heads;
   const int q0 = qt * BQ;
   const int nblk = qt + 1;  // causal: kv blocks 0..qt
@@ -114,8 +121,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(v_full0 + 8u * s, 1);
       ptx::mbar_init(v_empty0 + 8u * s, 1);
       ptx::mbar_init(s_full0 + 8u * s, 1);
+      ptx::mbar_init(p_ready0 + 8u * s, 8);
     }
-    ptx::mbar_init(p_ready, 4);
     ptx::mbar_init(o_done, 1);
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -136,44 +143,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 10) {
+    // ------------------------------------------------------------------ TMA producers
+    // warp 0: Q, then the K tiles (each waits only for the S MMA of the block two back);
+    // warp 10: the V^T tiles (each waits for the P V of the block two back)
     if (lane == 0) {
-      ptx::mbar_arrive_expect_tx(q_full, Q_BYTES);
-      for (int c = 0; c < 3; ++c)
-        ptx::tma_load_2d(sQ + c * CHUNK, &tmQ, q_full, h * 192 + c * 64, row0 + q0);
+      const bool is_k = warp == 0;
+      if (is_k) {
+        ptx::mbar_arrive_expect_tx(q_full, Q_BYTES);
+        for (int c = 0; c < 3; ++c)
+          ptx::tma_load_2d(sQ + c * CHUNK, &tmQ, q_full, h * 192 + c * 64, row0 + q0);
+      }
+      const uint32_t full0 = is_k ? k_full0 : v_full0;
+      const uint32_t empty0 = is_k ? k_empty0 : v_empty0;
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
         const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!ptx::mbar_wait(k_empty0 + 8u * st, ph ^ 1u, abort_flag, p.status, kTimeoutCycles,
-                            DS_ERR_TIMEOUT))
+        if (!ptx::mbar_wait(empty0 + 8u * st, ((j >> 1) & 1) ^ 1u, abort_flag, p.status,
+                            kTimeoutCycles, DS_ERR_TIMEOUT))
           break;
-        const uint32_t kf = k_full0 + 8u * st;
-        ptx::mbar_arrive_expect_tx(kf, K_BYTES);
-        const uint32_t kd = sK + st * K_BYTES;
-        ptx::tma_load_2d(kd, &tmKV, kf, h * 256, row0 + j * BKV);
-        ptx::tma_load_2d(kd + CHUNK, &tmKV, kf, h * 256 + 64, row0 + j * BKV);
-        ptx::tma_load_2d(kd + 2 * CHUNK, &tmQ, kf, p.krope_col, row0 + j * BKV);
-        if (!ptx::mbar_wait(v_empty0 + 8u * st, ph ^ 1u, abort_flag, p.status, kTimeoutCycles,
-                            DS_ERR_TIMEOUT)) {
-          issued = 2 * j + 1;
-          break;
+        const uint32_t fb = full0 + 8u * st;
+        if (is_k) {
+          ptx::mbar_arrive_expect_tx(fb, K_BYTES);
+          const uint32_t kd = sK + st * K_BYTES;
+          ptx::tma_load_2d(kd, &tmKV, fb, h * 256, row0 + j * BKV);
+          ptx::tma_load_2d(kd + CHUNK, &tmKV, fb, h * 256 + 64, row0 + j * BKV);
+          ptx::tma_load_2d(kd + 2 * CHUNK, &tmQ, fb, p.krope_col, row0 + j * BKV);
+        } else {
+          ptx::mbar_arrive_expect_tx(fb, V_BYTES);
+          const uint32_t vd = sV + st * V_BYTES;
+          ptx::tma_load_2d(vd, &tmVt, fb, j * BKV, bh * 128);
+          ptx::tma_load_2d(vd + CHUNK, &tmVt, fb, j * BKV + 64, bh * 128);
         }
-        const uint32_t vf = v_full0 + 8u * st;
-        ptx::mbar_arrive_expect_tx(vf, V_BYTES);
-        const uint32_t vd = sV + st * V_BYTES;
-        ptx::tma_load_2d(vd, &tmVt, vf, j * BKV, bh * 128);
-        ptx::tma_load_2d(vd + CHUNK, &tmVt, vf, j * BKV + 64, bh * 128);
-        issued = 2 * j + 2;
+        issued = j + 1;
       }
-      // every load issued here lands before the CTA exits: the last phase of each barrier
-      ptx::mbar_wait(q_full, 0, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
-      for (int n = issued - 1; n >= 0 && n >= issued - 4; --n) {
-        const int j = n >> 1;
-        const uint32_t bar = (n & 1) ? v_full0 + 8u * (j & 1) : k_full0 + 8u * (j & 1);
-        ptx::mbar_wait(bar, (j >> 1) & 1, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
-      }
+      // every load issued here lands before the CTA exits: the last phase of each stage
+      if (is_k)
+        ptx::mbar_wait(q_full, 0, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
+      for (int j = issued - 1; j >= 0 && j >= issued - 2; --j)
+        ptx::mbar_wait(full0 + 8u * (j & 1), (j >> 1) & 1, never_flag, p.status,
+                       kTimeoutCycles, DS_ERR_TIMEOUT);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -204,8 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= 1) {
           const int jp = j - 1;
           const int st = jp & 1;
-          if (!ptx::mbar_wait(p_ready, jp & 1, abort_flag, p.status, kTimeoutCycles,
-                              DS_ERR_TIMEOUT) ||
+          if (!ptx::mbar_wait(p_ready0 + 8u * st, (jp >> 1) & 1, abort_flag, p.status,
+                              kTimeoutCycles, DS_ERR_TIMEOUT) ||
               !ptx::mbar_wait(v_full0 + 8u * st, (jp >> 1) & 1, abort_flag, p.status,
                               kTimeoutCycles, DS_ERR_TIMEOUT)) {
             ok = false;
@@ -229,11 +238,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_wait(drain_bar, 0, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
     }
   } else {
-    // ------------------------------------------------------------------ softmax (warps 2-5)
+    // ------------------------------------------------------------------ softmax (warps 2-9)
+    // Two warps per 32-row TMEM quarter: `half` 0 takes S columns 0..63 (and O columns
+    // 0..63), half 1 columns 64..127.  Each thread holds one row's 64 values; the pair
+    // exchanges its partial row max through shared memory (named barrier 1 + quarter, 64
+    // threads), which also orders both warps' S loads before either writes P over S.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // q row within the tile (= TMEM lane)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t ob = tmem + lane_off + kOCol;
+    const uint32_t ob = tmem + lane_off + kOCol + half * 64;
+    float* red = reinterpret_cast<float*>(tail + 256);  // [2 parity][2 half][128 rows]
+    const uint32_t pair_bar = 1 + quarter;
+    // m: the max the row's P values are taken against (log2 domain).  It is raised only when
+    // the row max grows by more than kLazy (so P <= 2^kLazy), which leaves O untouched on
+    // most blocks; l and O always refer to the same m, and the final O / l is exact.
+    constexpr float kLazy = 8.f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
@@ -244,83 +264,105 @@ __global__ void __launch_bounds__(kThreads, 1)
                               kTimeoutCycles, DS_ERR_TIMEOUT)
                    ? 1
                    : 0;
-      if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
+      // the partner warp must not block in the named barrier below: the pair agrees first
+      w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+      red[(st * 2 + half) * 128 + r] = w_ok ? 0.f : 1.f;
+      ptx::named_bar_sync(pair_bar, 64);
+      const bool pair_ok = w_ok && red[(st * 2 + (half ^ 1)) * 128 + r] == 0.f;
+      ptx::named_bar_sync(pair_bar, 64);
+      if (!pair_ok) {
         ok = false;
         break;
       }
       ptx::tc_fence_after();
       const uint32_t sb = tmem + lane_off + (st ? kSCol1 : kSCol0);
-      const bool diag = j == qt;
-      // pass 1: row max in the log2 domain (masked columns: kv > q on the diagonal block)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        ptx::tmem_ld32(sb + c * 32, v);
-        ptx::tmem_wait_ld(v);
+      uint32_t v[2][32];
+      ptx::tmem_ld32(sb + half * 64, v[0]);
+      ptx::tmem_ld32(sb + half * 64 + 32, v[1]);
+      ptx::tmem_wait_ld2(v[0], v[1]);
+      if (j == qt) {  // diagonal block: kv column > q row is masked
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float s = __uint_as_float(v[i]) * p.scale_log2;
-          if (!(diag && c * 32 + i > r)) mx = fmaxf(mx, s);
-        }
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (half * 64 + c * 32 + i > r) v[c][i] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = (m == m_new) ? 1.f : ptx::ex2(m - m_new);
-      // pass 2: P = 2^(s - m_new) as bf16 into the first 64 columns of this S buffer (chunk c
-      // of S is read before chunk c of P overwrites columns that were already consumed)
-      float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        ptx::tmem_ld32(sb + c * 32, v);
-        ptx::tmem_wait_ld(v);
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        mx0 = fmaxf(mx0, __uint_as_float(v[0][i]));
+        mx1 = fmaxf(mx1, __uint_as_float(v[0][16 + i]));
+        mx2 = fmaxf(mx2, __uint_as_float(v[1][i]));
+        mx3 = fmaxf(mx3, __uint_as_float(v[1][16 + i]));
+      }
+      // exchange the partial max (double-buffered by block parity); the barrier also puts
+      // both warps' S loads before any P store below
+      red[(st * 2 + half) * 128 + r] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+      ptx::tc_fence_before();
+      ptx::named_bar_sync(pair_bar, 64);
+      ptx::tc_fence_after();
+      const float mcand = fmaxf(red[(st * 2) * 128 + r], red[(st * 2 + 1) * 128 + r]) * p.scale_log2;
+      float alpha = 1.f;
+      if (mcand > m + kLazy) {
+        alpha = ptx::ex2(m - mcand);  // 0 on the first block (m = -inf)
+        m = mcand;
+      }
+      const float neg = -m;
+      // P = 2^(s*scale - m) as bf16: this half's 64 values -> P columns half*32 .. +32
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int col = c * 32 + 2 * i;
-          const float s0 = __uint_as_float(v[2 * i]) * p.scale_log2;
-          const float s1 = __uint_as_float(v[2 * i + 1]) * p.scale_log2;
-          const float p0 = (diag && col > r) ? 0.f : ptx::ex2(s0 - m_new);
-          const float p1 = (diag && col + 1 > r) ? 0.f : ptx::ex2(s1 - m_new);
-          float r0, r1;
-          w[i] = pack_bf16(p0, p1, r0, r1);
-          sum += r0 + r1;
+          const float p0 = ptx::ex2(fmaf(__uint_as_float(v[c][2 * i]), p.scale_log2, neg));
+          const float p1 = ptx::ex2(fmaf(__uint_as_float(v[c][2 * i + 1]), p.scale_log2, neg));
+          sum0 += p0;
+          sum1 += p1;
+          const __nv_bfloat162 hp = __floats2bfloat162_rn(p0, p1);
+          w[i] = *reinterpret_cast<const uint32_t*>(&hp);
         }
-        ptx::tmem_st16(sb + c * 16, w);
+        ptx::tmem_st16(sb + half * 32 + c * 16, w);
       }
-      l = l * alpha + sum;
-      // O *= alpha once the previous P V has landed; a warp whose rows all kept their max
-      // leaves O alone (the P V of block j cannot start before this warp's p_ready arrival,
-      // so o_done is at most one phase ahead of the phase waited for here)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      l = l * alpha + (sum0 + sum1);  // this half's share of the row sum
+      // The P V of block j-1 must have landed before O is touched.  o_done is waited at every
+      // block, in order: the P V of block j cannot start before this warp's p_ready arrival,
+      // so o_done is never more than one phase past the phase waited for.
+      if (j > 0) {
         int o_ok = 1;
         if (lane == 0)
           o_ok = ptx::mbar_wait(o_done, (j - 1) & 1, abort_flag, p.status, kTimeoutCycles,
                                 DS_ERR_TIMEOUT)
                      ? 1
                      : 0;
-        if (!__shfl_sync(0xffffffffu, o_ok, 0)) {
-          ok = false;
-          break;
-        }
+        // a failed wait does not leave the loop here (the partner warp would then wait in
+        // the named barrier for good): the abort flag is set, so the next block's s_full
+        // wait fails at once and the pair leaves together after its flag exchange
+        if (!__shfl_sync(0xffffffffu, o_ok, 0)) ok = false;
         ptx::tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          ptx::tmem_ld32(ob + c * 32, v);
-          ptx::tmem_wait_ld(v);
+        if (ok && __any_sync(0xffffffffu, alpha != 1.f)) {
+          uint32_t o[2][32];
+          ptx::tmem_ld32(ob, o[0]);
+          ptx::tmem_ld32(ob + 32, o[1]);
+          ptx::tmem_wait_ld2(o[0], o[1]);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          ptx::tmem_st32(ob + c * 32, v);
+          for (int c = 0; c < 2; ++c) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
+            ptx::tmem_st32(ob + c * 32, o[c]);
+          }
         }
       }
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(p_ready);
-      m = m_new;
+      if (lane == 0) ptx::mbar_arrive(p_ready0 + 8u * st);
     }
-    if (ok) {
+    // the row sum is the two halves' shares (same m); exchanged once more
+    red[(2 * 2 + half) * 128 + r] = ok ? l : -1.f;
+    ptx::named_bar_sync(pair_bar, 64);
+    const float l_other = red[(2 * 2 + (half ^ 1)) * 128 + r];
+    if (ok && l_other >= 0.f) {
       int o_ok = 1;
       if (lane == 0)
         o_ok = ptx::mbar_wait(o_done, (nblk - 1) & 1, abort_flag, p.status, kTimeoutCycles,
@@ -329,25 +371,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                    : 0;
       if (__shfl_sync(0xffffffffu, o_ok, 0)) {
         ptx::tc_fence_after();
-        const float inv = 1.f / l;
+        const float inv = 1.f / (l + l_other);
         const bool valid = q0 + r < p.seq;
-        __nv_bfloat16* dst =
-            p.out + static_cast<int64_t>(row0 + q0 + r) * p.ldo + static_cast<int64_t>(h) * 128;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          ptx::tmem_ld32(ob + c * 32, v);
-          ptx::tmem_wait_ld(v);
-          if (valid) {
+        __nv_bfloat16* dst = p.out + static_cast<int64_t>(row0 + q0 + r) * p.ldo +
+                             static_cast<int64_t>(h) * 128 + half * 64;
+        uint32_t o[2][32];
+        ptx::tmem_ld32(ob, o[0]);
+        ptx::tmem_ld32(ob + 32, o[1]);
+        ptx::tmem_wait_ld2(o[0], o[1]);
+        if (valid) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
             uint32_t w[16];
             float r0, r1;
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              w[i] = pack_bf16(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv,
-                               r0, r1);
+              w[i] = pack_bf16(__uint_as_float(o[c][2 * i]) * inv,
+                               __uint_as_float(o[c][2 * i + 1]) * inv, r0, r1);
             uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            for (int i = 0; i < 4; ++i)
+              d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
           }
         }
       }
@@ -405,52 +449,68 @@ __global__ void __launch_bounds__(256)
 }
 
 // RoPE in place on qkv [rows, ld]: the 64-wide q_pe of each head (columns h*192 + 128 ..) and
-// k_pe (columns kcol ..), one thread per (token, head or k), all 64 elements of its row (so
-// the in-place update never races): the interleave -> half transform and the rotation of
+// k_pe (columns kcol ..): the interleave -> half transform and the rotation of
 // src/reference/mla.py:176-206, out[k] = x[2k] cos[k] - x[2k+1] sin[k],
 // out[32+k] = x[2k+1] cos[32+k] + x[2k] sin[32+k], one bf16 rounding.  cos/sin: bf16
 // [positions, 64] tables at position pos[row] (or row % seq when pos is null).
+// Four lanes per 64-wide row (lane l reads elements 16l..16l+15, i.e. pairs 8l..8l+7, and
+// writes out[8l..] and out[32+8l..]); a warp covers 8 rows, each read as one 128-byte line,
+// and every lane's loads complete (syncwarp) before any lane of the warp stores, so the
+// in-place update never races.
 __global__ void __launch_bounds__(256)
     mla_rope_inplace_kernel(__nv_bfloat16* __restrict__ qkv, int ld, int64_t rows, int seq,
                             int heads, int kcol, const __nv_bfloat16* __restrict__ cos_t,
                             const __nv_bfloat16* __restrict__ sin_t,
                             const int32_t* __restrict__ pos) {
   const int per_row = heads + 1;
-  const int64_t total = rows * per_row;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = i / per_row;
-    const int hh = static_cast<int>(i - row * per_row);
-    const int col = hh < heads ? hh * 192 + 128 : kcol;
-    uint4* x4 = reinterpret_cast<uint4*>(qkv + row * ld + col);
-    const int64_t pr = pos != nullptr ? __ldg(pos + row) : row % seq;
-    const uint4* c4 = reinterpret_cast<const uint4*>(cos_t + pr * 64);
-    const uint4* s4 = reinterpret_cast<const uint4*>(sin_t + pr * 64);
-    uint4 xv[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) xv[k] = x4[k];
-    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(xv);
-    uint4 ov[8];
-    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(ov);
-#pragma unroll
-    for (int k8 = 0; k8 < 4; ++k8) {
-      const uint4 cl = __ldg(c4 + k8), ch = __ldg(c4 + 4 + k8);
-      const uint4 sl = __ldg(s4 + k8), sh = __ldg(s4 + 4 + k8);
+  const int64_t items = rows * per_row;
+  const int lane = threadIdx.x & 31;
+  const int l = lane & 3;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t base = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) / 32 * 8;
+       base < items; base += warps * 8) {
+    const int64_t it = base + (lane >> 2);
+    const bool live = it < items;
+    uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0, cl = x0, ch = x0, sl = x0, sh = x0;
+    __nv_bfloat16* row = nullptr;
+    if (live) {
+      const int64_t tok = it / per_row;
+      const int hh = static_cast<int>(it - tok * per_row);
+      row = qkv + tok * ld + (hh < heads ? hh * 192 + 128 : kcol);
+      const uint4* x4 = reinterpret_cast<const uint4*>(row) + 2 * l;
+      x0 = x4[0];
+      x1 = x4[1];
+      const int64_t pr = pos != nullptr ? __ldg(pos + tok) : tok % seq;
+      const uint4* c4 = reinterpret_cast<const uint4*>(cos_t + pr * 64);
+      const uint4* s4 = reinterpret_cast<const uint4*>(sin_t + pr * 64);
+      cl = __ldg(c4 + l);
+      ch = __ldg(c4 + 4 + l);
+      sl = __ldg(s4 + l);
+      sh = __ldg(s4 + 4 + l);
+    }
+    __syncwarp();
+    if (live) {
+      const __nv_bfloat16* xa = reinterpret_cast<const __nv_bfloat16*>(&x0);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&x1);
       const __nv_bfloat16* clp = reinterpret_cast<const __nv_bfloat16*>(&cl);
       const __nv_bfloat16* chp = reinterpret_cast<const __nv_bfloat16*>(&ch);
       const __nv_bfloat16* slp = reinterpret_cast<const __nv_bfloat16*>(&sl);
       const __nv_bfloat16* shp = reinterpret_cast<const __nv_bfloat16*>(&sh);
+      uint4 lo, hi;
+      __nv_bfloat16* lop = reinterpret_cast<__nv_bfloat16*>(&lo);
+      __nv_bfloat16* hip = reinterpret_cast<__nv_bfloat16*>(&hi);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const int k = k8 * 8 + q;
-        const float a = __bfloat162float(xe[2 * k]), bb = __bfloat162float(xe[2 * k + 1]);
-        oe[k] = __float2bfloat16_rn(a * __bfloat162float(clp[q]) - bb * __bfloat162float(slp[q]));
-        oe[32 + k] =
-            __float2bfloat16_rn(bb * __bfloat162float(chp[q]) + a * __bfloat162float(shp[q]));
+        const __nv_bfloat16* xx = q < 4 ? xa : xb;
+        const float a = __bfloat162float(xx[2 * (q & 3)]);
+        const float bb = __bfloat162float(xx[2 * (q & 3) + 1]);
+        lop[q] = __float2bfloat16_rn(a * __bfloat162float(clp[q]) - bb * __bfloat162float(slp[q]));
+        hip[q] = __float2bfloat16_rn(bb * __bfloat162float(chp[q]) + a * __bfloat162float(shp[q]));
       }
+      uint4* o4 = reinterpret_cast<uint4*>(row);
+      o4[l] = lo;
+      o4[4 + l] = hi;
     }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) x4[k] = ov[k];
   }
 }
 
@@ -538,7 +598,7 @@ int launch_mla_rope(void* qkv, int ldq, int64_t rows, int seq, int heads, const 
   DeviceInfo di;
   DS_TRY(device_info(&di));
   const int64_t items = rows * (heads + 1);
-  int64_t grid = (items + 255) / 256;
+  int64_t grid = (items * 4 + 255) / 256;  // four lanes per row
   if (grid > di.num_sms * 16) grid = di.num_sms * 16;
   mla_rope_inplace_kernel<<<static_cast<int>(grid > 0 ? grid : 1), 256, 0, s>>>(
       static_cast<__nv_bfloat16*>(qkv), ldq, rows, seq, heads, heads * 192 + 512,

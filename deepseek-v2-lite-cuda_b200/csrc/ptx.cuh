@@ -60,6 +60,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
+// Named barrier `id` (1..15; 0 is __syncthreads) over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---- TMA -------------------------------------------------------------------------------
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -218,6 +223,25 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[32]) {
                  "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
                :
                : "memory");
+}
+__device__ __forceinline__ void tmem_tie32(uint32_t (&b)[32]) {
+  asm volatile(""
+               : "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]),
+                 "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]),
+                 "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]), "+r"(b[16]),
+                 "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]),
+                 "+r"(b[22]), "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]),
+                 "+r"(b[27]), "+r"(b[28]), "+r"(b[29]), "+r"(b[30]), "+r"(b[31])
+               :
+               : "memory");
+}
+// Four 32-column loads in flight, one wait; every register set is tied to the point after it.
+__device__ __forceinline__ void tmem_wait_ld4(uint32_t (&a)[32], uint32_t (&b)[32],
+                                              uint32_t (&c)[32], uint32_t (&d)[32]) {
+  tmem_wait_ld(a);
+  tmem_tie32(b);
+  tmem_tie32(c);
+  tmem_tie32(d);
 }
 __device__ __forceinline__ void tmem_wait_ld2(uint32_t (&a)[32], uint32_t (&b)[32]) {
   tmem_wait_ld(a);
