@@ -23,7 +23,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "ds_kernels", "libds_kernels_sm100.so")
 
 SOURCES = ["common.cu", "moe_kernels.cu", "mla_kernels.cu", "gemm_sm100.cu", "moe_layer.cu",
-           "moe_noalloc.cu", "moe_stages.cu", "ep_p2p.cu", "mla_attention.cu"]
+           "moe_noalloc.cu", "moe_stages.cu", "ep_p2p.cu", "mla_attention.cu", "mla_decode.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [

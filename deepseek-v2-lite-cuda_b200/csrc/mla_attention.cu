@@ -686,11 +686,34 @@ size_t ds_mla_forward_workspace_size(int batch, int seq, int hidden, int heads) 
   return carve_mla(c, nullptr, batch, seq, heads);
 }
 
-int ds_mla_forward(const void* x_bf16, const void* w_qkv_a_bf16, const float* kv_norm_weight,
-                   const void* w_kv_b_bf16, const void* w_o_bf16, const void* cos_bf16,
-                   const void* sin_bf16, const int32_t* positions, void* out_bf16, int batch,
-                   int seq, int hidden, int heads, float eps, float softmax_scale,
-                   void* workspace, size_t workspace_bytes, void** events, void* stream) {
+}  // extern "C"
+
+namespace ds {
+namespace dec {
+int launch_cache_append(const void* src_lat, int lat_ld, const void* src_kpe, int kpe_ld,
+                        int src_bstride, int batch, int n_new, int pos0, int max_seq,
+                        int copy_raw, void* c_lat, void* c_kpe, float* c_rstd, void* c_kpe_rot,
+                        const void* cos_t, const void* sin_t, float eps, cudaStream_t s);
+}  // namespace dec
+}  // namespace ds
+
+namespace {
+
+struct CacheArgs {
+  void* latent;
+  void* kpe;
+  float* rstd;
+  void* kpe_rot;
+  int max_seq;
+  int pos0;
+};
+
+int mla_forward_impl(const void* x_bf16, const void* w_qkv_a_bf16, const float* kv_norm_weight,
+                     const void* w_kv_b_bf16, const void* w_o_bf16, const void* cos_bf16,
+                     const void* sin_bf16, const int32_t* positions, void* out_bf16, int batch,
+                     int seq, int hidden, int heads, float eps, float softmax_scale,
+                     void* workspace, size_t workspace_bytes, void** events, void* stream,
+                     const CacheArgs* cache) {
   DS_REQUIRE(batch >= 0 && seq >= 0 && heads >= 1 && hidden > 0, "mla_forward: bad shape");
   DS_REQUIRE(hidden % 8 == 0, "mla_forward: hidden_size must be a multiple of 8");
   DS_REQUIRE(seq % 8 == 0 || batch * seq == 0, "mla_forward: seq_len must be a multiple of 8");
@@ -717,6 +740,14 @@ int ds_mla_forward(const void* x_bf16, const void* w_qkv_a_bf16, const float* kv
   DS_TRY(ds_rms_norm_strided(static_cast<const __nv_bfloat16*>(b.qkv) + heads * 192, ldq,
                              kv_norm_weight, b.lat, kLatent, static_cast<int>(M), kLatent, eps,
                              stream));
+  if (cache != nullptr) {
+    // the prompt's raw latents and k_pe (before the in-place RoPE below) into the cache
+    const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(b.qkv);
+    DS_TRY(ds::dec::launch_cache_append(q + heads * 192, ldq, q + heads * 192 + kLatent, ldq, seq,
+                                        batch, seq, cache->pos0, cache->max_seq, 1, cache->latent,
+                                        cache->kpe, cache->rstd, cache->kpe_rot, cos_bf16,
+                                        sin_bf16, eps, s));
+  }
   DS_TRY(mark(2));
   DS_TRY(ds::gemm::launch(dense_problem(b.lat, M, kLatent, w_kv_b_bf16, heads * 256, b.kv), s));
   DS_TRY(mark(3));
@@ -728,6 +759,36 @@ int ds_mla_forward(const void* x_bf16, const void* w_qkv_a_bf16, const float* kv
   DS_TRY(ds::gemm::launch(dense_problem(b.o, M, heads * 128, w_o_bf16, hidden, out_bf16), s));
   DS_TRY(mark(6));
   return DS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ds_mla_forward(const void* x_bf16, const void* w_qkv_a_bf16, const float* kv_norm_weight,
+                   const void* w_kv_b_bf16, const void* w_o_bf16, const void* cos_bf16,
+                   const void* sin_bf16, const int32_t* positions, void* out_bf16, int batch,
+                   int seq, int hidden, int heads, float eps, float softmax_scale,
+                   void* workspace, size_t workspace_bytes, void** events, void* stream) {
+  return mla_forward_impl(x_bf16, w_qkv_a_bf16, kv_norm_weight, w_kv_b_bf16, w_o_bf16, cos_bf16,
+                          sin_bf16, positions, out_bf16, batch, seq, hidden, heads, eps,
+                          softmax_scale, workspace, workspace_bytes, events, stream, nullptr);
+}
+
+int ds_mla_prefill(const void* x_bf16, const void* w_qkv_a_bf16, const float* kv_norm_weight,
+                   const void* w_kv_b_bf16, const void* w_o_bf16, const void* cos_bf16,
+                   const void* sin_bf16, void* out_bf16, int batch, int seq, int hidden,
+                   int heads, float eps, float softmax_scale, void* cache_latent_bf16,
+                   void* cache_kpe_bf16, float* cache_rstd, void* cache_kpe_rot_bf16,
+                   int max_seq, int pos0, void* workspace, size_t workspace_bytes, void* stream) {
+  DS_REQUIRE(pos0 == 0, "mla_prefill: the prompt starts at position 0 (pos0=%d)", pos0);
+  DS_REQUIRE(seq <= max_seq, "mla_prefill: prompt longer than the cache");
+  DS_REQUIRE(cache_latent_bf16 && cache_kpe_bf16 && cache_rstd && cache_kpe_rot_bf16,
+             "mla_prefill: null cache pointer");
+  CacheArgs c{cache_latent_bf16, cache_kpe_bf16, cache_rstd, cache_kpe_rot_bf16, max_seq, pos0};
+  return mla_forward_impl(x_bf16, w_qkv_a_bf16, kv_norm_weight, w_kv_b_bf16, w_o_bf16, cos_bf16,
+                          sin_bf16, nullptr, out_bf16, batch, seq, hidden, heads, eps,
+                          softmax_scale, workspace, workspace_bytes, nullptr, stream, &c);
 }
 
 }  // extern "C"

@@ -271,6 +271,21 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major bf16 operand written by TMA with 128-byte
+// swizzle: along M (or N) 64 contiguous elements per 128-byte row, the next 64 elements
+// `lbo_bytes` further (LBO: the next TMA box); along K one row per 128 bytes, 8-row groups
+// 1024 B apart (SBO).  The canonical SWIZZLE_128B MN-major form ((8,n),(8,k)):((1,LBO),
+// (8,SBO)) in 16-byte units.
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t saddr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: bf16 A and B (K-major), f32 accumulator, M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4)                                   // D format: f32
@@ -278,6 +293,10 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | (1u << 10)                                // B format: bf16
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+}
+// The same with A MN-major (bit 15).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_amn(int M, int N) {
+  return idesc_bf16_f32(M, N) | (1u << 15);
 }
 
 // ---- flags shared between GPUs (peer memory): release/acquire at system scope -----------

@@ -32,6 +32,7 @@ DS_ERR_TIMEOUT = 4
 DS_ERR_WORKSPACE = 5
 LAYER_NUM_EVENTS = 9
 MLA_NUM_EVENTS = 7
+MLA_DECODE_NUM_EVENTS = 5
 EP_NUM_EVENTS = 7
 EP_IPC_HANDLE_BYTES = 64
 
@@ -70,6 +71,13 @@ SIGNATURES = {
     "ds_mla_forward_workspace_size": (_sz, [_i, _i, _i, _i]),
     "ds_mla_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _f,
                             _vp, _sz, _vp, _vp]),
+    "ds_mla_prefill": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _f, _vp,
+                            _vp, _vp, _vp, _i, _i, _vp, _sz, _vp]),
+    "ds_mla_cache_append": (_i, [_vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp,
+                                 _vp, _vp, _f, _vp]),
+    "ds_mla_decode_workspace_size": (_sz, [_i, _i]),
+    "ds_mla_decode_step": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
+                                _f, _f, _vp, _vp, _sz, _vp, _vp]),
     "ds_moe_layer_workspace_routing": (_i, [_i, _i, _i, _i, _i, _i, ctypes.POINTER(_sz),
                                             ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
     "ds_moe_layer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
@@ -649,6 +657,94 @@ def mla_forward(hidden_states: torch.Tensor, w_qkv_a: torch.Tensor,
                                    _ptr(cos), _ptr(sin), _ptr(pos), _ptr(out), B, S, Hd, heads,
                                    float(eps), float(softmax_scale), _ptr(workspace),
                                    workspace.numel(), ev, _stream(x)), "mla_forward")
+    return out
+
+
+def mla_prefill(hidden_states: torch.Tensor, w_qkv_a: torch.Tensor,
+                kv_norm_weight: torch.Tensor, w_kv_b: torch.Tensor, w_o: torch.Tensor,
+                cos: torch.Tensor, sin: torch.Tensor, softmax_scale: float, heads: int, cache,
+                eps: float = 1e-6, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """mla_forward over a prompt at positions 0 .. seq-1 that also fills `cache` (an empty
+    mla_cache.LatentKVCache on the same device) with the prompt's raw latents and k_pe."""
+    x = hidden_states.contiguous()
+    B, S, Hd = x.shape
+    _require(cache.current_len == 0, "mla_prefill: the cache must be empty")
+    _require(cache.bsz == B and S <= cache.max_seq, "mla_prefill: cache shape")
+    out = torch.empty((B, S, Hd), dtype=torch.bfloat16, device=x.device)
+    if B * S == 0:
+        return out
+    need = mla_forward_workspace_size(B, S, Hd, heads)
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(need, x.device)
+    nw = kv_norm_weight.detach().float().contiguous()
+    with _on_device(x):
+        _check(_lib.ds_mla_prefill(_ptr(x), _ptr(w_qkv_a), _ptr(nw), _ptr(w_kv_b), _ptr(w_o),
+                                   _ptr(cos), _ptr(sin), _ptr(out), B, S, Hd, heads, float(eps),
+                                   float(softmax_scale), _ptr(cache.kv_latent),
+                                   _ptr(cache.k_pe_cache), _ptr(cache.rstd), _ptr(cache.k_pe_rot),
+                                   cache.max_seq, 0, _ptr(workspace), workspace.numel(),
+                                   _stream(x)), "mla_prefill")
+    cache._advance(S, cos, sin, eps)
+    return out
+
+
+def mla_cache_append(latent: torch.Tensor, k_pe: torch.Tensor, cache, pos0: int,
+                     cos: torch.Tensor, sin: torch.Tensor, eps: float = 1e-6,
+                     copy_raw: bool = True) -> None:
+    """latent [bsz, n, 512], k_pe [bsz, n, 64] (bf16, CUDA; any row stride with 16-byte aligned
+    rows) -> cache positions pos0 .. pos0+n-1, with the side arrays (rstd, rotated k_pe)."""
+    B, n, _ = latent.shape
+    if B * n == 0:
+        return
+    _require(latent.stride(2) == 1 and k_pe.stride(2) == 1, "mla_cache_append: unsupported strides")
+    rows = latent.stride(0) // latent.stride(1)
+    _require(latent.stride(0) == rows * latent.stride(1)
+             and k_pe.stride(0) == rows * k_pe.stride(1),
+             "mla_cache_append: latent and k_pe must step sequences by the same number of rows")
+    with _on_device(latent):
+        _check(_lib.ds_mla_cache_append(_ptr(latent), latent.stride(1), _ptr(k_pe), k_pe.stride(1),
+                                        rows, B, n, pos0, cache.max_seq, 1 if copy_raw else 0,
+                                        _ptr(cache.kv_latent), _ptr(cache.k_pe_cache),
+                                        _ptr(cache.rstd), _ptr(cache.k_pe_rot), _ptr(cos),
+                                        _ptr(sin), float(eps), _stream(latent)),
+               "mla_cache_append")
+
+
+def mla_decode_workspace_size(batch: int, max_seq: int) -> int:
+    return int(_lib.ds_mla_decode_workspace_size(batch, max_seq))
+
+
+def mla_decode_step(x: torch.Tensor, w_dec: torch.Tensor, w_out: torch.Tensor, cos: torch.Tensor,
+                    sin: torch.Tensor, cache, softmax_scale: float, heads: int = 16,
+                    eps: float = 1e-6, workspace: Optional[torch.Tensor] = None,
+                    events: Optional[Sequence[torch.cuda.Event]] = None) -> torch.Tensor:
+    """One decode step: x bf16 [bsz, hidden] (one new token per sequence) -> [bsz, hidden];
+    appends the token to `cache` (mla_cache.LatentKVCache) at position cache.current_len and
+    attends over every cached position (see include/ds_kernels.h for w_dec / w_out)."""
+    _check_tensor(x, "x", torch.bfloat16, "bfloat16", 2, "[bsz, hidden]")
+    B, Hd = x.shape
+    _require(cache.bsz == B, "mla_decode_step: cache batch size differs from x")
+    out = torch.empty((B, Hd), dtype=torch.bfloat16, device=x.device)
+    need = mla_decode_workspace_size(B, cache.max_seq)
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(need, x.device)
+    ev = None
+    if events is not None:
+        _require(len(events) == MLA_DECODE_NUM_EVENTS,
+                 f"events must hold {MLA_DECODE_NUM_EVENTS} events")
+        st = torch.cuda.current_stream(x.device)
+        for e in events:
+            e.record(st)
+        ev = (ctypes.c_void_p * MLA_DECODE_NUM_EVENTS)(*[e.cuda_event for e in events])
+    cache._sync_side(cos, sin, eps)
+    with _on_device(x):
+        _check(_lib.ds_mla_decode_step(_ptr(x), _ptr(w_dec), _ptr(w_out), _ptr(cos), _ptr(sin),
+                                       _ptr(cache.kv_latent), _ptr(cache.k_pe_cache),
+                                       _ptr(cache.rstd), _ptr(cache.k_pe_rot), B, cache.max_seq,
+                                       cache.current_len, Hd, heads, float(eps),
+                                       float(softmax_scale), _ptr(out), _ptr(workspace),
+                                       workspace.numel(), ev, _stream(x)), "mla_decode_step")
+    cache._advance(1, cos, sin, eps)
     return out
 
 

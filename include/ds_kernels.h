@@ -236,6 +236,54 @@ DS_API int ds_mla_forward(const void* x_bf16, const void* w_qkv_a_bf16,
                           void* workspace, size_t workspace_bytes, void** events,
                           void* stream);
 
+/* ds_mla_prefill: ds_mla_forward over a prompt (positions 0 .. seq-1) that also writes the
+ * prompt's raw latents and raw k_pe into a latent KV cache (the layout of
+ * src/kernels/mla_cache.py:29-219: latent bf16 [batch, max_seq, 512], k_pe bf16
+ * [batch, max_seq, 64]) together with the cache's two side arrays (rstd f32
+ * [batch, max_seq], k_pe_rot bf16 [batch, max_seq, 64]; see ds_mla_cache_append). */
+DS_API int ds_mla_prefill(const void* x_bf16, const void* w_qkv_a_bf16,
+                          const float* kv_norm_weight, const void* w_kv_b_bf16,
+                          const void* w_o_bf16, const void* cos_bf16, const void* sin_bf16,
+                          void* out_bf16, int batch, int seq, int hidden, int heads, float eps,
+                          float softmax_scale, void* cache_latent_bf16, void* cache_kpe_bf16,
+                          float* cache_rstd, void* cache_kpe_rot_bf16, int max_seq, int pos0,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * MLA decode over the latent KV cache (config 4; the cache of src/kernels/mla_cache.py:29-219
+ * and the attention of src/reference/mla.py:295-393 for one new token per sequence; the
+ * reference has no decode kernel).
+ *
+ * ds_mla_cache_append: tokens pos0 .. pos0+new_tokens-1 of each of `batch` sequences; token i
+ * of sequence b reads its latent (512) at latent + (b*src_rows_per_seq + i)*latent_ld and its
+ * raw k_pe (64) at kpe + (...)*kpe_ld.  Writes the raw values into the cache (copy_raw != 0;
+ * 0 refreshes only the side arrays of tokens already in it), and the side arrays the decode
+ * attention reads: rstd = rsqrt(mean(latent^2) + eps) and k_pe rotated at its position with
+ * the bf16 cos/sin [positions, 64] tables.
+ *
+ * ds_mla_decode_step: one token per sequence, heads == 16.  x bf16 [batch, hidden];
+ * w_dec bf16 [16*512 + 16*64 + 512 + 64, hidden] = the absorbed query weights (per head
+ * diag(g) W_uk_h^T W_q_nope_h, g the latent norm weight), the q_pe rows of q_proj, and
+ * kv_a_proj_with_mqa; w_out bf16 [hidden, 16*512] = per head W_o_h W_uv_h diag(g).  Appends
+ * the token at position cache_len, attends over positions 0 .. cache_len, writes out bf16
+ * [batch, hidden].  `events`: NULL or DS_MLA_DECODE_NUM_EVENTS handles (projection, append +
+ * query, attention, output projection). */
+DS_API int ds_mla_cache_append(const void* latent_bf16, int latent_ld, const void* kpe_bf16,
+                               int kpe_ld, int src_rows_per_seq, int batch, int new_tokens,
+                               int pos0, int max_seq, int copy_raw, void* cache_latent_bf16,
+                               void* cache_kpe_bf16, float* cache_rstd, void* cache_kpe_rot_bf16,
+                               const void* cos_bf16, const void* sin_bf16, float eps,
+                               void* stream);
+#define DS_MLA_DECODE_NUM_EVENTS 5
+DS_API size_t ds_mla_decode_workspace_size(int batch, int max_seq);
+DS_API int ds_mla_decode_step(const void* x_bf16, const void* w_dec_bf16, const void* w_out_bf16,
+                              const void* cos_bf16, const void* sin_bf16,
+                              void* cache_latent_bf16, void* cache_kpe_bf16, float* cache_rstd,
+                              void* cache_kpe_rot_bf16, int batch, int max_seq, int cache_len,
+                              int hidden, int heads, float eps, float softmax_scale,
+                              void* out_bf16, void* workspace, size_t workspace_bytes,
+                              void** events, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Fused MoE layer (new, additive; the pipeline of src/kernels/moe_fused.py:118-154 plus the
  * shared expert of src/reference/moe.py:72-74,106-107 that the reference pipeline drops).

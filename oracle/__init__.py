@@ -16,5 +16,5 @@ from .moe_oracle import (  # noqa: F401
 )
 from .mla_oracle import (  # noqa: F401
     rms_norm, rms_norm_residual, rope, yarn_cos_sin, kv_upproj, mla_attention, mla_forward,
-    mla_forward_rows,
+    mla_forward_rows, mla_decode_step,
 )

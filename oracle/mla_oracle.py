@@ -12,6 +12,10 @@ mla_attention: the causal scaled-dot-product step of src/reference/mla.py:355-37
 mla_forward: the whole DeepSeekMLA.forward of src/reference/mla.py:295-393 in f32 (q_proj,
              kv_a_proj_with_mqa, kv_a_layernorm, kv_b_proj, RoPE on the 64-wide parts,
              causal attention over 192-wide q/k and 128-wide v, o_proj).
+mla_decode_step: the same forward for one new token per sequence whose predecessors are
+             given as the raw latents / raw k_pe of a latent KV cache (src/kernels/
+             mla_cache.py:29-219 stores exactly those): the last row of mla_forward when the
+             cache holds the prefix's projections.
 """
 from __future__ import annotations
 
@@ -154,4 +158,31 @@ def mla_forward_rows(x: torch.Tensor, w_q: torch.Tensor, w_kva: torch.Tensor,
     masked = torch.arange(s_len)[None, :] > rows[:, None]
     w = torch.softmax(w.masked_fill(masked[None, None], float("-inf")), dim=-1)
     attn = torch.matmul(w, v).transpose(1, 2).reshape(b, R, heads * 128)
+    return attn @ w_o.to(F32).t()
+
+
+def mla_decode_step(x_new: torch.Tensor, cache_latent: torch.Tensor, cache_kpe: torch.Tensor,
+                    w_q: torch.Tensor, w_kva: torch.Tensor, norm_w: torch.Tensor,
+                    w_kvb: torch.Tensor, w_o: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                    softmax_scale: float, heads: int, eps: float = 1e-6) -> torch.Tensor:
+    """x_new [b, hidden] at position L = cache_latent.shape[1]; cache_latent [b, L, 512] and
+    cache_kpe [b, L, 64] the raw latents / k_pe of positions 0 .. L-1.  Returns f32
+    [b, hidden]: DeepSeekMLA.forward's output row L (src/reference/mla.py:295-393)."""
+    b, L, _ = cache_latent.shape
+    xf = x_new.to(F32)
+    q = (xf @ w_q.to(F32).t()).view(b, heads, 1, 192)
+    ckv = xf @ w_kva.to(F32).t()
+    latent = torch.cat([cache_latent.to(F32), ckv[:, None, :512]], dim=1)    # [b, L+1, 512]
+    kpe = torch.cat([cache_kpe.to(F32), ckv[:, None, 512:]], dim=1)          # [b, L+1, 64]
+    kv = (rms_norm(latent, norm_w, eps) @ w_kvb.to(F32).t()).view(b, L + 1, heads, 256)
+    kv = kv.transpose(1, 2)
+    k_nope, v = kv[..., :128], kv[..., 128:]
+    _, k_rot = rope(kpe[:, None], kpe[:, None], cos[:L + 1].to(F32)[None, None],
+                    sin[:L + 1].to(F32)[None, None])
+    q_rot, _ = rope(q[..., 128:], q[..., 128:][:, :1], cos[L:L + 1].to(F32)[None, None],
+                    sin[L:L + 1].to(F32)[None, None])
+    qs = torch.cat([q[..., :128], q_rot], dim=-1)                             # [b, h, 1, 192]
+    ks = torch.cat([k_nope, k_rot.expand(b, heads, L + 1, 64)], dim=-1)       # [b, h, L+1, 192]
+    w = torch.softmax(torch.matmul(qs, ks.transpose(2, 3)) * softmax_scale, dim=-1)
+    attn = torch.matmul(w, v).reshape(b, heads * 128)
     return attn @ w_o.to(F32).t()

@@ -152,3 +152,18 @@ def test_mla_forward_rows_agrees_with_the_full_forward():
     rows = torch.tensor([0, 1, 7, 20, 39])
     torch.testing.assert_close(oracle.mla_forward_rows(*args, rows), full[:, rows],
                                atol=1e-5, rtol=1e-5)
+
+
+def test_mla_decode_step_is_the_last_row_of_the_forward():
+    # the decode oracle over a cache holding a prefix's raw latents / k_pe equals the full
+    # forward's row at the new position (pinned through mla_forward to the reference module)
+    fx = _load("mla_forward_yarn40.pt")
+    x = fx["x"]
+    L = x.shape[1] - 1
+    ckv = x[:, :L] @ fx["w_kva"].t()
+    out = oracle.mla_decode_step(x[:, L], ckv[..., :512], ckv[..., 512:], fx["w_q"], fx["w_kva"],
+                                 fx["norm_w"], fx["w_kvb"], fx["w_o"], fx["cos"], fx["sin"],
+                                 fx["softmax_scale"], fx["heads"])
+    full = oracle.mla_forward(x, fx["w_q"], fx["w_kva"], fx["norm_w"], fx["w_kvb"], fx["w_o"],
+                              fx["cos"], fx["sin"], fx["softmax_scale"], fx["heads"])
+    torch.testing.assert_close(out, full[:, L], atol=1e-5, rtol=1e-5)
