@@ -540,6 +540,10 @@ def run_ours(args, rank, world, local_rank):
         line["cpu_baseline"] = base
     if world == 1 and not args.no_cfg3:
         line["cfg3_mla"] = mla_cfg3(dev)
+    if world == 1 and not args.no_cfg4:
+        del layer, full
+        torch.cuda.empty_cache()
+        line["cfg4_decode"] = decode_cfg4(dev)
     print(json.dumps(line), flush=True)
     if not par.get("ok", True):
         raise SystemExit("parity check failed: " + json.dumps(par))
@@ -603,6 +607,62 @@ def mla_cfg3(dev, steps=10, warmup=3):
             "TFLOP/s": round(sum(fl.values()) / (total / 1e3) / 1e12, 1),
             "attention_note": "flops of the causal lower triangle: B*heads*S^2*(192+128)",
             "kernels": kern, "peak_source": f"{pk['source']} bf16 burst / HBM copy"}
+
+
+def decode_cfg4(dev, steps=5, warmup=2):
+    """BASELINE config 4 on one GPU: a decode step of the full 27-layer DeepSeek-V2-Lite stack
+    (layer 0 dense SwiGLU 2048->10944->2048, layers 1-26 the MoE block; every layer's MLA over
+    a 2048-token latent cache of N(0,1) values) for 64 sequences; random-init N(0, 0.02^2)
+    weights.  Each timed step appends one token per sequence (positions 2048+warmup ..), with
+    CUDA events around the steps.  Returns ms per step and tokens/s (64 tokens per step),
+    with the bytes the step must stream (weights + caches) against HBM."""
+    import decoder
+    B, L = 64, 2048
+    stack = decoder.random_stack(27, dev, positions=L + 64, seed=4)
+    caches = stack.new_caches(B, L + 64, dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    for c in caches:
+        c.update(torch.randn(B, L, 512, generator=g, device=dev).to(torch.bfloat16),
+                 torch.randn(B, L, 64, generator=g, device=dev).to(torch.bfloat16))
+    xs = [torch.randn(B, 2048, generator=g, device=dev).to(torch.bfloat16)
+          for _ in range(warmup + steps + 1)]
+    # eager steps (launch-bound: ~15 launches per layer from the host), then the same step as
+    # one CUDA graph per step (positions read from the caches' device-side lengths)
+    stack.decode_step(xs[0], caches)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(warmup):
+        stack.decode_step(xs[1 + i], caches)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_eager = e0.elapsed_time(e1) / warmup
+    stack.capture_decode(xs[1], caches)
+    for i in range(warmup):
+        stack.replay_decode(xs[1 + i])
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(steps):
+        stack.replay_decode(xs[1 + warmup + i])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    moe_w = 26 * (64 * 3 * 2048 * 1408 + 3 * 2048 * 2816) * 2
+    dense_w = 3 * 2048 * 10944 * 2
+    mla_w = 27 * ((16 * 576 + 576) * 2048 + 2048 * 16 * 512) * 2
+    cache = 27 * B * (L + 2 * warmup + 2 + steps // 2) * (512 * 2 + 4 + 64 * 2)  # latent, rstd, k_pe_rot
+    nbytes = moe_w + dense_w + mla_w + cache
+    pk = peaks()
+    return {"workload": "cfg4: decode step of the 27-layer stack, batch 64, 2048-token latent "
+                        "caches, one GPU (all 64 experts of every layer resident)",
+            "ms_per_step": round(ms, 4), "tokens_per_s": round(B / (ms / 1e3), 1),
+            "ms_per_step_eager": round(ms_eager, 4),
+            "positions": f"steps at cache lengths {L + 2 + 2 * warmup} .. {L + 1 + 2 * warmup + steps}",
+            "bytes_per_step": nbytes, "GB/s": round(nbytes / (ms / 1e3) / 1e9, 1),
+            "frac_hbm": round(nbytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+            "note": "HBM-bound: every step streams the 27 layers' weights (MoE experts, "
+                    "absorbed MLA weights, dense FFN) and the latent caches"}
 
 
 L2_BYTES = 126 * 2 ** 20
@@ -786,6 +846,20 @@ def kernel_case(name, reps=2):
         g1 = torch.randn(16384 * K // 2, 2 * I, device=dev).to(torch.bfloat16)  # as op_report
         for _ in range(reps):
             ds_kernels.swiglu(g1)
+    elif name == "decode":
+        # config-4 decode steps of a 3-layer stack (layer 0 dense, layers 1-2 MoE) at the real
+        # sizes: batch 64, 2048-token caches; forward 1 warms up
+        import decoder
+        B, L = 64, 2048
+        stack = decoder.random_stack(3, dev, positions=L + 64, seed=4)
+        caches = stack.new_caches(B, L + 64, dev)
+        g = torch.Generator(device=dev).manual_seed(7)
+        for c in caches:
+            c.update(torch.randn(B, L, 512, generator=g, device=dev).to(torch.bfloat16),
+                     torch.randn(B, L, 64, generator=g, device=dev).to(torch.bfloat16))
+        x = torch.randn(B, 2048, generator=g, device=dev).to(torch.bfloat16)
+        for _ in range(reps + 1):
+            stack.decode_step(x, caches)
     elif name == "mla":
         # config 3 MLA forward: forward 1 warms up, the next ones can be captured
         for _ in range(reps + 1):
@@ -823,12 +897,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-cfg3", action="store_true",
                     help="skip the config-3 MLA forward measurement (cfg3_mla key)")
+    ap.add_argument("--no-cfg4", action="store_true",
+                    help="skip the config-4 decode-step measurement (cfg4_decode key)")
     ap.add_argument("--ep", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel transport for --gpus > 1")
     ap.add_argument("--op-report", default=None)
     ap.add_argument("--kernel-case", default=None,
                     choices=["layer", "gemm1", "gemm2", "dispatch", "routing", "router", "combine", "swiglu",
-                             "rms_norm", "rope", "kv_upproj", "mla"],
+                             "rms_norm", "rope", "kv_upproj", "mla", "decode"],
                     help="run one kernel at its BASELINE size twice (profiling) and exit")
     args = ap.parse_args()
     if args.kernel_case:

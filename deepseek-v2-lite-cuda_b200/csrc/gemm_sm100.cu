@@ -73,8 +73,10 @@ struct ProbParams {
   int ldo;
   const int32_t* out_row_map;
   int tma_out;        // contiguous output rows: full 32-row slabs leave by TMA store
-  int kb_per_split;   // router: k-blocks per K slice (the n-tile index is the slice)
-  float* logits_out;  // router: partial accumulators
+  int kb_per_split;   // router / split-K: k-blocks per K slice
+  int k_splits;       // split-K: K slices per output tile (1 otherwise)
+  float* logits_out;  // router / split-K: partial accumulators
+  int partial_cols;   // split-K: columns of a partial row
   // cross-GPU hooks (expert parallelism over peer memory)
   const int* wait_flag;      // before this problem's first tile: wait until *flag >= target
   int wait_target;
@@ -111,6 +113,7 @@ struct TileInfo {
   int nt;
   int v0, v1;  // valid output columns of the two 128-column halves (<= 0: none)
   bool full;   // both halves hold 128 valid columns
+  int ks;      // split-K slice (0 without split-K)
 };
 
 __device__ __forceinline__ const ProbParams& prob_params(const Params& p, int pb) {
@@ -127,8 +130,11 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const Params& p, const in
   const int* go = goff + ti.prob * kGroupStride;
   const int* gt = gtile + ti.prob * kGroupStride;
   const int tt = t - pstart[ti.prob];
-  const int mtg = tt / q.n_tiles;
-  ti.nt = tt - mtg * q.n_tiles;
+  const int per_m = q.n_tiles * q.k_splits;
+  const int mtg = tt / per_m;
+  const int rem = tt - mtg * per_m;
+  ti.nt = rem / q.k_splits;
+  ti.ks = rem - ti.nt * q.k_splits;
   int lo = 0, hi = q.groups;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -329,6 +335,27 @@ __device__ __forceinline__ void epilogue_router_partials(uint32_t tb, bool valid
   }
 }
 
+// Split-K: the 256 raw accumulator columns of this row as f32, half h to columns
+// col0 + h*half1_off of the slice's partial row (the first v0 / v1 columns of each half).
+__device__ __forceinline__ void epilogue_partial(uint32_t tb, bool valid, float* row, int col0,
+                                                 int half1_off, int v0, int v1) {
+#pragma unroll 1
+  for (int cc = 0; cc < 8; ++cc) {
+    uint32_t a[32];
+    ptx::tmem_ld32(tb + cc * 32, a);
+    ptx::tmem_wait_ld(a);
+    const int lim = (cc >> 2) ? v1 : v0;
+    if (valid && (cc & 3) * 32 < lim) {
+      float4* d4 = reinterpret_cast<float4*>(row + col0 + (cc >> 2) * half1_off + (cc & 3) * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if ((cc & 3) * 32 + 4 * i < lim)
+          d4[i] = make_float4(__uint_as_float(a[4 * i]), __uint_as_float(a[4 * i + 1]),
+                              __uint_as_float(a[4 * i + 2]), __uint_as_float(a[4 * i + 3]));
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA0,
@@ -405,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       gt[q.groups] = acc;
       pstart[pb] = start;
-      start += acc * q.n_tiles;
+      start += acc * q.n_tiles * q.k_splits;
     }
     pstart[p.nprob] = start;
   }
@@ -438,8 +465,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const CUtensorMap* tA = ti.prob ? &tmA1 : &tmA0;
         const CUtensorMap* tB = ti.prob ? &tmB1 : &tmB0;
-        const int kb0 = EPI == kRouter ? ti.nt * q.kb_per_split : 0;
-        const int kb1 = EPI == kRouter ? min(q.k_blocks, kb0 + q.kb_per_split) : q.k_blocks;
+        const int kb0 = EPI == kRouter    ? ti.nt * q.kb_per_split
+                        : EPI == kPartial ? ti.ks * q.kb_per_split
+                                          : 0;
+        const int kb1 = (EPI == kRouter || EPI == kPartial) ? min(q.k_blocks, kb0 + q.kb_per_split)
+                                                            : q.k_blocks;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(empty0 + 8u * stage, phase ^ 1u, abort_flag, p.status,
                               p.timeout_cycles, DS_ERR_TIMEOUT)) {
@@ -488,6 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int kb0 = 0, kb1 = q.k_blocks;
         if constexpr (EPI == kRouter) {
           kb0 = ti.nt * q.kb_per_split;
+          kb1 = min(q.k_blocks, kb0 + q.kb_per_split);
+        } else if constexpr (EPI == kPartial) {
+          kb0 = ti.ks * q.kb_per_split;
           kb1 = min(q.k_blocks, kb0 + q.kb_per_split);
         }
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -569,6 +602,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if constexpr (EPI == kRouter) {
         epilogue_router_partials(
             tb, valid, qp.logits_out + (static_cast<int64_t>(ti.nt) * qp.dense_rows + orow) * 192);
+      } else if constexpr (EPI == kPartial) {
+        epilogue_partial(tb, valid,
+                         qp.logits_out + (static_cast<int64_t>(ti.ks) * qp.dense_rows + orow) *
+                                             qp.partial_cols,
+                         ti.nt * qp.b_tile_stride, qp.b_half1_off, ti.v0, ti.v1);
       } else {
         if (staged)
           epilogue_plain_staged(tb, tO, slab, lane, ti.row0 + q * 32, ti.nt * qp.b_tile_stride,
@@ -625,11 +663,48 @@ __global__ void zero_uncovered_kernel(uint4* __restrict__ out, int64_t S, int ld
   }
 }
 
+// Split-K reduce: out[r, c] = bf16( sum_s part[s, r, c] ) (plain), or with the SwiGLU
+// epilogue bf16( silu(sum gate) * sum up ) for the gate column c and the up column seg + c.
+// Four columns per thread; slices summed in order (deterministic).
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float* __restrict__ part, int ks, int64_t rows, int pcols,
+                         int swiglu, int seg, __nv_bfloat16* __restrict__ out, int ldo) {
+  const int ocols = swiglu ? seg : pcols;
+  const int c4n = ocols >> 2;
+  const int64_t total = rows * c4n;
+  const int64_t slice = rows * pcols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / c4n;
+    const int c = static_cast<int>(i - r * c4n) * 4;
+    const float* src = part + r * pcols + c;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), u = a;
+    for (int s = 0; s < ks; ++s) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + s * slice));
+      a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+      if (swiglu) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(src + s * slice + seg));
+        u.x += w.x; u.y += w.y; u.z += w.z; u.w += w.w;
+      }
+    }
+    if (swiglu) {
+      a.x = silu_mul(a.x, u.x);
+      a.y = silu_mul(a.y, u.y);
+      a.z = silu_mul(a.z, u.z);
+      a.w = silu_mul(a.w, u.w);
+    }
+    uint2 o;
+    o.x = pack2(a.x, a.y);
+    o.y = pack2(a.z, a.w);
+    *reinterpret_cast<uint2*>(out + r * ldo + c) = o;
+  }
+}
+
 // ---- host side --------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 cudaError_t g_encode_err = cudaSuccess;
-bool g_attr_set[3][64] = {};
+bool g_attr_set[4][64] = {};
 std::mutex g_attr_mutex;
 
 int get_encode(PFN_cuTensorMapEncodeTiled_v12000* fn) {
@@ -687,7 +762,8 @@ int check_problem(const Problem& pr) {
   DS_REQUIRE(pr.n_tiles >= 1 && pr.weight_group_mod >= 1, "gemm: bad tiling");
   DS_REQUIRE(pr.seg_cols >= 0 && pr.seg_cols % 8 == 0, "gemm: seg_cols must be a multiple of 8");
   DS_REQUIRE(pr.a_rows < (1LL << 31) && pr.b_rows < (1LL << 31), "gemm: too many rows");
-  DS_REQUIRE(pr.epilogue == kPlain || pr.epilogue == kSwiGLU || pr.epilogue == kRouter,
+  DS_REQUIRE(pr.epilogue == kPlain || pr.epilogue == kSwiGLU || pr.epilogue == kRouter ||
+                 pr.epilogue == kPartial,
              "gemm: unknown epilogue %d", pr.epilogue);
   return DS_OK;
 }
@@ -710,8 +786,15 @@ ProbParams prob_params_of(const Problem& pr) {
   q.out = static_cast<__nv_bfloat16*>(pr.out);
   q.ldo = pr.ldo;
   q.out_row_map = pr.out_row_map;
+  q.k_splits = 1;
   q.kb_per_split = (q.k_blocks + pr.n_tiles - 1) / pr.n_tiles;
   q.logits_out = pr.logits_out;
+  q.partial_cols = 0;
+  if (pr.epilogue == kPartial) {
+    q.k_splits = pr.k_splits;
+    q.kb_per_split = (q.k_blocks + pr.k_splits - 1) / pr.k_splits;
+    q.partial_cols = q.paired ? 2 * q.seg_cols : q.seg_cols;
+  }
   q.wait_flag = pr.wait_flag;
   q.wait_target = pr.wait_target;
   q.out_meta = pr.out_meta;
@@ -741,9 +824,10 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
   {
     std::lock_guard<std::mutex> lock(g_attr_mutex);
     if (!g_attr_set[epi][di.device]) {
-      const void* fn = epi == kSwiGLU  ? reinterpret_cast<const void*>(grouped_gemm_kernel<kSwiGLU>)
-                       : epi == kRouter ? reinterpret_cast<const void*>(grouped_gemm_kernel<kRouter>)
-                                        : reinterpret_cast<const void*>(grouped_gemm_kernel<kPlain>);
+      const void* fn = epi == kSwiGLU   ? reinterpret_cast<const void*>(grouped_gemm_kernel<kSwiGLU>)
+                       : epi == kRouter  ? reinterpret_cast<const void*>(grouped_gemm_kernel<kRouter>)
+                       : epi == kPartial ? reinterpret_cast<const void*>(grouped_gemm_kernel<kPartial>)
+                                         : reinterpret_cast<const void*>(grouped_gemm_kernel<kPlain>);
       DS_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(kSmemBytes)));
       g_attr_set[epi][di.device] = true;
@@ -764,11 +848,13 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
     DS_TRY(make_tmap(&tmB[i], pr.B, pr.b_rows, pr.K));
     p.pr[i] = prob_params_of(pr);
     // output rows = A rows, in order: stores leave through TMA (box = one warp's slab)
-    if (pr.epilogue != kRouter && pr.out_row_map == nullptr && pr.out_meta == nullptr) {
+    if (pr.epilogue != kRouter && pr.epilogue != kPartial && pr.out_row_map == nullptr &&
+        pr.out_meta == nullptr) {
       DS_TRY(make_tmap(&tmO[i], pr.out, pr.a_rows, pr.ldo, 32u));
       p.pr[i].tma_out = 1;
     }
-    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles;
+    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles *
+                 p.pr[i].k_splits;
     if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
     // a cross-GPU wait may legitimately hold the pipeline: every wait gets its bound
     if (pr.wait_timeout_cycles > p.timeout_cycles) p.timeout_cycles = pr.wait_timeout_cycles;
@@ -790,15 +876,68 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
     grouped_gemm_kernel<kSwiGLU><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
   else if (epi == kRouter)
     grouped_gemm_kernel<kRouter><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
+  else if (epi == kPartial)
+    grouped_gemm_kernel<kPartial><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
   else
     grouped_gemm_kernel<kPlain><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
   DS_LAUNCH_CHECK("grouped_gemm_kernel");
   return DS_OK;
 }
 
+int choose_k_splits(const Problem& pr, int num_sms) {
+  if (pr.offsets != nullptr || pr.out_row_map != nullptr || pr.out_meta != nullptr ||
+      pr.wait_flag != nullptr || (pr.epilogue != kPlain && pr.epilogue != kSwiGLU))
+    return 1;
+  const int64_t tiles = (pr.a_rows + BM - 1) / BM * pr.n_tiles;
+  const int k_blocks = (pr.K + BK - 1) / BK;
+  if (tiles * 2 >= num_sms || k_blocks < 8) return 1;
+  int ks = static_cast<int>((num_sms + tiles - 1) / tiles);
+  if (ks > k_blocks / 4) ks = k_blocks / 4;  // at least four k-blocks per slice
+  if (ks > 32) ks = 32;
+  return ks < 2 ? 1 : ks;
+}
+
+size_t partial_bytes(const Problem& pr, int k_splits) {
+  if (k_splits <= 1) return 0;
+  const bool paired = pr.b_tile_stride == 128;
+  const int64_t seg = pr.seg_cols > 0 ? pr.seg_cols : (paired ? pr.b_half1_off : pr.n_tiles * 256);
+  const int64_t cols = paired ? 2 * seg : seg;
+  return static_cast<size_t>(k_splits) * pr.a_rows * cols * sizeof(float);
+}
+
 int launch(const Problem& pr, cudaStream_t s) {
-  const Problem* one[1] = {&pr};
-  return launch_multi(one, 1, s, nullptr);
+  if (pr.k_splits <= 1) {
+    const Problem* one[1] = {&pr};
+    return launch_multi(one, 1, s, nullptr);
+  }
+  // split-K: raw f32 partials of every K slice, then the reduce applies the epilogue
+  DS_REQUIRE(pr.offsets == nullptr && pr.partial != nullptr &&
+                 aligned16(pr.partial) && (pr.epilogue == kPlain || pr.epilogue == kSwiGLU),
+             "gemm: split-K needs a dense plain/SwiGLU problem and a partial buffer");
+  const bool paired = pr.b_tile_stride == 128;
+  const int seg = pr.seg_cols > 0 ? pr.seg_cols : (paired ? pr.b_half1_off : pr.n_tiles * 256);
+  const int pcols = paired ? 2 * seg : seg;
+  DS_REQUIRE(seg % 4 == 0, "gemm: split-K needs output widths that are multiples of 4");
+  // slices of ceil(k_blocks / k_splits) k-blocks; the count is trimmed so none is empty
+  const int k_blocks = (pr.K + BK - 1) / BK;
+  const int per = (k_blocks + pr.k_splits - 1) / pr.k_splits;
+  const int ks = (k_blocks + per - 1) / per;
+  Problem q = pr;
+  q.epilogue = kPartial;
+  q.k_splits = ks;
+  q.logits_out = pr.partial;
+  const Problem* one[1] = {&q};
+  DeviceInfo di;
+  DS_TRY(device_info(&di));
+  DS_TRY(launch_multi(one, 1, s, nullptr));
+  const int64_t items = pr.a_rows * ((pr.epilogue == kSwiGLU ? seg : pcols) / 4);
+  int64_t grid = (items + 255) / 256;
+  if (grid > static_cast<int64_t>(di.num_sms) * 8) grid = static_cast<int64_t>(di.num_sms) * 8;
+  splitk_reduce_kernel<<<static_cast<int>(grid > 0 ? grid : 1), 256, 0, s>>>(
+      pr.partial, ks, pr.a_rows, pcols, pr.epilogue == kSwiGLU ? 1 : 0, seg,
+      static_cast<__nv_bfloat16*>(pr.out), pr.ldo);
+  DS_LAUNCH_CHECK("splitk_reduce_kernel");
+  return DS_OK;
 }
 
 int launch_zero_uncovered(void* out, int64_t S, int ldo, const int32_t* offsets, int groups,

@@ -58,7 +58,9 @@ int launch_swiglu(const void* in, void* out, int64_t rows, int I, cudaStream_t s
 
 namespace gemm {
 
-enum Epilogue : int { kPlain = 0, kSwiGLU = 1, kRouter = 2 };
+// kPartial is internal: a split-K launch of a kPlain / kSwiGLU problem writes raw f32 partial
+// accumulators, and a reduce kernel applies the problem's own epilogue.
+enum Epilogue : int { kPlain = 0, kSwiGLU = 1, kRouter = 2, kPartial = 3 };
 
 // Grouped / dense bf16 GEMM on tcgen05: for each row group g (rows [off[g], off[g+1]) of A)
 // out[rows, cols] = A[rows, :] @ B_w[...]^T with w = g % weight_group_mod.  B rows for
@@ -86,6 +88,12 @@ struct Problem {
   // Paired layout (b_tile_stride 128: gate | up halves) = I; contiguous (256) = N.  A
   // multiple of 8; columns past it are computed but not stored.
   int seg_cols = 0;
+  // split-K (dense problems, no row map / cross-GPU hooks): k_splits > 1 slices the K blocks
+  // over that many tiles per output tile; each writes raw f32 partials to `partial`
+  // [k_splits, a_rows, partial_cols] and a reduce kernel sums them into `out` through the
+  // problem's epilogue.  partial_cols = 2*seg_cols (paired layout) or seg_cols.
+  int k_splits = 1;
+  float* partial = nullptr;
   // router epilogue (epilogue == kRouter): B = split gate [256, K]; n_tiles = number of K
   // slices; slice s writes its raw accumulator columns [0, 192) as f32 to
   // logits_out + (s * a_rows + row) * 192
@@ -110,6 +118,11 @@ struct Signal {
 };
 
 int launch(const Problem& pr, cudaStream_t s);
+
+// K splits worth using for a dense problem on `num_sms` SMs: 1 unless its output tiles leave
+// most SMs idle; bytes of the partial buffer that needs (0 for 1 split).
+int choose_k_splits(const Problem& pr, int num_sms);
+size_t partial_bytes(const Problem& pr, int k_splits);
 
 // One persistent launch over up to two problems with the same epilogue (their tiles are
 // enumerated one problem after the other; null or empty problems are skipped).

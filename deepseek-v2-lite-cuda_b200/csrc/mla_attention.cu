@@ -691,9 +691,10 @@ size_t ds_mla_forward_workspace_size(int batch, int seq, int hidden, int heads) 
 namespace ds {
 namespace dec {
 int launch_cache_append(const void* src_lat, int lat_ld, const void* src_kpe, int kpe_ld,
-                        int src_bstride, int batch, int n_new, int pos0, int max_seq,
-                        int copy_raw, void* c_lat, void* c_kpe, float* c_rstd, void* c_kpe_rot,
-                        const void* cos_t, const void* sin_t, float eps, cudaStream_t s);
+                        int src_bstride, int batch, int n_new, int pos0, const int* pos0_dev,
+                        int max_seq, int copy_raw, void* c_lat, void* c_kpe, float* c_rstd,
+                        void* c_kpe_rot, const void* cos_t, const void* sin_t, float eps,
+                        cudaStream_t s);
 }  // namespace dec
 }  // namespace ds
 
@@ -744,7 +745,8 @@ int mla_forward_impl(const void* x_bf16, const void* w_qkv_a_bf16, const float* 
     // the prompt's raw latents and k_pe (before the in-place RoPE below) into the cache
     const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(b.qkv);
     DS_TRY(ds::dec::launch_cache_append(q + heads * 192, ldq, q + heads * 192 + kLatent, ldq, seq,
-                                        batch, seq, cache->pos0, cache->max_seq, 1, cache->latent,
+                                        batch, seq, cache->pos0, nullptr, cache->max_seq, 1,
+                                        cache->latent,
                                         cache->kpe, cache->rstd, cache->kpe_rot, cos_bf16,
                                         sin_bf16, eps, s));
   }

@@ -61,6 +61,7 @@ constexpr long long kTimeoutCycles = 4000000000LL;
 
 struct Params {
   int batch, max_seq, len, nsplit, chunks_per_split;
+  const int* len_dev;  // when set: the cached length before this token, read on the device
   const float* rstd;   // [batch * max_seq]
   float scale_log2;
   float* part_o;       // [batch][nsplit][16][512]
@@ -93,8 +94,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int b = blockIdx.x / p.nsplit;
   const int split = blockIdx.x - b * p.nsplit;
+  const int len = p.len_dev != nullptr ? *p.len_dev + 1 : p.len;
   const int t_begin = split * p.chunks_per_split * kChunk;
-  const int t_end = min(p.len, t_begin + p.chunks_per_split * kChunk);
+  const int t_end = min(len, t_begin + p.chunks_per_split * kChunk);
   const int nchunk = t_end > t_begin ? (t_end - t_begin + kChunk - 1) / kChunk : 0;
   const int row0 = b * p.max_seq;
 
@@ -402,7 +404,8 @@ __global__ void __launch_bounds__(128)
 __global__ void __launch_bounds__(256)
     cache_append_kernel(const __nv_bfloat16* __restrict__ src_lat, int lat_ld,
                         const __nv_bfloat16* __restrict__ src_kpe, int kpe_ld, int src_bstride,
-                        int batch, int n_new, int pos0, int max_seq, int copy_raw,
+                        int batch, int n_new, int pos0, const int* pos0_dev, int max_seq,
+                        int copy_raw,
                         __nv_bfloat16* c_lat, __nv_bfloat16* c_kpe, float* __restrict__ c_rstd,
                         __nv_bfloat16* __restrict__ c_kpe_rot,
                         const __nv_bfloat16* __restrict__ cos_t,
@@ -411,7 +414,7 @@ __global__ void __launch_bounds__(256)
   const int64_t w = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   if (w >= static_cast<int64_t>(batch) * n_new) return;
   const int b = static_cast<int>(w / n_new), i = static_cast<int>(w - static_cast<int64_t>(b) * n_new);
-  const int pos = pos0 + i;
+  const int pos = (pos0_dev != nullptr ? *pos0_dev : pos0) + i;
   const int64_t srow = static_cast<int64_t>(b) * src_bstride + i;
   const int64_t dst = static_cast<int64_t>(b) * max_seq + pos;
   // latent: 512 = 32 lanes x 16 elements
@@ -452,12 +455,14 @@ __global__ void __launch_bounds__(256)
 // projection row of sequence b.  One warp per (sequence, head).
 __global__ void __launch_bounds__(256)
     decode_q_kernel(const __nv_bfloat16* __restrict__ proj, int ld, int qpe_col, int batch,
-                    int heads, int pos, const __nv_bfloat16* __restrict__ cos_t,
+                    int heads, int pos_host, const int* pos_dev,
+                    const __nv_bfloat16* __restrict__ cos_t,
                     const __nv_bfloat16* __restrict__ sin_t, __nv_bfloat16* __restrict__ q) {
   const int lane = threadIdx.x & 31;
   const int64_t w = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   if (w >= static_cast<int64_t>(batch) * heads) return;
   const int b = static_cast<int>(w / heads), h = static_cast<int>(w - static_cast<int64_t>(b) * heads);
+  const int pos = pos_dev != nullptr ? *pos_dev : pos_host;
   const __nv_bfloat16* row = proj + static_cast<int64_t>(b) * ld;
   __nv_bfloat16* dst = q + w * kQCols;
   const uint4* s4 = reinterpret_cast<const uint4*>(row + h * kLatent) + 2 * lane;
@@ -513,16 +518,20 @@ int nsplit_for(int batch, int len, int num_sms, int* chunks_per_split) {
 
 }  // namespace
 
+// The cache's device-side length += n (one thread), after the step's kernels have used it.
+__global__ void len_add_kernel(int* len, int n) { *len += n; }
+
 int launch_cache_append(const void* src_lat, int lat_ld, const void* src_kpe, int kpe_ld,
-                        int src_bstride, int batch, int n_new, int pos0, int max_seq,
-                        int copy_raw, void* c_lat, void* c_kpe, float* c_rstd, void* c_kpe_rot,
-                        const void* cos_t, const void* sin_t, float eps, cudaStream_t s) {
+                        int src_bstride, int batch, int n_new, int pos0, const int* pos0_dev,
+                        int max_seq, int copy_raw, void* c_lat, void* c_kpe, float* c_rstd,
+                        void* c_kpe_rot, const void* cos_t, const void* sin_t, float eps,
+                        cudaStream_t s) {
   const int64_t warps = static_cast<int64_t>(batch) * n_new;
   if (warps == 0) return DS_OK;
   cache_append_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, s>>>(
       static_cast<const __nv_bfloat16*>(src_lat), lat_ld,
       static_cast<const __nv_bfloat16*>(src_kpe), kpe_ld, src_bstride, batch, n_new, pos0,
-      max_seq, copy_raw, static_cast<__nv_bfloat16*>(c_lat), static_cast<__nv_bfloat16*>(c_kpe),
+      pos0_dev, max_seq, copy_raw, static_cast<__nv_bfloat16*>(c_lat), static_cast<__nv_bfloat16*>(c_kpe),
       c_rstd, static_cast<__nv_bfloat16*>(c_kpe_rot), static_cast<const __nv_bfloat16*>(cos_t),
       static_cast<const __nv_bfloat16*>(sin_t), eps);
   DS_LAUNCH_CHECK("cache_append_kernel");
@@ -540,13 +549,15 @@ size_t attn_workspace(int batch, int len, int num_sms) {
 // 576] bf16; out: o_lat [batch, 16*512] bf16.
 int launch_decode_attention(const void* q, const void* c_lat, const float* c_rstd,
                             const void* c_kpe_rot, int batch, int max_seq, int len,
-                            float softmax_scale, void* out, void* workspace, size_t ws_bytes,
-                            cudaStream_t s) {
+                            const int* len_dev, float softmax_scale, void* out, void* workspace,
+                            size_t ws_bytes, cudaStream_t s) {
   DeviceInfo di;
   DS_TRY(device_info(&di));
   int cps = 1;
-  const int ns = nsplit_for(batch, len, di.num_sms, &cps);
-  DS_REQUIRE(ws_bytes >= attn_workspace(batch, len, di.num_sms), "decode attention: workspace");
+  // with the length on the device the splits cover max_seq; splits past the length exit
+  const int ns = nsplit_for(batch, len_dev != nullptr ? max_seq : len, di.num_sms, &cps);
+  DS_REQUIRE(ws_bytes >= attn_workspace(batch, len_dev != nullptr ? max_seq : len, di.num_sms),
+             "decode attention: workspace");
   {
     std::lock_guard<std::mutex> lock(g_attr_mutex);
     if (!g_attr_set[di.device]) {
@@ -564,6 +575,7 @@ int launch_decode_attention(const void* q, const void* c_lat, const float* c_rst
   p.batch = batch;
   p.max_seq = max_seq;
   p.len = len;
+  p.len_dev = len_dev;
   p.nsplit = ns;
   p.chunks_per_split = cps;
   p.rstd = c_rstd;
@@ -583,10 +595,11 @@ int launch_decode_attention(const void* q, const void* c_lat, const float* c_rst
 }
 
 int launch_decode_q(const void* proj, int ld, int qpe_col, int batch, int heads, int pos,
-                    const void* cos_t, const void* sin_t, void* q, cudaStream_t s) {
+                    const int* pos_dev, const void* cos_t, const void* sin_t, void* q,
+                    cudaStream_t s) {
   const int64_t warps = static_cast<int64_t>(batch) * heads;
   decode_q_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(proj), ld, qpe_col, batch, heads, pos,
+      static_cast<const __nv_bfloat16*>(proj), ld, qpe_col, batch, heads, pos, pos_dev,
       static_cast<const __nv_bfloat16*>(cos_t), static_cast<const __nv_bfloat16*>(sin_t),
       static_cast<__nv_bfloat16*>(q));
   DS_LAUNCH_CHECK("decode_q_kernel");
@@ -604,21 +617,44 @@ constexpr int kDecHeads = 16;
 int dec_proj_cols(int heads) { return heads * 512 + heads * 64 + 512 + 64; }
 
 struct DecBuffers {
-  void* proj;  // bf16 [batch, dec_proj_cols]
-  void* q;     // bf16 [batch*16, 576]
-  void* olat;  // bf16 [batch, 16*512]
-  void* attn;  // f32 partials
+  void* proj;      // bf16 [batch, dec_proj_cols]
+  void* q;         // bf16 [batch*16, 576]
+  void* olat;      // bf16 [batch, 16*512]
+  void* attn;      // f32 attention partials
+  float* partial;  // f32 split-K partials of the two projections
 };
 
-size_t carve_dec(ds::Carve& c, DecBuffers* b, int batch, int max_seq, int num_sms) {
+ds::gemm::Problem dense(const void* A, int64_t rows, int K, const void* B, int N, void* out);
+
+// the decode step's projections: x [batch, hidden] -> proj, and o_lat -> out; with 64 rows
+// their output tiles leave most SMs idle, so they run split-K
+size_t dec_partial_bytes(int batch, int hidden, int num_sms) {
+  ds::gemm::Problem a = dense(nullptr, batch, hidden, nullptr, dec_proj_cols(kDecHeads), nullptr);
+  ds::gemm::Problem o = dense(nullptr, batch, kDecHeads * 512, nullptr, hidden, nullptr);
+  const size_t pa = ds::gemm::partial_bytes(a, ds::gemm::choose_k_splits(a, num_sms));
+  const size_t po = ds::gemm::partial_bytes(o, ds::gemm::choose_k_splits(o, num_sms));
+  return pa > po ? pa : po;
+}
+
+size_t carve_dec(ds::Carve& c, DecBuffers* b, int batch, int max_seq, int hidden, int num_sms) {
   DecBuffers x{};
   x.proj = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * dec_proj_cols(kDecHeads));
   x.q = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * kDecHeads * 576);
   x.olat = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * kDecHeads * 512);
   const size_t aw = ds::dec::attn_workspace(batch, max_seq, num_sms);
   x.attn = c.take<uint8_t>(aw);
+  x.partial = c.take<float>(dec_partial_bytes(batch, hidden, num_sms) / sizeof(float));
   if (b) *b = x;
   return ds::align_up(c.used, 256);
+}
+
+// a dense problem; `partial` set: split-K when the output tiles leave most SMs idle
+ds::gemm::Problem dense_split(const void* A, int64_t rows, int K, const void* B, int N, void* out,
+                              float* partial, int num_sms) {
+  ds::gemm::Problem p = dense(A, rows, K, B, N, out);
+  p.k_splits = ds::gemm::choose_k_splits(p, num_sms);
+  p.partial = partial;
+  return p;
 }
 
 ds::gemm::Problem dense(const void* A, int64_t rows, int K, const void* B, int N, void* out) {
@@ -661,25 +697,25 @@ int ds_mla_cache_append(const void* latent_bf16, int latent_ld, const void* kpe_
                  ds::aligned16(kpe_bf16),
              "mla_cache_append: rows must start on 16-byte boundaries");
   return ds::dec::launch_cache_append(latent_bf16, latent_ld, kpe_bf16, kpe_ld, src_rows_per_seq,
-                                      batch, new_tokens, pos0, max_seq, copy_raw,
+                                      batch, new_tokens, pos0, nullptr, max_seq, copy_raw,
                                       cache_latent_bf16, cache_kpe_bf16, cache_rstd,
                                       cache_kpe_rot_bf16, cos_bf16, sin_bf16, eps,
                                       static_cast<cudaStream_t>(stream));
 }
 
-size_t ds_mla_decode_workspace_size(int batch, int max_seq) {
+size_t ds_mla_decode_workspace_size(int batch, int max_seq, int hidden) {
   ds::DeviceInfo di;
   if (ds::device_info(&di) != DS_OK) return 0;
   ds::Carve c(nullptr, 0);
-  return carve_dec(c, nullptr, batch, max_seq, di.num_sms);
+  return carve_dec(c, nullptr, batch, max_seq, hidden, di.num_sms);
 }
 
 int ds_mla_decode_step(const void* x_bf16, const void* w_dec_bf16, const void* w_out_bf16,
                        const void* cos_bf16, const void* sin_bf16, void* cache_latent_bf16,
                        void* cache_kpe_bf16, float* cache_rstd, void* cache_kpe_rot_bf16,
-                       int batch, int max_seq, int cache_len, int hidden, int heads, float eps,
-                       float softmax_scale, void* out_bf16, void* workspace,
-                       size_t workspace_bytes, void** events, void* stream) {
+                       int batch, int max_seq, int cache_len, int32_t* cache_len_dev, int hidden,
+                       int heads, float eps, float softmax_scale, void* out_bf16,
+                       void* workspace, size_t workspace_bytes, void** events, void* stream) {
   DS_REQUIRE(batch >= 0 && hidden > 0 && hidden % 8 == 0, "mla_decode_step: bad shape");
   DS_REQUIRE(heads == kDecHeads, "mla_decode_step: %d heads (the decode kernel serves 16)", heads);
   DS_REQUIRE(cache_len >= 0 && cache_len < max_seq, "mla_decode_step: cache is full");
@@ -697,27 +733,35 @@ int ds_mla_decode_step(const void* x_bf16, const void* w_dec_bf16, const void* w
   DS_TRY(ds::device_info(&di));
   ds::Carve c(workspace, workspace_bytes);
   DecBuffers b;
-  carve_dec(c, &b, batch, max_seq, di.num_sms);
+  carve_dec(c, &b, batch, max_seq, hidden, di.num_sms);
   if (!c.ok()) return ds::fail(DS_ERR_WORKSPACE, "mla_decode_step: workspace needs %zu bytes", c.used);
   const int P = dec_proj_cols(heads);
   const int qpe_col = heads * 512, lat_col = qpe_col + heads * 64, kpe_col = lat_col + 512;
   DS_TRY(mark(0));
-  DS_TRY(ds::gemm::launch(dense(x_bf16, batch, hidden, w_dec_bf16, P, b.proj), s));
+  DS_TRY(ds::gemm::launch(
+      dense_split(x_bf16, batch, hidden, w_dec_bf16, P, b.proj, b.partial, di.num_sms), s));
   DS_TRY(mark(1));
   DS_TRY(ds::dec::launch_cache_append(static_cast<const __nv_bfloat16*>(b.proj) + lat_col, P,
                                       static_cast<const __nv_bfloat16*>(b.proj) + kpe_col, P, 1,
-                                      batch, 1, cache_len, max_seq, 1, cache_latent_bf16,
+                                      batch, 1, cache_len, cache_len_dev, max_seq, 1,
+                                      cache_latent_bf16,
                                       cache_kpe_bf16, cache_rstd, cache_kpe_rot_bf16, cos_bf16,
                                       sin_bf16, eps, s));
-  DS_TRY(ds::dec::launch_decode_q(b.proj, P, qpe_col, batch, heads, cache_len, cos_bf16, sin_bf16,
-                                  b.q, s));
+  DS_TRY(ds::dec::launch_decode_q(b.proj, P, qpe_col, batch, heads, cache_len, cache_len_dev,
+                                  cos_bf16, sin_bf16, b.q, s));
   DS_TRY(mark(2));
   DS_TRY(ds::dec::launch_decode_attention(b.q, cache_latent_bf16, cache_rstd, cache_kpe_rot_bf16,
-                                          batch, max_seq, cache_len + 1, softmax_scale, b.olat,
-                                          b.attn, ds::dec::attn_workspace(batch, max_seq, di.num_sms),
-                                          s));
+                                          batch, max_seq, cache_len + 1, cache_len_dev,
+                                          softmax_scale, b.olat, b.attn,
+                                          ds::dec::attn_workspace(batch, max_seq, di.num_sms), s));
+  if (cache_len_dev != nullptr) {
+    ds::dec::len_add_kernel<<<1, 1, 0, s>>>(cache_len_dev, 1);
+    DS_LAUNCH_CHECK("len_add_kernel");
+  }
   DS_TRY(mark(3));
-  DS_TRY(ds::gemm::launch(dense(b.olat, batch, heads * 512, w_out_bf16, hidden, out_bf16), s));
+  DS_TRY(ds::gemm::launch(dense_split(b.olat, batch, heads * 512, w_out_bf16, hidden, out_bf16,
+                                      b.partial, di.num_sms),
+                          s));
   DS_TRY(mark(4));
   return DS_OK;
 }

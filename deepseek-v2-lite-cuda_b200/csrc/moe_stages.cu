@@ -236,6 +236,44 @@ int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16, const vo
   return ds::gemm::launch(g2, s);
 }
 
+size_t ds_dense_mlp_workspace_size(int num_rows, int hidden_size, int intermediate_size) {
+  ds::DeviceInfo di;
+  if (ds::device_info(&di) != DS_OK || num_rows <= 0) return 0;
+  const int H = hidden_size, I = intermediate_size;
+  ds::gemm::Problem g1 = ds::mlp_gemm1(nullptr, num_rows, H, nullptr, 2 * static_cast<int64_t>(I),
+                                       nullptr, 1, I, nullptr);
+  ds::gemm::Problem g2 = ds::mlp_gemm2(nullptr, num_rows, I, nullptr, H, nullptr, 1, H, nullptr,
+                                       nullptr);
+  const size_t p1 = ds::gemm::partial_bytes(g1, ds::gemm::choose_k_splits(g1, di.num_sms));
+  const size_t p2 = ds::gemm::partial_bytes(g2, ds::gemm::choose_k_splits(g2, di.num_sms));
+  return ds::align_up(p1 > p2 ? p1 : p2, 256);
+}
+
+int ds_dense_mlp_ws(const void* x_bf16, int num_rows, const void* w1_bf16, const void* w2_bf16,
+                    int hidden_size, int intermediate_size, void* h_bf16, void* out_bf16,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  const int H = hidden_size, I = intermediate_size;
+  DS_REQUIRE(num_rows >= 0, "dense_mlp: bad shape");
+  DS_REQUIRE(H > 0 && I > 0 && H % 8 == 0 && I % 8 == 0,
+             "dense_mlp: hidden_size and intermediate_size must be positive multiples of 8");
+  if (num_rows == 0) return DS_OK;
+  DS_REQUIRE(x_bf16 && w1_bf16 && w2_bf16 && h_bf16 && out_bf16, "dense_mlp: null pointer");
+  DS_REQUIRE(workspace_bytes >= ds_dense_mlp_workspace_size(num_rows, H, I),
+             "dense_mlp: workspace needs %zu bytes", ds_dense_mlp_workspace_size(num_rows, H, I));
+  ds::DeviceInfo di;
+  DS_TRY(ds::device_info(&di));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ds::gemm::Problem g1 = ds::mlp_gemm1(x_bf16, num_rows, H, w1_bf16, 2 * static_cast<int64_t>(I),
+                                       nullptr, 1, I, h_bf16);
+  ds::gemm::Problem g2 = ds::mlp_gemm2(h_bf16, num_rows, I, w2_bf16, H, nullptr, 1, H, out_bf16,
+                                       nullptr);
+  g1.k_splits = ds::gemm::choose_k_splits(g1, di.num_sms);
+  g2.k_splits = ds::gemm::choose_k_splits(g2, di.num_sms);
+  g1.partial = g2.partial = static_cast<float*>(workspace);
+  DS_TRY(ds::gemm::launch(g1, s));
+  return ds::gemm::launch(g2, s);
+}
+
 int ds_dense_gemm1_swiglu(const void* x_bf16, int num_rows, const void* w1_bf16,
                           int hidden_size, int intermediate_size, void* h_bf16, int max_ctas,
                           void* stream) {

@@ -75,9 +75,9 @@ SIGNATURES = {
                             _vp, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "ds_mla_cache_append": (_i, [_vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp,
                                  _vp, _vp, _f, _vp]),
-    "ds_mla_decode_workspace_size": (_sz, [_i, _i]),
-    "ds_mla_decode_step": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
-                                _f, _f, _vp, _vp, _sz, _vp, _vp]),
+    "ds_mla_decode_workspace_size": (_sz, [_i, _i, _i]),
+    "ds_mla_decode_step": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i,
+                                _i, _f, _f, _vp, _vp, _sz, _vp, _vp]),
     "ds_moe_layer_workspace_routing": (_i, [_i, _i, _i, _i, _i, _i, ctypes.POINTER(_sz),
                                             ctypes.POINTER(_sz), ctypes.POINTER(_sz)]),
     "ds_moe_layer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i,
@@ -88,6 +88,8 @@ SIGNATURES = {
                                    _sz, _vp]),
     "ds_moe_expert_mlp": (_i, [_vp, _i, _vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
     "ds_dense_mlp": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp, _vp, _i, _vp]),
+    "ds_dense_mlp_workspace_size": (_sz, [_i, _i, _i]),
+    "ds_dense_mlp_ws": (_i, [_vp, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _sz, _vp]),
     "ds_router_weight_split": (_i, [_vp, _i, _i, _vp, _vp]),
     "ds_dense_gemm1_swiglu": (_i, [_vp, _i, _vp, _i, _i, _vp, _i, _vp]),
     "ds_dense_gemm2": (_i, [_vp, _i, _vp, _i, _i, _vp, _i, _vp]),
@@ -684,7 +686,7 @@ def mla_prefill(hidden_states: torch.Tensor, w_qkv_a: torch.Tensor,
                                    _ptr(cache.k_pe_cache), _ptr(cache.rstd), _ptr(cache.k_pe_rot),
                                    cache.max_seq, 0, _ptr(workspace), workspace.numel(),
                                    _stream(x)), "mla_prefill")
-    cache._advance(S, cos, sin, eps)
+    cache._advance(S, device_counted=False)
     return out
 
 
@@ -710,8 +712,8 @@ def mla_cache_append(latent: torch.Tensor, k_pe: torch.Tensor, cache, pos0: int,
                "mla_cache_append")
 
 
-def mla_decode_workspace_size(batch: int, max_seq: int) -> int:
-    return int(_lib.ds_mla_decode_workspace_size(batch, max_seq))
+def mla_decode_workspace_size(batch: int, max_seq: int, hidden: int) -> int:
+    return int(_lib.ds_mla_decode_workspace_size(batch, max_seq, hidden))
 
 
 def mla_decode_step(x: torch.Tensor, w_dec: torch.Tensor, w_out: torch.Tensor, cos: torch.Tensor,
@@ -725,7 +727,7 @@ def mla_decode_step(x: torch.Tensor, w_dec: torch.Tensor, w_out: torch.Tensor, c
     B, Hd = x.shape
     _require(cache.bsz == B, "mla_decode_step: cache batch size differs from x")
     out = torch.empty((B, Hd), dtype=torch.bfloat16, device=x.device)
-    need = mla_decode_workspace_size(B, cache.max_seq)
+    need = mla_decode_workspace_size(B, cache.max_seq, Hd)
     if workspace is None or workspace.numel() < need:
         workspace = _workspace(need, x.device)
     ev = None
@@ -741,10 +743,10 @@ def mla_decode_step(x: torch.Tensor, w_dec: torch.Tensor, w_out: torch.Tensor, c
         _check(_lib.ds_mla_decode_step(_ptr(x), _ptr(w_dec), _ptr(w_out), _ptr(cos), _ptr(sin),
                                        _ptr(cache.kv_latent), _ptr(cache.k_pe_cache),
                                        _ptr(cache.rstd), _ptr(cache.k_pe_rot), B, cache.max_seq,
-                                       cache.current_len, Hd, heads, float(eps),
+                                       cache.current_len, _ptr(cache.len_dev), Hd, heads, float(eps),
                                        float(softmax_scale), _ptr(out), _ptr(workspace),
                                        workspace.numel(), ev, _stream(x)), "mla_decode_step")
-    cache._advance(1, cos, sin, eps)
+    cache._advance(1, device_counted=True)
     return out
 
 
@@ -825,6 +827,24 @@ def dense_mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
     with _on_device(x):
         _check(_lib.ds_dense_mlp(_ptr(x), R, _ptr(w1), _ptr(w2), H, I, _ptr(h), _ptr(out),
                                  int(max_ctas), _stream(x)), "dense_mlp")
+    return out
+
+
+def dense_mlp_ws(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                 workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """dense_mlp whose GEMMs split K over the SMs when there are few rows (decode)."""
+    R, H = x.shape
+    I = w1.shape[0] // 2
+    out = torch.empty((R, H), dtype=torch.bfloat16, device=x.device)
+    if R == 0:
+        return out
+    h = torch.empty((R, I), dtype=torch.bfloat16, device=x.device)
+    need = int(_lib.ds_dense_mlp_workspace_size(R, H, I))
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(need, x.device)
+    with _on_device(x):
+        _check(_lib.ds_dense_mlp_ws(_ptr(x), R, _ptr(w1), _ptr(w2), H, I, _ptr(h), _ptr(out),
+                                    _ptr(workspace), workspace.numel(), _stream(x)), "dense_mlp")
     return out
 
 

@@ -57,6 +57,31 @@ class FusedMLA(nn.Module):
         self._dec_w = None
         self._dec_ws: Optional[torch.Tensor] = None
 
+    @classmethod
+    def from_weights(cls, w_q: torch.Tensor, w_kva: torch.Tensor, kv_norm_weight: torch.Tensor,
+                     w_kvb: torch.Tensor, w_o: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                     softmax_scale: float, heads: int = 16, eps: float = 1e-6) -> "FusedMLA":
+        """Build from the raw weights (the tensors DeepSeekMLA holds: q_proj [heads*192, H],
+        kv_a_proj_with_mqa [576, H], kv_a_layernorm [512], kv_b_proj [heads*256, 512], o_proj
+        [H, heads*128]) and the RoPE tables [positions, 64], all on one CUDA device."""
+        self = cls.__new__(cls)
+        nn.Module.__init__(self)
+        bf = torch.bfloat16
+        self.heads = heads
+        self.hidden = w_q.shape[1]
+        self.w_qkv_a = torch.cat([w_q.detach(), w_kva.detach()]).to(bf).contiguous()
+        self.kv_norm_weight = kv_norm_weight.detach().float().contiguous()
+        self.eps = float(eps)
+        self.w_kv_b = w_kvb.detach().to(bf).contiguous()
+        self.w_o = w_o.detach().to(bf).contiguous()
+        self.cos = cos.detach().to(bf).contiguous()
+        self.sin = sin.detach().to(bf).contiguous()
+        self.softmax_scale = float(softmax_scale)
+        self._ws = None
+        self._dec_w = None
+        self._dec_ws = None
+        return self
+
     def decode_weights(self):
         """(w_dec bf16 [heads*(512+64) + 576, hidden], w_out bf16 [hidden, heads*512]): the
         absorbed decode weights, built once from the module's bf16 weights in f32."""
@@ -95,7 +120,7 @@ class FusedMLA(nn.Module):
         if cache.current_len >= self.cos.shape[0]:
             raise RuntimeError("FusedMLA.decode: position beyond the RoPE tables")
         w_dec, w_out = self.decode_weights()
-        need = ds_kernels.mla_decode_workspace_size(x2.shape[0], cache.max_seq)
+        need = ds_kernels.mla_decode_workspace_size(x2.shape[0], cache.max_seq, self.hidden)
         if self._dec_ws is None or self._dec_ws.numel() < need or self._dec_ws.device != x.device:
             self._dec_ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
         out = ds_kernels.mla_decode_step(x2, w_dec, w_out, self.cos, self.sin, cache,

@@ -43,8 +43,12 @@ class LatentKVCache:
             self.rstd = torch.zeros((bsz, max_seq), dtype=torch.float32, device=self.device)
             self.k_pe_rot = torch.zeros((bsz, max_seq, rope_head_dim), dtype=dtype,
                                         device=self.device)
+            # the length on the device: the decode kernels read the position from it and
+            # advance it, so a captured CUDA graph of a decode step replays at successive
+            # positions (the host-side length is advanced alongside)
+            self.len_dev = torch.zeros((1,), dtype=torch.int32, device=self.device)
         else:
-            self.rstd = self.k_pe_rot = None
+            self.rstd = self.k_pe_rot = self.len_dev = None
 
     # ---- properties (reference surface) --------------------------------------------------
     @property
@@ -89,6 +93,8 @@ class LatentKVCache:
         self.kv_latent[:, slot, :] = compressed_kv.to(self.device, self.dtype)
         self.k_pe_cache[:, slot, :] = k_pe.to(self.device, self.dtype)
         self._len += new_tokens
+        if self.len_dev is not None:
+            self.len_dev.fill_(self._len)
 
     def get(self, seq_len: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
         """(kv_latent [bsz, seq_len, kv_lora_rank], k_pe [bsz, seq_len, rope_head_dim]) views."""
@@ -102,6 +108,8 @@ class LatentKVCache:
         """Clear the cache for a new sequence (keeps the memory)."""
         self._len = 0
         self._side_len = 0
+        if self.len_dev is not None:
+            self.len_dev.zero_()
 
     def __repr__(self) -> str:
         used_mb = (self._len * (self.kv_lora_rank + self.rope_head_dim)
@@ -133,10 +141,13 @@ class LatentKVCache:
                                         s0, cos, sin, eps, copy_raw=False)
             self._side_len = s1
 
-    def _advance(self, n: int, cos: torch.Tensor, sin: torch.Tensor, eps: float) -> None:
+    def _advance(self, n: int, device_counted: bool) -> None:
         """A fused kernel appended n tokens, side arrays included (the callers bring the side
-        arrays of earlier positions up to date before they launch)."""
+        arrays of earlier positions up to date before they launch); device_counted: the
+        kernels already advanced len_dev."""
         if self._side_len < self._len:
             raise RuntimeError("LatentKVCache: side arrays were stale when tokens were appended")
         self._len += n
         self._side_len = self._len
+        if not device_counted:
+            self.len_dev.fill_(self._len)

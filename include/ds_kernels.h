@@ -266,8 +266,11 @@ DS_API int ds_mla_prefill(const void* x_bf16, const void* w_qkv_a_bf16,
  * diag(g) W_uk_h^T W_q_nope_h, g the latent norm weight), the q_pe rows of q_proj, and
  * kv_a_proj_with_mqa; w_out bf16 [hidden, 16*512] = per head W_o_h W_uv_h diag(g).  Appends
  * the token at position cache_len, attends over positions 0 .. cache_len, writes out bf16
- * [batch, hidden].  `events`: NULL or DS_MLA_DECODE_NUM_EVENTS handles (projection, append +
- * query, attention, output projection). */
+ * [batch, hidden].  cache_len_dev: NULL, or a device int32 holding the cached length; the
+ * kernels then read the position from it (cache_len is only checked against max_seq), and
+ * the step adds 1 to it after its attention — so a captured CUDA graph of the step replays
+ * at successive positions.  `events`: NULL or DS_MLA_DECODE_NUM_EVENTS handles (projection,
+ * append + query, attention, output projection). */
 DS_API int ds_mla_cache_append(const void* latent_bf16, int latent_ld, const void* kpe_bf16,
                                int kpe_ld, int src_rows_per_seq, int batch, int new_tokens,
                                int pos0, int max_seq, int copy_raw, void* cache_latent_bf16,
@@ -275,14 +278,14 @@ DS_API int ds_mla_cache_append(const void* latent_bf16, int latent_ld, const voi
                                const void* cos_bf16, const void* sin_bf16, float eps,
                                void* stream);
 #define DS_MLA_DECODE_NUM_EVENTS 5
-DS_API size_t ds_mla_decode_workspace_size(int batch, int max_seq);
+DS_API size_t ds_mla_decode_workspace_size(int batch, int max_seq, int hidden);
 DS_API int ds_mla_decode_step(const void* x_bf16, const void* w_dec_bf16, const void* w_out_bf16,
                               const void* cos_bf16, const void* sin_bf16,
                               void* cache_latent_bf16, void* cache_kpe_bf16, float* cache_rstd,
                               void* cache_kpe_rot_bf16, int batch, int max_seq, int cache_len,
-                              int hidden, int heads, float eps, float softmax_scale,
-                              void* out_bf16, void* workspace, size_t workspace_bytes,
-                              void** events, void* stream);
+                              int32_t* cache_len_dev, int hidden, int heads, float eps,
+                              float softmax_scale, void* out_bf16, void* workspace,
+                              size_t workspace_bytes, void** events, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Fused MoE layer (new, additive; the pipeline of src/kernels/moe_fused.py:118-154 plus the
@@ -368,6 +371,14 @@ DS_API int ds_moe_expert_mlp(const void* rows_bf16, int num_rows, const int32_t*
 DS_API int ds_dense_mlp(const void* x_bf16, int num_rows, const void* w1_bf16,
                         const void* w2_bf16, int hidden_size, int intermediate_size,
                         void* h_bf16, void* out_bf16, int max_ctas, void* stream);
+/* ds_dense_mlp with a caller workspace (ds_dense_mlp_workspace_size; 0 bytes when no split
+ * is needed): for few rows (decode) the GEMMs split K over the SMs, f32 partials in the
+ * workspace reduced through the same epilogues. */
+DS_API size_t ds_dense_mlp_workspace_size(int num_rows, int hidden_size, int intermediate_size);
+DS_API int ds_dense_mlp_ws(const void* x_bf16, int num_rows, const void* w1_bf16,
+                           const void* w2_bf16, int hidden_size, int intermediate_size,
+                           void* h_bf16, void* out_bf16, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* ds_dense_gemm1_swiglu / ds_dense_gemm2: the two halves of ds_dense_mlp as separate
  *   launches (h = silu(x gate^T) * (x up^T); out = h w2^T), so each can overlap a different

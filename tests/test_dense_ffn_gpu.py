@@ -59,3 +59,17 @@ def test_layer0_dense_ffn_gemm1_halves():
     ref = gt / (1 + torch.exp(-gt)) * up
     hf = h.float().cpu()
     assert ((hf - ref).abs() <= 2e-2 + 2 ** -8 * ref.abs()).all()
+
+
+@pytest.mark.parametrize("T", [1, 64, 200])
+def test_layer0_dense_ffn_split_k(T):
+    # few rows: dense_mlp_ws splits the K loop of both GEMMs over the SMs (f32 partials in the
+    # workspace, summed in slice order, then the SwiGLU / plain epilogue)
+    import ds_kernels
+    w1, w2 = weights()
+    g = torch.Generator().manual_seed(100 + T)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    out = ds_kernels.dense_mlp_ws(x.cuda(), w1.cuda(), w2.cuda())
+    assert out.shape == (T, H)
+    check(out, oracle.dense_mlp(x, w1, w2))
+    assert int(ds_kernels.library().ds_dense_mlp_workspace_size(T, H, I_DENSE)) > 0
