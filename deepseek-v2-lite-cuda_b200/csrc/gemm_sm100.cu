@@ -24,7 +24,9 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -54,6 +56,15 @@ constexpr uint32_t kSlabBytes = 32 * 128;
 constexpr uint32_t kOutStageBytes = 4 * kSlabBytes;
 constexpr size_t kSmemBytes = 1024 + STAGES * (A_BYTES + B_BYTES) + kOutStageBytes + kTailBytes +
                               2 * kMaxProblems * kGroupStride * sizeof(int);
+// CTA-pair mode (cta_group::2): a 256 x 256 tile per pair of CTAs, each CTA loading its own
+// 128 A rows and one 128-row half of B per k-block (32 KB a stage), so the ring holds 6
+// stages in the same shared memory.
+constexpr int kPairStages = 6;
+constexpr size_t kPairSmemBytes = 1024 + kPairStages * (A_BYTES + B_HALF_BYTES) +
+                                  kOutStageBytes + kTailBytes +
+                                  2 * kMaxProblems * kGroupStride * sizeof(int);
+static_assert(kSmemBytes <= 227 * 1024 && kPairSmemBytes <= 227 * 1024, "shared memory");
+static_assert(8 * (2 * kPairStages + 5) + 24 <= kTailBytes, "tail holds the barriers");
 constexpr long long kDefaultTimeoutCycles = 4000000000LL;  // ~2 s at 2 GHz
 
 // One GEMM problem of a launch (fields as in Problem, kernels.cuh).
@@ -120,10 +131,13 @@ __device__ __forceinline__ const ProbParams& prob_params(const Params& p, int pb
   return pb ? p.pr[1] : p.pr[0];
 }
 
-// goff/gtile: per problem, kGroupStride row offsets and m-tile prefix; pstart[pb] = first
-// tile of problem pb.
+// goff/gtile: per problem, kGroupStride row offsets and m-tile prefix (m-tiles of TR rows);
+// pstart[pb] = first tile of problem pb.  In a CTA pair (TR = 256) CTA `rank` owns rows
+// [128 rank, 128 rank + 128) of the tile; its row count may be <= 0.
+template <int TR = BM>
 __device__ __forceinline__ TileInfo decode_tile(int t, const Params& p, const int* goff,
-                                                const int* gtile, const int* pstart) {
+                                                const int* gtile, const int* pstart,
+                                                int rank = 0) {
   TileInfo ti;
   ti.prob = (p.nprob > 1 && t >= pstart[1]) ? 1 : 0;
   const ProbParams& q = prob_params(p, ti.prob);
@@ -141,7 +155,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const Params& p, const in
     if (gt[mid] <= mtg) lo = mid;
     else hi = mid;
   }
-  ti.row0 = go[lo] + (mtg - gt[lo]) * BM;
+  ti.row0 = go[lo] + (mtg - gt[lo]) * TR + rank * BM;
   ti.rows = min(BM, go[lo + 1] - ti.row0);
   ti.brow0 = (lo % q.weight_group_mod) * q.b_rows_per_group + ti.nt * q.b_tile_stride;
   const int c0 = ti.nt * q.b_tile_stride;
@@ -356,7 +370,14 @@ __device__ __forceinline__ void epilogue_partial(uint32_t tb, bool valid, float*
   }
 }
 
-template <int EPI>
+// PAIR: the CTAs of a 2-CTA cluster share each 256 x 256 tile.  Both CTAs TMA-load their
+// own 128 A rows and one half of B, with every byte counted on the leader's (rank 0) full
+// barrier; the leader's MMA thread issues cta_group::2 MMAs (M = 256) that accumulate each
+// CTA's 128 rows in its own tensor memory, and commits to the stage-empty and
+// accumulator-full barriers of both CTAs; both CTAs' epilogue warps release an accumulator
+// on the leader's barrier (8 arrivals).  Neither CTA leaves before the other (cluster
+// barrier at the end), so no remote arrival can reach an exited CTA.
+template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA0,
                         const __grid_constant__ CUtensorMap tmB0,
@@ -364,19 +385,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmB1,
                         const __grid_constant__ CUtensorMap tmO0,
                         const __grid_constant__ CUtensorMap tmO1, const Params p) {
+  constexpr int NST = PAIR ? kPairStages : STAGES;        // ring stages
+  constexpr uint32_t BST = PAIR ? B_HALF_BYTES : B_BYTES;  // B bytes a stage in this CTA
+  constexpr int TR = PAIR ? 2 * BM : BM;                   // A rows of a tile
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t sA = ptx::smem_u32(smem);
-  const uint32_t sB = sA + STAGES * A_BYTES;
-  const uint32_t sOut = sA + STAGES * (A_BYTES + B_BYTES);  // 1024-aligned slabs
-  uint8_t* tail = smem + STAGES * (A_BYTES + B_BYTES) + kOutStageBytes;
+  const uint32_t sB = sA + NST * A_BYTES;
+  const uint32_t sOut = sA + NST * (A_BYTES + BST);  // 1024-aligned slabs
+  uint8_t* tail = smem + NST * (A_BYTES + BST) + kOutStageBytes;
   const uint32_t bar0 = ptx::smem_u32(tail);
   // barrier k lives at bar0 + 8k: full[0..S), empty[S..2S), tfull[2], tempty[2], drain
-  const uint32_t full0 = bar0, empty0 = bar0 + 8u * STAGES;
-  const uint32_t tfull0 = bar0 + 16u * STAGES, tempty0 = tfull0 + 16u;
+  const uint32_t full0 = bar0, empty0 = bar0 + 8u * NST;
+  const uint32_t tfull0 = bar0 + 16u * NST, tempty0 = tfull0 + 16u;
   const uint32_t drain_bar = tempty0 + 16u;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 8 * (2 * STAGES + 5));
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 8 * (2 * NST + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* never_flag = abort_flag + 1;
   int* pstart = const_cast<int*>(reinterpret_cast<volatile int*>(never_flag + 1));  // [3]
@@ -385,6 +409,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // tile stream: a pair walks the tiles as one unit
+  const int rank = PAIR ? static_cast<int>(ptx::cluster_ctarank()) : 0;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int nunits = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   for (int pb = 0; pb < p.nprob; ++pb) {
     const ProbParams& q = prob_params(p, pb);
@@ -392,13 +420,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       goff[pb * kGroupStride + i] = q.offsets ? __ldg(q.offsets + i) : (i == 0 ? 0 : q.dense_rows);
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       ptx::mbar_init(full0 + 8u * s, 1);
       ptx::mbar_init(empty0 + 8u * s, 1);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(tfull0 + 8u * a, 1);
-      ptx::mbar_init(tempty0 + 8u * a, 4);
+      ptx::mbar_init(tempty0 + 8u * a, PAIR ? 8 : 4);
     }
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -414,8 +442,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (warp == 1) {
-    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kTmemCols);
-    ptx::tmem_relinquish();
+    if constexpr (PAIR) {
+      ptx::tmem_alloc_pair(ptx::smem_u32(tmem_holder), kTmemCols);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kTmemCols);
+      ptx::tmem_relinquish();
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -428,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int g = 0; g < q.groups; ++g) {
         gt[g] = acc;
         const int m = go[g + 1] - go[g];
-        acc += m > 0 ? (m + BM - 1) / BM : 0;
+        acc += m > 0 ? (m + TR - 1) / TR : 0;
       }
       gt[q.groups] = acc;
       pstart[pb] = start;
@@ -437,7 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     pstart[p.nprob] = start;
   }
   ptx::tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  // a pair: both CTAs' barriers are initialised before either CTA signals the other's
+  if constexpr (PAIR) ptx::cluster_sync();
+  else __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int total_tiles = pstart[p.nprob];
@@ -450,8 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t used_mask = 0, phase_mask = 0;
       bool ok = true;
       uint32_t waited = 0;
-      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-        const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
+      for (int t = unit; ok && t < total_tiles; t += nunits) {
+        const TileInfo ti = decode_tile<TR>(t, p, goff, gtile, pstart, rank);
         const ProbParams& q = prob_params(p, ti.prob);
         if (q.wait_flag != nullptr && !(waited & (1u << ti.prob))) {
           if (!ptx::wait_flag_ge(q.wait_flag, q.wait_target, abort_flag, p.status,
@@ -477,43 +513,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t fb = full0 + 8u * stage;
-          ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
           const uint32_t a_dst = sA + stage * A_BYTES;
-          const uint32_t b_dst = sB + stage * B_BYTES;
-          ptx::tma_load_2d(a_dst, tA, fb, kb * BK, ti.row0);
-          ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
-          ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
+          const uint32_t b_dst = sB + stage * BST;
+          if constexpr (PAIR) {
+            // the leader's barrier counts both CTAs' bytes; this CTA loads B half `rank`
+            const uint32_t fb_lead = ptx::mapa_shared(fb, 0);
+            if (rank == 0) ptx::mbar_arrive_expect_tx(fb, 2u * (A_BYTES + B_HALF_BYTES));
+            ptx::tma_load_2d_pair(a_dst, tA, fb_lead, kb * BK, ti.row0);
+            ptx::tma_load_2d_pair(b_dst, tB, fb_lead, kb * BK, ti.brow0 + rank * q.b_half1_off);
+          } else {
+            ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
+            ptx::tma_load_2d(a_dst, tA, fb, kb * BK, ti.row0);
+            ptx::tma_load_2d(b_dst, tB, fb, kb * BK, ti.brow0);
+            ptx::tma_load_2d(b_dst + B_HALF_BYTES, tB, fb, kb * BK, ti.brow0 + q.b_half1_off);
+          }
           used_mask |= 1u << stage;
           phase_mask = (phase_mask & ~(1u << stage)) | (phase << stage);
-          if (++stage == STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      // Every load issued here must land before the CTA may exit.
-      for (int s = 0; s < STAGES; ++s) {
+      // Every load issued here must land before the CTA may exit.  The peer CTA of a pair
+      // cannot see the leader's full barrier: it waits until the MMAs consumed its last
+      // fill of each stage (after a failure that wait runs out, long after the loads landed).
+      for (int s = 0; s < NST; ++s) {
         if (used_mask & (1u << s))
-          ptx::mbar_wait(full0 + 8u * s, (phase_mask >> s) & 1u, never_flag, p.status,
-                         p.timeout_cycles, DS_ERR_TIMEOUT);
+          ptx::mbar_wait((PAIR && rank != 0 ? empty0 : full0) + 8u * s, (phase_mask >> s) & 1u,
+                         never_flag, p.status, p.timeout_cycles, DS_ERR_TIMEOUT);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
+    if (lane == 0 && rank == 0) {  // a pair's MMAs are issued by the leader alone
+      constexpr uint32_t idesc = ptx::idesc_bf16_f32(TR, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      for (int t = unit; ok && t < total_tiles; t += nunits) {
         if (!ptx::mbar_wait(tempty0 + 8u * acc, acc_phase ^ 1u, abort_flag, p.status,
                             p.timeout_cycles, DS_ERR_TIMEOUT))
           break;
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
+        const TileInfo ti = decode_tile<TR>(t, p, goff, gtile, pstart, rank);
         const ProbParams& q = prob_params(p, ti.prob);
         int kb0 = 0, kb1 = q.k_blocks;
         if constexpr (EPI == kRouter) {
@@ -531,28 +577,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::tc_fence_after();
           const uint32_t a0 = sA + stage * A_BYTES;
-          const uint32_t b0 = sB + stage * B_BYTES;
+          const uint32_t b0 = sB + stage * BST;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            ptx::umma_f16(d, ptx::sw128_kmajor_desc(a0 + kk * 32u),
-                          ptx::sw128_kmajor_desc(b0 + kk * 32u), idesc,
-                          (kb != kb0 || kk != 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              ptx::umma_f16_pair(d, ptx::sw128_kmajor_desc(a0 + kk * 32u),
+                                 ptx::sw128_kmajor_desc(b0 + kk * 32u), idesc,
+                                 (kb != kb0 || kk != 0) ? 1u : 0u);
+            else
+              ptx::umma_f16(d, ptx::sw128_kmajor_desc(a0 + kk * 32u),
+                            ptx::sw128_kmajor_desc(b0 + kk * 32u), idesc,
+                            (kb != kb0 || kk != 0) ? 1u : 0u);
           }
-          ptx::umma_commit(empty0 + 8u * stage);
-          if (++stage == STAGES) {
+          if constexpr (PAIR) {  // the stage is free in both CTAs
+            ptx::umma_commit_pair(empty0 + 8u * stage);
+            ptx::umma_commit_pair(ptx::mapa_shared(empty0 + 8u * stage, 1));
+          } else {
+            ptx::umma_commit(empty0 + 8u * stage);
+          }
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        ptx::umma_commit(tfull0 + 8u * acc);
+        if constexpr (PAIR) {  // both CTAs' halves of the accumulator are complete
+          ptx::umma_commit_pair(tfull0 + 8u * acc);
+          ptx::umma_commit_pair(ptx::mapa_shared(tfull0 + 8u * acc, 1));
+        } else {
+          ptx::umma_commit(tfull0 + 8u * acc);
+        }
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       // No MMA may still be writing TMEM when it is released.
-      ptx::umma_commit(drain_bar);
+      if constexpr (PAIR) ptx::umma_commit_pair(drain_bar);
+      else ptx::umma_commit(drain_bar);
       ptx::mbar_wait(drain_bar, 0, never_flag, p.status, p.timeout_cycles, DS_ERR_TIMEOUT);
     }
   } else {
@@ -561,8 +623,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile(t, p, goff, gtile, pstart);
+    for (int t = unit; t < total_tiles; t += nunits) {
+      const TileInfo ti = decode_tile<TR>(t, p, goff, gtile, pstart, rank);
       const ProbParams& qp = prob_params(p, ti.prob);
       int ok = 1;
       if (lane == 0)
@@ -620,7 +682,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(tempty0 + 8u * acc);
+      if (lane == 0) {
+        if (PAIR && rank != 0) ptx::mbar_arrive_remote(ptx::mapa_shared(tempty0 + 8u * acc, 0));
+        else ptx::mbar_arrive(tempty0 + 8u * acc);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -631,10 +696,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   __syncwarp();  // lanes 1..31 of warps 0/1 rejoin their role lane before the CTA barrier
   if (p.done_counter != nullptr) __threadfence_system();  // this thread's (peer) stores
-  __syncthreads();
+  ptx::tc_fence_before();
+  if constexpr (PAIR) ptx::cluster_sync();  // the leader's MMAs and both epilogues are done
+  else __syncthreads();
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR) ptx::tmem_dealloc_pair(tmem_base, kTmemCols);
+    else ptx::tmem_dealloc(tmem_base, kTmemCols);
   }
   if (p.done_counter != nullptr && threadIdx.x == 0) {
     const int prev = atomicAdd(p.done_counter, 1);
@@ -704,8 +772,36 @@ __global__ void __launch_bounds__(256)
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 cudaError_t g_encode_err = cudaSuccess;
-bool g_attr_set[4][64] = {};
+bool g_attr_set[4][2][64] = {};
+int g_pair_clusters[64] = {};  // co-resident 2-CTA clusters of the pair kernels, per device
 std::mutex g_attr_mutex;
+
+// Pair-mode switch: 0 keeps every launch on single-CTA tiles, 1 uses pairs wherever they
+// apply, -1 = the automatic rule in launch_multi.  Initialised from DS_GEMM_PAIR, changed by
+// ds_gemm_pair_mode().
+std::atomic<int> g_pair_mode{-2};
+int pair_mode() {
+  int m = g_pair_mode.load(std::memory_order_relaxed);
+  if (m == -2) {
+    const char* e = getenv("DS_GEMM_PAIR");
+    const int init = (e == nullptr || *e == 0) ? -1 : (atoi(e) != 0 ? 1 : 0);
+    g_pair_mode.compare_exchange_strong(m, init);
+    m = g_pair_mode.load(std::memory_order_relaxed);
+  }
+  return m;
+}
+
+template <int EPI, bool PAIR>
+const void* kernel_fn() {
+  return reinterpret_cast<const void*>(grouped_gemm_kernel<EPI, PAIR>);
+}
+const void* kernel_for(int epi, bool pair) {
+  if (pair) return epi == kSwiGLU ? kernel_fn<kSwiGLU, true>() : kernel_fn<kPlain, true>();
+  return epi == kSwiGLU   ? kernel_fn<kSwiGLU, false>()
+         : epi == kRouter  ? kernel_fn<kRouter, false>()
+         : epi == kPartial ? kernel_fn<kPartial, false>()
+                           : kernel_fn<kPlain, false>();
+}
 
 int get_encode(PFN_cuTensorMapEncodeTiled_v12000* fn) {
   std::call_once(g_encode_once, [] {
@@ -821,16 +917,51 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
   DS_REQUIRE(nl == 1 || live[1]->epilogue == epi, "gemm: problems of one launch share an epilogue");
   DeviceInfo di;
   DS_TRY(device_info(&di));
+  // CTA pairs (256-row tiles) for plain / SwiGLU launches whose groups average at least
+  // 2048 rows: half the B bytes per MMA and a deeper ring (measured on B200: +3-4 % on dense
+  // 57344 x 2816 x 2048 and 49152 x 2048 x 1408), but the last m-tile of every group pads to
+  // 256 rows instead of 128, which costs more than pairs gain at MoE group sizes (~768 rows:
+  // the config-2 GEMM1 launch ran 636 us in pairs against 609 us in single CTAs).
+  bool pair = false;
+  if (epi == kPlain || epi == kSwiGLU) {
+    int64_t rows = 0, groups = 0;
+    for (int i = 0; i < nl; ++i) {
+      rows += live[i]->a_rows;
+      groups += live[i]->offsets ? live[i]->groups : 1;
+    }
+    const int mode = pair_mode();
+    pair = mode == 1 || (mode < 0 && rows >= 2048 * groups && rows >= 4096);
+  }
   {
     std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (!g_attr_set[epi][di.device]) {
-      const void* fn = epi == kSwiGLU   ? reinterpret_cast<const void*>(grouped_gemm_kernel<kSwiGLU>)
-                       : epi == kRouter  ? reinterpret_cast<const void*>(grouped_gemm_kernel<kRouter>)
-                       : epi == kPartial ? reinterpret_cast<const void*>(grouped_gemm_kernel<kPartial>)
-                                         : reinterpret_cast<const void*>(grouped_gemm_kernel<kPlain>);
+    if (pair && !g_attr_set[epi][1][di.device]) {
+      const void* fn = kernel_for(epi, true);
       DS_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(kPairSmemBytes)));
+      if (g_pair_clusters[di.device] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * (di.num_sms / 2));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = kPairSmemBytes;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        DS_CUDA(cudaOccupancyMaxActiveClusters(&n, fn, &cfg));
+        g_pair_clusters[di.device] = n > 0 ? n : -1;
+      }
+      g_attr_set[epi][1][di.device] = true;
+    }
+    if (pair && g_pair_clusters[di.device] < 1) pair = false;  // no pair fits: single CTAs
+    if (!pair && !g_attr_set[epi][0][di.device]) {
+      DS_CUDA(cudaFuncSetAttribute(kernel_for(epi, false),
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(kSmemBytes)));
-      g_attr_set[epi][di.device] = true;
+      g_attr_set[epi][0][di.device] = true;
     }
   }
   CUtensorMap tmA[kMaxProblems], tmB[kMaxProblems], tmO[kMaxProblems];
@@ -853,7 +984,8 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
       DS_TRY(make_tmap(&tmO[i], pr.out, pr.a_rows, pr.ldo, 32u));
       p.pr[i].tma_out = 1;
     }
-    max_tiles += ((pr.a_rows + BM - 1) / BM + (pr.offsets ? pr.groups : 0)) * pr.n_tiles *
+    const int tr = pair ? 2 * BM : BM;
+    max_tiles += ((pr.a_rows + tr - 1) / tr + (pr.offsets ? pr.groups : 0)) * pr.n_tiles *
                  p.pr[i].k_splits;
     if (pr.max_ctas > 0 && pr.max_ctas < cap) cap = pr.max_ctas;
     // a cross-GPU wait may legitimately hold the pipeline: every wait gets its bound
@@ -864,7 +996,14 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
     tmB[1] = tmB[0];
     tmO[1] = tmO[0];
   }
-  const int grid = static_cast<int>(max_tiles < cap ? max_tiles : cap);
+  int grid = static_cast<int>(max_tiles < cap ? max_tiles : cap);
+  if (pair) {  // whole clusters, at most the co-resident ones, each with a tile
+    int64_t units = cap / 2;
+    if (units > g_pair_clusters[di.device]) units = g_pair_clusters[di.device];
+    if (units > max_tiles) units = max_tiles;
+    if (units < 1) units = 1;
+    grid = static_cast<int>(2 * units);
+  }
   if (sig != nullptr) {
     DS_REQUIRE(sig->done_counter != nullptr && sig->nsignal >= 0 && sig->nsignal <= 8,
                "gemm: bad completion signal");
@@ -872,14 +1011,34 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
     p.nsignal = sig->nsignal;
     for (int i = 0; i < sig->nsignal; ++i) p.signal_flags[i] = sig->flags[i];
   }
-  if (epi == kSwiGLU)
-    grouped_gemm_kernel<kSwiGLU><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
-  else if (epi == kRouter)
-    grouped_gemm_kernel<kRouter><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
-  else if (epi == kPartial)
-    grouped_gemm_kernel<kPartial><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
-  else
-    grouped_gemm_kernel<kPlain><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
+  if (pair) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kPairSmemBytes;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (epi == kSwiGLU)
+      DS_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<kSwiGLU, true>, tmA[0], tmB[0], tmA[1],
+                                 tmB[1], tmO[0], tmO[1], p));
+    else
+      DS_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<kPlain, true>, tmA[0], tmB[0], tmA[1],
+                                 tmB[1], tmO[0], tmO[1], p));
+  } else if (epi == kSwiGLU) {
+    grouped_gemm_kernel<kSwiGLU, false><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
+  } else if (epi == kRouter) {
+    grouped_gemm_kernel<kRouter, false><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
+  } else if (epi == kPartial) {
+    grouped_gemm_kernel<kPartial, false><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
+  } else {
+    grouped_gemm_kernel<kPlain, false><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
+  }
   DS_LAUNCH_CHECK("grouped_gemm_kernel");
   return DS_OK;
 }
@@ -1031,6 +1190,12 @@ int moe_gemm2_impl(const void* swiglu_out_bf16, const void* w2_bf16,
 }  // namespace
 
 extern "C" {
+
+int ds_gemm_pair_mode(int mode) {
+  const int prev = ds::gemm::pair_mode();
+  if (mode >= -1 && mode <= 1) ds::gemm::g_pair_mode.store(mode);
+  return prev;
+}
 
 int ds_moe_gemm1(const void* dispatched_bf16, const void* packed_w1_bf16,
                  const int32_t* expert_offsets, void* gemm1_out_bf16, int total_slots,

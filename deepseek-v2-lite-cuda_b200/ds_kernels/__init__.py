@@ -64,6 +64,7 @@ SIGNATURES = {
     "ds_rms_norm_strided": (_i, [_vp, _i64, _vp, _vp, _i64, _i, _i, _f, _vp]),
     "ds_rms_norm_residual": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp]),
     "ds_kv_upproj": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "ds_gemm_pair_mode": (_i, [_i]),
     "ds_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "ds_moe_layer_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
     "ds_mla_attention_workspace_size": (_sz, [_i, _i, _i]),
@@ -435,6 +436,12 @@ def rms_norm_residual(input: torch.Tensor, residual: torch.Tensor, weight: torch
                                          _ptr(s), _ptr(n), rows, H, float(eps), _stream(input)),
                "rms_norm_residual")
     return [n, s]
+
+
+def gemm_pair_mode(mode: Optional[int] = None) -> int:
+    """Tiling of the tcgen05 grouped GEMM (process-wide): 0 single-CTA 128x256 tiles, 1 CTA
+    pairs on 256x256 tiles, -1 automatic; None only queries.  Returns the previous mode."""
+    return _lib.ds_gemm_pair_mode(-2 if mode is None else int(mode))
 
 
 def kv_upproj(normed_kv: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:

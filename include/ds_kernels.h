@@ -153,6 +153,14 @@ DS_API int ds_moe_gemm1_swiglu(const void* dispatched_bf16, const void* packed_w
                         int total_slots, int num_experts, int hidden_size,
                         int double_intermed, void* stream);
 
+/* Tiling of the tcgen05 grouped GEMM behind ds_moe_gemm1/2, ds_kv_upproj and the layer
+ * (additive; no reference counterpart): 0 = one CTA per 128 x 256 tile, 1 = CTA pairs
+ * (2-CTA clusters, cta_group::2 MMAs) on 256 x 256 tiles for every plain / SwiGLU launch,
+ * -1 = automatic (pairs when a launch's groups average at least 2048 rows).  The default comes
+ * from the DS_GEMM_PAIR environment variable (unset: -1).  Other values only query.
+ * Returns the previous mode.  Process-wide; results are identical in every mode. */
+DS_API int ds_gemm_pair_mode(int mode);
+
 /* ---------------------------------------------------------------------------------------
  * K6 grouped GEMM2.  Replaces launch_moe_gemm2 (src/kernels/include/moe/gemm2.h:25-34,
  * src/kernels/moe/gemm2.cu:75-124) and moe_gemm2_forward (gemm2.cu:136-195).
