@@ -80,7 +80,7 @@ def test_prefill_then_decode_steps_match_the_forward():
     assert ds_kernels.device_status() == ds_kernels.DS_OK
 
 
-@pytest.mark.parametrize("L", [0, 1, 127, 128, 129, 300])
+@pytest.mark.parametrize("L", [0, 1, 63, 64, 65, 127, 128, 129, 300])
 def test_decode_at_chunk_boundaries_from_update(L):
     # positions written through update() (the reference API: raw values only) get their
     # side arrays on the next decode step
