@@ -16,18 +16,22 @@
 //   out   = o_lat @ W_ouv^T    W_ouv_h = W_o_h W_uv_h diag(g)
 // and the attention reads the cache once: it is HBM-bound (576 bf16 + 68 bytes per token).
 //
-// Attention kernel: one CTA per (sequence, split of the positions), 192 threads.
+// Attention kernel: one CTA per (sequence, split of the positions), 192 threads, ~95 KB of
+// shared memory, so two CTAs share an SM and one CTA's chunk load overlaps the other's
+// chain of MMAs and softmax (a CTA's own chunks run one after another).
 //   warp 0   TMA producer: the sequence's Q (16 heads x 576: nine 16x64 boxes) once, then per
-//            128-token chunk the latent (eight 128x64 boxes) and k_pe_rot (one box).
-//   warp 1   MMA issuer: S^T = C Q'^T (M = 128 tokens, N = 16 heads, K = 512) and the RoPE
-//            part (K = 64) into two TMEM accumulators; after the softmax, O^T += C^T P^T
-//            (M = 128 latent dims x 4 blocks, N = 16 heads, K = 128 tokens) with the SAME
-//            latent tile read as an MN-major A operand (no second copy of the cache).
-//   warps 2-5  softmax, one token per thread: s = rstd*S1 + S2 for the 16 heads, per-head max
-//            over the chunk (shuffles + shared memory), lazy running max (O^T rescaled in
-//            TMEM only when a head's max grows by more than 2^8), P^T (times rstd) as bf16
-//            into a 16 x 128 shared-memory tile; at the end the O^T rows (one latent dim per
-//            thread), maxima and sums go to a per-split partial.
+//            64-token chunk the latent (eight 64x64 boxes) and k_pe_rot (one box).
+//   warp 1   MMA issuer: S^T = C Q'^T (M = 128, N = 16 heads, K = 512) and the RoPE part
+//            (K = 64) into two TMEM accumulators -- rows 64-127 of the M = 128 operand read
+//            the shared memory that follows the chunk's 64 token rows and are ignored; after
+//            the softmax, O^T += C^T P^T (M = 128 latent dims x 4 blocks, N = 16 heads, K = 64
+//            tokens) with the SAME latent tile read as an MN-major A operand (no second copy
+//            of the cache).
+//   warps 2-5  softmax, one token per thread (threads 0-63): s = rstd*S1 + S2 for the 16
+//            heads, per-head max over the chunk (shuffles + shared memory), lazy running max
+//            (O^T rescaled in TMEM only when a head's max grows by more than 2^8), P^T (times
+//            rstd) as bf16 into a 16 x 64 shared-memory tile; at the end the O^T rows (one
+//            latent dim per thread), maxima and sums go to a per-split partial.
 // A combine kernel merges the splits per (sequence, head) into o_lat (bf16).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -46,13 +50,14 @@ constexpr int kLatent = 512;
 constexpr int kRope = 64;
 constexpr int kQCols = kLatent + kRope;  // 576
 constexpr int kHeads = 16;               // N of the attention MMAs
-constexpr int kChunk = 128;
+constexpr int kChunk = 64;
 constexpr int kThreads = 192;
-constexpr uint32_t kBox = 128 * 64 * 2;        // 128 rows x 64 columns bf16: 16 KiB
+constexpr uint32_t kBox = 64 * 64 * 2;         // 64 rows x 64 columns bf16: 8 KiB
 constexpr uint32_t kQBox = 16 * 64 * 2;        // 16 rows x 64 columns: 2 KiB
-constexpr uint32_t kQBytes = 9 * kQBox;        // 18 KiB
-constexpr uint32_t kCBytes = 9 * kBox;         // 8 latent boxes + k_pe_rot: 144 KiB
-constexpr uint32_t kPBytes = 2 * kQBox;        // P^T: 16 heads x 128 tokens, two 16x64 boxes
+constexpr uint32_t kQBytes = 9 * kQBox;        // 18 KiB (follows the chunk: the 128-row
+                                               // operands over its last box stay in bounds)
+constexpr uint32_t kCBytes = 9 * kBox;         // 8 latent boxes + k_pe_rot: 72 KiB
+constexpr uint32_t kPBytes = kQBox;            // P^T: 16 heads x 64 tokens, one 16x64 box
 constexpr uint32_t kTail = 512;
 constexpr size_t kSmemBytes = 1024 + kCBytes + kQBytes + kPBytes + kTail;
 constexpr uint32_t kTmemCols = 128;
@@ -69,7 +74,7 @@ struct Params {
   int* status;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     mla_decode_attn_kernel(const __grid_constant__ CUtensorMap tmQ,   // Q [batch*16, 576]
                            const __grid_constant__ CUtensorMap tmC,   // latent [batch*max_seq, 512]
                            const __grid_constant__ CUtensorMap tmKr,  // k_pe_rot [batch*max_seq, 64]
@@ -178,14 +183,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         ptx::tc_fence_after();
         // O^T (4 blocks of 128 latent dims) += C^T P^T: A = the latent tile read MN-major
-        // (64 dims per 128-byte row, the next 64 one box = 16 KiB on; tokens 128 bytes
-        // apart), B = P^T [16 heads x 128 tokens] K-major
+        // (64 dims per 128-byte row, the next 64 one box = 8 KiB on; tokens 128 bytes
+        // apart), B = P^T [16 heads x 64 tokens] K-major
 #pragma unroll 1
         for (int i = 0; i < 4; ++i) {
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {
             const uint32_t a = sC + (2 * i) * kBox + kk * 16 * 128;
-            const uint32_t pb = sP + (kk >> 2) * kQBox + (kk & 3) * 32;
+            const uint32_t pb = sP + kk * 32;
             ptx::umma_f16(tmem + kColO + i * kHeads, ptx::sw128_mnmajor_desc(a, kBox),
                           ptx::sw128_kmajor_desc(pb), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
           }
@@ -232,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tmem_ld32(tmem + lane_off + kColS1, s1);  // columns 0..31: S1 (0..15), S2 (16..31)
       ptx::tmem_wait_ld(s1);
       const int t = t_begin + j * kChunk + tl;
-      const bool live = t < t_end;
+      const bool live = tl < kChunk && t < t_end;  // lanes 64-127 of S hold no token
       const float r = live ? __ldg(p.rstd + row0 + t) : 0.f;
       float s[kHeads];
       float mx[kHeads];
@@ -263,18 +268,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           any_rescale = true;
         }
       }
-      // P^T (times rstd) into the 16 x 128 shared tile: head h is row h of box tl / 64,
-      // token tl % 64 is element (tl % 64) of the row's 128 bytes, 16-byte chunks XOR-
-      // swizzled by (h & 7) as the SWIZZLE_128B operand layout expects
-      {
-        const int box = tl >> 6, col = tl & 63;
-        uint8_t* pbase = sPgen + box * kQBox;
+      // P^T (times rstd) into the 16 x 64 shared tile: head h is row h, token tl is element
+      // tl of the row's 128 bytes, 16-byte chunks XOR-swizzled by (h & 7) as the
+      // SWIZZLE_128B operand layout expects
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-          const float pv = ptx::ex2(s[h] - m[h]);
-          lsum[h] = lsum[h] * alpha[h] + pv;
-          const uint32_t chunk = (static_cast<uint32_t>(col >> 3) ^ static_cast<uint32_t>(h & 7));
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(pbase + h * 128 + chunk * 16) + (col & 7);
+      for (int h = 0; h < kHeads; ++h) {
+        const float pv = ptx::ex2(s[h] - m[h]);  // 0 for a token that is not live
+        lsum[h] = lsum[h] * alpha[h] + pv;
+        if (tl < kChunk) {
+          const uint32_t chunk = (static_cast<uint32_t>(tl >> 3) ^ static_cast<uint32_t>(h & 7));
+          __nv_bfloat16* dst =
+              reinterpret_cast<__nv_bfloat16*>(sPgen + h * 128 + chunk * 16) + (tl & 7);
           *dst = __float2bfloat16_rn(pv * r);
         }
       }
@@ -508,8 +512,8 @@ int tmap_2d(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, uint32_
 
 int nsplit_for(int batch, int len, int num_sms, int* chunks_per_split) {
   const int chunks = (len + kChunk - 1) / kChunk;
-  // about two CTAs' worth of chunks per SM across the grid, at least one chunk per split
-  int want = (2 * num_sms + batch - 1) / batch;
+  // one wave of two CTAs per SM, at least one chunk per split
+  int want = (2 * num_sms) / batch;
   if (want > chunks) want = chunks;
   if (want < 1) want = 1;
   *chunks_per_split = (chunks + want - 1) / want;
@@ -569,8 +573,8 @@ int launch_decode_attention(const void* q, const void* c_lat, const float* c_rst
   }
   CUtensorMap tq, tc, tk;
   DS_TRY(tmap_2d(&tq, q, static_cast<int64_t>(batch) * kHeads, kQCols, 16u));
-  DS_TRY(tmap_2d(&tc, c_lat, static_cast<int64_t>(batch) * max_seq, kLatent, 128u));
-  DS_TRY(tmap_2d(&tk, c_kpe_rot, static_cast<int64_t>(batch) * max_seq, kRope, 128u));
+  DS_TRY(tmap_2d(&tc, c_lat, static_cast<int64_t>(batch) * max_seq, kLatent, kChunk));
+  DS_TRY(tmap_2d(&tk, c_kpe_rot, static_cast<int64_t>(batch) * max_seq, kRope, kChunk));
   Params p{};
   p.batch = batch;
   p.max_seq = max_seq;
