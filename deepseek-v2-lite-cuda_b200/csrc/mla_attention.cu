@@ -6,7 +6,6 @@
 //   lat   = RMSNorm(qkv[:, heads*192 : +512])
 //   kv    = lat @ W_kv_b^T                  [M, heads*(128 + 128)]  (k_nope | v per head)
 //   RoPE in place on the 64-wide q_pe of every head and on k_pe inside qkv
-//   V^T   = transpose of the v halves       [(b*heads + h)*128 + d, S]
 //   o     = causal softmax(q k^T * scale) v  (this file's attention kernel), [M, heads*128]
 //   out   = o @ W_o^T                        [M, hidden]
 //
@@ -15,11 +14,12 @@
 //                columns: nope, nope, rope, straight out of qkv), then per 128-row kv block
 //                the K tile (k_nope 2 boxes from kv, k_pe 1 box from qkv, shared by the
 //                heads) into a 2-stage ring (128-byte swizzle).
-//   warp 10      TMA producer of the V^T tiles (2 boxes per block, 2-stage ring), so a K
-//                load never waits behind a V stage.
+//   warp 10      TMA producer of the V tiles (2 boxes per block: 128 kv rows x 64 dims of
+//                the v half of kv, 2-stage ring), so a K load never waits behind a V stage.
 //   warp 1       MMA issuer (one thread): S_j = Q K_j^T (M=128, N=128, K=192) into one of two
 //                TMEM buffers, then O += P_{j-1} V_{j-1} (M=128, N=128, K=128) with P read
-//                from TMEM (the softmax warps write it over S) and V^T from shared memory.
+//                from TMEM (the softmax warps write it over S) and V read straight from
+//                the kv rows as an MN-major B operand (no transposed copy).
 //   warps 2-9    softmax, two warps per 32-row TMEM quarter, each thread one row's 64 of the
 //                128 S values of a block (the pair exchanges row maxima through shared
 //                memory): row max (log2 domain), P_j = 2^(s*scale - m) rounded to bf16 into
@@ -78,7 +78,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b, float& ra, float
 __global__ void __launch_bounds__(kThreads, 1)
     mla_attention_kernel(const __grid_constant__ CUtensorMap tmQ,   // qkv [B*S, ldq]
                          const __grid_constant__ CUtensorMap tmKV,  // kv [B*S, heads*256]
-                         const __grid_constant__ CUtensorMap tmVt,  // V^T [B*heads*128, S]
                          const Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
@@ -132,7 +131,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&tmQ);
     ptx::prefetch_tmap(&tmKV);
-    ptx::prefetch_tmap(&tmVt);
   }
   if (warp == 1) {
     ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kTmemCols);
@@ -172,8 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           ptx::mbar_arrive_expect_tx(fb, V_BYTES);
           const uint32_t vd = sV + st * V_BYTES;
-          ptx::tma_load_2d(vd, &tmVt, fb, j * BKV, bh * 128);
-          ptx::tma_load_2d(vd + CHUNK, &tmVt, fb, j * BKV + 64, bh * 128);
+          // V_j: kv rows j*128 .. +127, head h's v dims 0-63 and 64-127
+          ptx::tma_load_2d(vd, &tmKV, fb, h * 256 + 128, row0 + j * BKV);
+          ptx::tma_load_2d(vd + CHUNK, &tmKV, fb, h * 256 + 192, row0 + j * BKV);
         }
         issued = j + 1;
       }
@@ -223,12 +222,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after();
           const uint32_t pa = tmem + (st ? kSCol1 : kSCol0);
           const uint32_t vb = sV + st * V_BYTES;
+          // B = V_j [128 kv (K) x 128 dims (N)] MN-major: dims 0-63 of a kv row in one
+          // 128-byte row of the first box, dims 64-127 one box (LBO) on; 16 kv rows per step
+          constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32_bmn(128, 128);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
-            ptx::umma_f16_ts(tmem + kOCol, pa + kk * 8, ptx::sw128_kmajor_desc(vb + off), idesc,
+          for (int kk = 0; kk < 8; ++kk)
+            ptx::umma_f16_ts(tmem + kOCol, pa + kk * 8,
+                             ptx::sw128_mnmajor_desc(vb + kk * 16 * 128, CHUNK), idesc_pv,
                              (jp > 0 || kk > 0) ? 1u : 0u);
-          }
           ptx::umma_commit(v_empty0 + 8u * st);
           ptx::umma_commit(o_done);
         }
@@ -407,47 +408,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// V^T: kv [B*S, heads*256] (per head 128 k_nope then 128 v) -> vt [(b*heads + h)*128 + d, S].
-// A block moves a 64-token x 64-dim tile through shared memory: 16-byte loads along d,
-// 16-byte stores along the sequence.
-__global__ void __launch_bounds__(256)
-    v_transpose_kernel(const __nv_bfloat16* __restrict__ kv, int ldkv,
-                       __nv_bfloat16* __restrict__ vt, int seq, int heads) {
-  __shared__ __nv_bfloat16 tile[64][64 + 8];
-  const int s0 = blockIdx.x * 64;
-  const int d0 = blockIdx.y * 64;
-  const int bh = blockIdx.z;
-  const int b = bh / heads, h = bh - b * heads;
-  const int t = threadIdx.x;
-  // load: 64 tokens x 8 uint4 (64 dims)
-#pragma unroll
-  for (int it = 0; it < 2; ++it) {
-    const int idx = it * 256 + t;
-    const int ts = idx >> 3, c = idx & 7;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (s0 + ts < seq)
-      v = __ldg(reinterpret_cast<const uint4*>(
-          kv + static_cast<int64_t>(b * seq + s0 + ts) * ldkv + h * 256 + 128 + d0 + c * 8));
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) tile[c * 8 + k][ts] = e[k];
-  }
-  __syncthreads();
-  // store: 64 dims x 8 uint4 (64 tokens)
-#pragma unroll
-  for (int it = 0; it < 2; ++it) {
-    const int idx = it * 256 + t;
-    const int dd = idx >> 3, c = idx & 7;
-    if (s0 + c * 8 < seq) {
-      uint4 v;
-      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&v);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] = tile[dd][c * 8 + k];
-      *reinterpret_cast<uint4*>(vt + (static_cast<int64_t>(bh) * 128 + d0 + dd) * seq + s0 + c * 8) = v;
-    }
-  }
-}
-
 // RoPE in place on qkv [rows, ld]: the 64-wide q_pe of each head (columns h*192 + 128 ..) and
 // k_pe (columns kcol ..): the interleave -> half transform and the rotation of
 // src/reference/mla.py:176-206, out[k] = x[2k] cos[k] - x[2k+1] sin[k],
@@ -546,14 +506,14 @@ int tmap_2d(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t
 
 }  // namespace
 
-// Attention over qkv (RoPE already applied in place) and kv; vt = V^T scratch
+// Attention over qkv (RoPE already applied in place) and kv
 // [batch*heads*128, seq]; out [batch*seq, heads*128].
-int launch_attention(const void* qkv, int ldq, const void* kv, void* vt, void* out, int batch,
+int launch_attention(const void* qkv, int ldq, const void* kv, void* out, int batch,
                      int seq, int heads, float softmax_scale, cudaStream_t s) {
   DS_REQUIRE(batch >= 1 && seq >= 1 && heads >= 1, "mla_attention: bad shape");
   DS_REQUIRE(seq % 8 == 0, "mla_attention: seq_len must be a multiple of 8");
   DS_REQUIRE(ldq % 8 == 0 && ldq >= heads * 192 + 512 + 64, "mla_attention: bad qkv stride");
-  DS_REQUIRE(aligned16(qkv) && aligned16(kv) && aligned16(vt) && aligned16(out),
+  DS_REQUIRE(aligned16(qkv) && aligned16(kv) && aligned16(out),
              "mla_attention: buffers must be 16-byte aligned");
   DeviceInfo di;
   DS_TRY(device_info(&di));
@@ -567,16 +527,9 @@ int launch_attention(const void* qkv, int ldq, const void* kv, void* vt, void* o
     }
   }
   const int64_t M = static_cast<int64_t>(batch) * seq;
-  {
-    dim3 grid((seq + 63) / 64, 2, batch * heads);
-    v_transpose_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(kv), heads * 256,
-                                            static_cast<__nv_bfloat16*>(vt), seq, heads);
-    DS_LAUNCH_CHECK("v_transpose_kernel");
-  }
-  CUtensorMap tq, tkv, tvt;
+  CUtensorMap tq, tkv;
   DS_TRY(tmap_2d(&tq, qkv, M, ldq, ldq));
   DS_TRY(tmap_2d(&tkv, kv, M, static_cast<int64_t>(heads) * 256, static_cast<int64_t>(heads) * 256));
-  DS_TRY(tmap_2d(&tvt, vt, static_cast<int64_t>(batch) * heads * 128, seq, seq));
   Params p{};
   p.batch = batch;
   p.seq = seq;
@@ -588,7 +541,7 @@ int launch_attention(const void* qkv, int ldq, const void* kv, void* vt, void* o
   p.status = device_status_ptr();
   if (p.status == nullptr) return fail(DS_ERR_CUDA, "device status word unavailable");
   const int ntq = (seq + BQ - 1) / BQ;
-  mla_attention_kernel<<<ntq * batch * heads, kThreads, kSmemBytes, s>>>(tq, tkv, tvt, p);
+  mla_attention_kernel<<<ntq * batch * heads, kThreads, kSmemBytes, s>>>(tq, tkv, p);
   DS_LAUNCH_CHECK("mla_attention_kernel");
   return DS_OK;
 }
@@ -617,7 +570,6 @@ struct MlaBuffers {
   void* qkv;  // bf16 [M, ldq]
   void* lat;  // bf16 [M, 512]
   void* kv;   // bf16 [M, heads*256]
-  void* vt;   // bf16 [batch*heads*128, seq]
   void* o;    // bf16 [M, heads*128]
 };
 
@@ -631,7 +583,6 @@ size_t carve_mla(ds::Carve& c, MlaBuffers* b, int batch, int seq, int heads) {
   x.qkv = c.take<__nv_bfloat16>(M * mla_ldq(heads));
   x.lat = c.take<__nv_bfloat16>(M * kLatent);
   x.kv = c.take<__nv_bfloat16>(M * heads * 256);
-  x.vt = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * heads * 128 * seq);
   x.o = c.take<__nv_bfloat16>(M * heads * 128);
   if (b) *b = x;
   return ds::align_up(c.used, 256);
@@ -664,7 +615,10 @@ ds::gemm::Problem dense_problem(const void* A, int64_t rows, int K, const void* 
 extern "C" {
 
 size_t ds_mla_attention_workspace_size(int batch, int seq, int heads) {
-  return ds::align_up(static_cast<size_t>(batch) * heads * 128 * seq * 2, 256);
+  (void)batch;
+  (void)seq;
+  (void)heads;
+  return 0;  // the attention reads v in place: no scratch
 }
 
 int ds_mla_attention(const void* qkv_bf16, int qkv_ld, const void* kv_bf16, void* out_bf16,
@@ -672,12 +626,11 @@ int ds_mla_attention(const void* qkv_bf16, int qkv_ld, const void* kv_bf16, void
                      size_t workspace_bytes, void* stream) {
   DS_REQUIRE(batch >= 0 && seq >= 0 && heads >= 1, "mla_attention: bad shape");
   if (batch == 0 || seq == 0) return DS_OK;
-  DS_REQUIRE(qkv_bf16 && kv_bf16 && out_bf16 && workspace, "mla_attention: null pointer");
-  DS_REQUIRE(workspace_bytes >= ds_mla_attention_workspace_size(batch, seq, heads),
-             "mla_attention: workspace needs %zu bytes",
-             ds_mla_attention_workspace_size(batch, seq, heads));
-  return ds::attn::launch_attention(qkv_bf16, qkv_ld, kv_bf16, workspace, out_bf16, batch, seq,
-                                    heads, softmax_scale, static_cast<cudaStream_t>(stream));
+  DS_REQUIRE(qkv_bf16 && kv_bf16 && out_bf16, "mla_attention: null pointer");
+  (void)workspace;
+  (void)workspace_bytes;
+  return ds::attn::launch_attention(qkv_bf16, qkv_ld, kv_bf16, out_bf16, batch, seq, heads,
+                                    softmax_scale, static_cast<cudaStream_t>(stream));
 }
 
 size_t ds_mla_forward_workspace_size(int batch, int seq, int hidden, int heads) {
@@ -755,7 +708,7 @@ int mla_forward_impl(const void* x_bf16, const void* w_qkv_a_bf16, const float* 
   DS_TRY(mark(3));
   DS_TRY(ds::attn::launch_mla_rope(b.qkv, ldq, M, seq, heads, cos_bf16, sin_bf16, positions, s));
   DS_TRY(mark(4));
-  DS_TRY(ds::attn::launch_attention(b.qkv, ldq, b.kv, b.vt, b.o, batch, seq, heads,
+  DS_TRY(ds::attn::launch_attention(b.qkv, ldq, b.kv, b.o, batch, seq, heads,
                                     softmax_scale, s));
   DS_TRY(mark(5));
   DS_TRY(ds::gemm::launch(dense_problem(b.o, M, heads * 128, w_o_bf16, hidden, out_bf16), s));

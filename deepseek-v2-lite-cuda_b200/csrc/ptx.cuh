@@ -365,6 +365,10 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 __host__ __device__ constexpr uint32_t idesc_bf16_f32_amn(int M, int N) {
   return idesc_bf16_f32(M, N) | (1u << 15);
 }
+// The same with B MN-major (bit 16).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int M, int N) {
+  return idesc_bf16_f32(M, N) | (1u << 16);
+}
 
 // ---- flags shared between GPUs (peer memory): release/acquire at system scope -----------
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
