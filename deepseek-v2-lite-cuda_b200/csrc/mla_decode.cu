@@ -21,14 +21,15 @@
 // chain of MMAs and softmax (a CTA's own chunks run one after another).
 //   warp 0   TMA producer: the sequence's Q (16 heads x 576: nine 16x64 boxes) once, then per
 //            64-token chunk the latent (eight 64x64 boxes) and k_pe_rot (one box).
-//   warp 1   MMA issuer: S^T = C Q'^T (M = 128, N = 16 heads, K = 512) and the RoPE part
-//            (K = 64) into two TMEM accumulators -- rows 64-127 of the M = 128 operand read
-//            the shared memory that follows the chunk's 64 token rows and are ignored; after
-//            the softmax, O^T += C^T P^T (M = 128 latent dims x 4 blocks, N = 16 heads, K = 64
-//            tokens) with the SAME latent tile read as an MN-major A operand (no second copy
-//            of the cache).
-//   warps 2-5  softmax, one token per thread (threads 0-63): s = rstd*S1 + S2 for the 16
-//            heads, per-head max over the chunk (shuffles + shared memory), lazy running max
+//   warp 1   MMA issuer: S^T = C Q'^T (M = 64 tokens, N = 16 heads, K = 512) and the RoPE
+//            part (K = 64) into two TMEM accumulators (M = 64 puts token r in lane
+//            32 (r / 16) + r % 16); after the softmax, O^T += C^T P^T (M = 128 latent dims x 4
+//            blocks, N = 16 heads, K = 64 tokens) with the SAME latent tile read as an
+//            MN-major A operand (no second copy of the cache).  These N = 16 MMAs are bound
+//            by the tensor cores' shared-memory operand reads, so each one reads only the
+//            chunk's 64 token rows: every latent byte is read once per phase.
+//   warps 2-5  softmax, one token per thread (lanes 0-15 of each warp): s = rstd*S1 + S2 for
+//            the 16 heads, per-head max over the chunk (shuffles + shared memory), lazy running max
 //            (O^T rescaled in TMEM only when a head's max grows by more than 2^8), P^T (times
 //            rstd) as bf16 into a 16 x 64 shared-memory tile; at the end the O^T rows (one
 //            latent dim per thread), maxima and sums go to a per-split partial.
@@ -54,8 +55,7 @@ constexpr int kChunk = 64;
 constexpr int kThreads = 192;
 constexpr uint32_t kBox = 64 * 64 * 2;         // 64 rows x 64 columns bf16: 8 KiB
 constexpr uint32_t kQBox = 16 * 64 * 2;        // 16 rows x 64 columns: 2 KiB
-constexpr uint32_t kQBytes = 9 * kQBox;        // 18 KiB (follows the chunk: the 128-row
-                                               // operands over its last box stay in bounds)
+constexpr uint32_t kQBytes = 9 * kQBox;        // 18 KiB
 constexpr uint32_t kCBytes = 9 * kBox;         // 8 latent boxes + k_pe_rot: 72 KiB
 constexpr uint32_t kPBytes = kQBox;            // P^T: 16 heads x 64 tokens, one 16x64 box
 constexpr uint32_t kTail = 512;
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0 && nchunk > 0) {
-      constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(128, kHeads);
+      constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(64, kHeads);
       constexpr uint32_t idesc_o = ptx::idesc_bf16_f32_amn(128, kHeads);
       bool ok = ptx::mbar_wait(q_full, 0, abort_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
       for (int j = 0; ok && j < nchunk; ++j) {
@@ -204,7 +204,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else {
     // ------------------------------------------------------------------ softmax (warps 2-5)
     const int quarter = warp & 3;
-    const int tl = quarter * 32 + lane;  // token within the chunk (= TMEM lane)
+    const int tl = quarter * 32 + lane;  // TMEM lane = latent dim within an O^T block
+    const int tok = quarter * 16 + (lane & 15);  // token of S lane tl (lanes 0-15 of a warp)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     constexpr float kLazy = 8.f;
     float m[kHeads], lsum[kHeads];
@@ -215,6 +216,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     bool ok = nchunk > 0;
     for (int j = 0; ok && j < nchunk; ++j) {
+      const int t = t_begin + j * kChunk + tok;
+      const bool live = lane < 16 && t < t_end;  // lanes 16-31 of each quarter hold no token
+      const float r = live ? __ldg(p.rstd + row0 + t) : 0.f;  // in flight during the wait
       int w_ok = 1;
       if (lane == 0)
         w_ok = ptx::mbar_wait(s_full, j & 1, abort_flag, p.status, kTimeoutCycles,
@@ -236,9 +240,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t s1[32];
       ptx::tmem_ld32(tmem + lane_off + kColS1, s1);  // columns 0..31: S1 (0..15), S2 (16..31)
       ptx::tmem_wait_ld(s1);
-      const int t = t_begin + j * kChunk + tl;
-      const bool live = tl < kChunk && t < t_end;  // lanes 64-127 of S hold no token
-      const float r = live ? __ldg(p.rstd + row0 + t) : 0.f;
       float s[kHeads];
       float mx[kHeads];
 #pragma unroll
@@ -268,17 +269,17 @@ __global__ void __launch_bounds__(kThreads, 2)
           any_rescale = true;
         }
       }
-      // P^T (times rstd) into the 16 x 64 shared tile: head h is row h, token tl is element
-      // tl of the row's 128 bytes, 16-byte chunks XOR-swizzled by (h & 7) as the
+      // P^T (times rstd) into the 16 x 64 shared tile: head h is row h, token tok is element
+      // tok of the row's 128 bytes, 16-byte chunks XOR-swizzled by (h & 7) as the
       // SWIZZLE_128B operand layout expects
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) {
         const float pv = ptx::ex2(s[h] - m[h]);  // 0 for a token that is not live
         lsum[h] = lsum[h] * alpha[h] + pv;
-        if (tl < kChunk) {
-          const uint32_t chunk = (static_cast<uint32_t>(tl >> 3) ^ static_cast<uint32_t>(h & 7));
+        if (lane < 16) {
+          const uint32_t chunk = (static_cast<uint32_t>(tok >> 3) ^ static_cast<uint32_t>(h & 7));
           __nv_bfloat16* dst =
-              reinterpret_cast<__nv_bfloat16*>(sPgen + h * 128 + chunk * 16) + (tl & 7);
+              reinterpret_cast<__nv_bfloat16*>(sPgen + h * 128 + chunk * 16) + (tok & 7);
           *dst = __float2bfloat16_rn(pv * r);
         }
       }
