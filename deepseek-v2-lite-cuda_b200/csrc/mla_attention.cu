@@ -52,10 +52,10 @@ constexpr uint32_t K_BYTES = 3 * CHUNK;
 constexpr uint32_t V_BYTES = 2 * CHUNK;
 constexpr int STAGES = 2;
 constexpr uint32_t kTileBytes = Q_BYTES + STAGES * (K_BYTES + V_BYTES);  // 208 KiB
-constexpr uint32_t kTailBytes = 256 + 6 * 128 * 4;  // barriers, then the softmax pairs' exchange
+constexpr uint32_t kTailBytes = 256 + 6 * 128 * 4 + 128;  // barriers, then the softmax pairs' exchange
 constexpr size_t kSmemBytes = 1024 + kTileBytes + kTailBytes;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSCol0 = 0, kSCol1 = 128, kOCol = 256;
+constexpr uint32_t kSCol0 = 0, kSCol1 = 128, kOCol0 = 256, kOCol1 = 384;  // O per tile parity
 constexpr long long kTimeoutCycles = 4000000000LL;
 
 struct Params {
@@ -64,6 +64,7 @@ struct Params {
   float scale_log2;     // softmax scale * log2(e)
   __nv_bfloat16* out;   // [batch*seq, heads*128]
   int ldo;
+  int* tile_counter;  // zero at launch: the next tile to hand out
   int* status;
 };
 
@@ -88,32 +89,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* tail = smem + kTileBytes;
   const uint32_t bar0 = ptx::smem_u32(tail);
   // barriers (8 bytes each): q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2],
-  // p_ready[2], o_done, drain.  p_ready alternates by block: the softmax warps may finish
-  // block j+1 before the MMA thread has seen block j's phase, and a barrier that moved two
-  // phases past its waiter would read as not yet complete.
+  // p_ready[2], o_done, drain, q_empty, o_free[2], tile_full[2], tile_empty[2].  Block barriers alternate by the CTA's
+  // running block count g (over all its tiles): the softmax warps may finish block g+1
+  // before the MMA thread has seen block g's phase, and a barrier that moved two phases past
+  // its waiter would read as not yet complete.
   const uint32_t q_full = bar0;
   const uint32_t k_full0 = bar0 + 8, k_empty0 = bar0 + 24;
   const uint32_t v_full0 = bar0 + 40, v_empty0 = bar0 + 56;
   const uint32_t s_full0 = bar0 + 72;
   const uint32_t p_ready0 = bar0 + 88, o_done = bar0 + 104, drain_bar = bar0 + 112;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 120);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 124);
-  volatile int* never_flag = reinterpret_cast<volatile int*>(tail + 128);
+  const uint32_t q_empty = bar0 + 120, o_free0 = bar0 + 128;
+  const uint32_t tile_full0 = bar0 + 144, tile_empty0 = bar0 + 160;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 176);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 180);
+  volatile int* never_flag = reinterpret_cast<volatile int*>(tail + 184);
+  volatile int* tile_slot = reinterpret_cast<volatile int*>(tail + 192);  // [2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int ntq = (p.seq + BQ - 1) / BQ;
-  // (batch, head)-major: the q tiles of one head run together and share its K / V tiles
-  // through L2; within a head the longest tiles (most kv blocks) start first
-  const int bh = static_cast<int>(blockIdx.x) / ntq;
-  const int qt = ntq - 1 - (static_cast<int>(blockIdx.x) - bh * ntq);
-  const int b = bh / p.heads, h = bh - (bh / p.heads) * p.heads;
-  const int q0 = qt * BQ;
-  const int nblk = qt + 1;  // causal: kv blocks 0..qt
-  const int row0 = b * p.seq;
+  const int ntiles = ntq * p.batch * p.heads;
+  // tile k: (batch, head)-major so that the tiles in flight on the GPU at any time share a
+  // few heads' K / V tiles through L2; within a head the longest tiles (most kv blocks)
+  // first.  Tiles are handed out in that order by a global counter: the K producer of a CTA
+  // takes the next one when it is ready for it and passes it to the CTA's other roles
+  // through a 2-slot ring (tile_full / tile_empty; -1 = no more tiles).
+  struct Tile {
+    int h, qt, q0, nblk, row0;
+  };
+  auto tile_of = [&](int k) {
+    Tile t;
+    const int bh = k / ntq;
+    t.qt = ntq - 1 - (k - bh * ntq);
+    const int b = bh / p.heads;
+    t.h = bh - b * p.heads;
+    t.q0 = t.qt * BQ;
+    t.nblk = t.qt + 1;  // causal: kv blocks 0..qt
+    t.row0 = b * p.seq;
+    return t;
+  };
+  // the MMA thread, the V producer and the eight softmax warps release a slot
+  constexpr uint32_t kTileConsumers = 10;
+  auto take_tile = [&](int i, int& k) -> bool {  // one thread of a consumer role
+    const int sl = i & 1;
+    if (!ptx::mbar_wait(tile_full0 + 8u * sl, (i >> 1) & 1, abort_flag, p.status,
+                        kTimeoutCycles, DS_ERR_TIMEOUT))
+      return false;
+    k = tile_slot[sl];
+    ptx::mbar_arrive(tile_empty0 + 8u * sl);
+    return true;
+  };
 
   if (threadIdx.x == 0) {
     ptx::mbar_init(q_full, 1);
+    ptx::mbar_init(q_empty, 1);
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(k_full0 + 8u * s, 1);
       ptx::mbar_init(k_empty0 + 8u * s, 1);
@@ -121,6 +150,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(v_empty0 + 8u * s, 1);
       ptx::mbar_init(s_full0 + 8u * s, 1);
       ptx::mbar_init(p_ready0 + 8u * s, 8);
+      ptx::mbar_init(o_free0 + 8u * s, 8);
+    }
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(tile_full0 + 8u * s, 1);
+      ptx::mbar_init(tile_empty0 + 8u * s, kTileConsumers);
     }
     ptx::mbar_init(o_done, 1);
     ptx::mbar_init(drain_bar, 1);
@@ -143,56 +177,141 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 || warp == 10) {
     // ------------------------------------------------------------------ TMA producers
-    // warp 0: Q, then the K tiles (each waits only for the S MMA of the block two back);
-    // warp 10: the V^T tiles (each waits for the P V of the block two back)
+    // warp 0: per tile its Q (once the previous tile's last S MMA has read the Q buffer),
+    // then the K tiles (each waits only for the S MMA of the block two back); warp 10: the
+    // V tiles (each waits for the P V of the block two back).  Both run ahead into the next
+    // tile while the current one finishes.
     if (lane == 0) {
       const bool is_k = warp == 0;
-      if (is_k) {
-        ptx::mbar_arrive_expect_tx(q_full, Q_BYTES);
-        for (int c = 0; c < 3; ++c)
-          ptx::tma_load_2d(sQ + c * CHUNK, &tmQ, q_full, h * 192 + c * 64, row0 + q0);
-      }
       const uint32_t full0 = is_k ? k_full0 : v_full0;
       const uint32_t empty0 = is_k ? k_empty0 : v_empty0;
-      int issued = 0;
-      for (int j = 0; j < nblk; ++j) {
-        const int st = j & 1;
-        if (!ptx::mbar_wait(empty0 + 8u * st, ((j >> 1) & 1) ^ 1u, abort_flag, p.status,
-                            kTimeoutCycles, DS_ERR_TIMEOUT))
+      int g = 0, ti = 0, q_issued = 0;
+      bool ok = true;
+      for (;; ++ti) {
+        int k = -1;
+        if (is_k) {  // fetch the next tile into slot ti & 1 once its previous use is released
+          const int sl = ti & 1;
+          if (!ptx::mbar_wait(tile_empty0 + 8u * sl, ((ti >> 1) & 1) ^ 1u, abort_flag, p.status,
+                              kTimeoutCycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          k = atomicAdd(p.tile_counter, 1);
+          if (k >= ntiles) k = -1;
+          tile_slot[sl] = k;
+          ptx::mbar_arrive(tile_full0 + 8u * sl);
+        } else if (!take_tile(ti, k)) {
+          ok = false;
           break;
-        const uint32_t fb = full0 + 8u * st;
-        if (is_k) {
-          ptx::mbar_arrive_expect_tx(fb, K_BYTES);
-          const uint32_t kd = sK + st * K_BYTES;
-          ptx::tma_load_2d(kd, &tmKV, fb, h * 256, row0 + j * BKV);
-          ptx::tma_load_2d(kd + CHUNK, &tmKV, fb, h * 256 + 64, row0 + j * BKV);
-          ptx::tma_load_2d(kd + 2 * CHUNK, &tmQ, fb, p.krope_col, row0 + j * BKV);
-        } else {
-          ptx::mbar_arrive_expect_tx(fb, V_BYTES);
-          const uint32_t vd = sV + st * V_BYTES;
-          // V_j: kv rows j*128 .. +127, head h's v dims 0-63 and 64-127
-          ptx::tma_load_2d(vd, &tmKV, fb, h * 256 + 128, row0 + j * BKV);
-          ptx::tma_load_2d(vd + CHUNK, &tmKV, fb, h * 256 + 192, row0 + j * BKV);
         }
-        issued = j + 1;
+        if (k < 0) break;
+        const Tile t = tile_of(k);
+        if (is_k) {
+          if (!ptx::mbar_wait(q_empty, (ti & 1) ^ 1u, abort_flag, p.status, kTimeoutCycles,
+                              DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(q_full, Q_BYTES);
+          for (int c = 0; c < 3; ++c)
+            ptx::tma_load_2d(sQ + c * CHUNK, &tmQ, q_full, t.h * 192 + c * 64, t.row0 + t.q0);
+          ++q_issued;
+        }
+        for (int j = 0; j < t.nblk; ++j, ++g) {
+          const int st = g & 1;
+          if (!ptx::mbar_wait(empty0 + 8u * st, ((g >> 1) & 1) ^ 1u, abort_flag, p.status,
+                              kTimeoutCycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + 8u * st;
+          if (is_k) {
+            ptx::mbar_arrive_expect_tx(fb, K_BYTES);
+            const uint32_t kd = sK + st * K_BYTES;
+            ptx::tma_load_2d(kd, &tmKV, fb, t.h * 256, t.row0 + j * BKV);
+            ptx::tma_load_2d(kd + CHUNK, &tmKV, fb, t.h * 256 + 64, t.row0 + j * BKV);
+            ptx::tma_load_2d(kd + 2 * CHUNK, &tmQ, fb, p.krope_col, t.row0 + j * BKV);
+          } else {
+            ptx::mbar_arrive_expect_tx(fb, V_BYTES);
+            const uint32_t vd = sV + st * V_BYTES;
+            // V_j: kv rows j*128 .. +127, head h's v dims 0-63 and 64-127
+            ptx::tma_load_2d(vd, &tmKV, fb, t.h * 256 + 128, t.row0 + j * BKV);
+            ptx::tma_load_2d(vd + CHUNK, &tmKV, fb, t.h * 256 + 192, t.row0 + j * BKV);
+          }
+        }
+        if (!ok) break;
       }
-      // every load issued here lands before the CTA exits: the last phase of each stage
-      if (is_k)
-        ptx::mbar_wait(q_full, 0, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
-      for (int j = issued - 1; j >= 0 && j >= issued - 2; --j)
-        ptx::mbar_wait(full0 + 8u * (j & 1), (j >> 1) & 1, never_flag, p.status,
+      // every load issued here lands before the CTA exits: the last Q, the last phase of
+      // each stage (a load whose stage wait failed was not issued)
+      if (is_k && q_issued > 0)
+        ptx::mbar_wait(q_full, (q_issued - 1) & 1, never_flag, p.status, kTimeoutCycles,
+                       DS_ERR_TIMEOUT);
+      for (int gg = g - 1; gg >= 0 && gg >= g - 2; --gg)
+        ptx::mbar_wait(full0 + 8u * (gg & 1), (gg >> 1) & 1, never_flag, p.status,
                        kTimeoutCycles, DS_ERR_TIMEOUT);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // For block g: S_g = Q K_g^T into S buffer g & 1, then P_{g-1} V_{g-1} into the O buffer
+    // of the tile (tile parity).  A tile's last P V is issued before the wait for the next
+    // tile's Q, so the tile's epilogue does not wait for that load.
     if (lane == 0) {
       constexpr uint32_t idesc = ptx::idesc_bf16_f32(128, 128);
-      bool ok = ptx::mbar_wait(q_full, 0, abort_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
-      ptx::tc_fence_after();
-      for (int j = 0; ok && j <= nblk; ++j) {
-        if (j < nblk) {
-          const int st = j & 1;
-          if (!ptx::mbar_wait(k_full0 + 8u * st, (j >> 1) & 1, abort_flag, p.status,
+      // B = V [128 kv (K) x 128 dims (N)] MN-major: dims 0-63 of a kv row in one 128-byte
+      // row of the first box, dims 64-127 one box (LBO) on; 16 kv rows per step
+      constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32_bmn(128, 128);
+      bool ok = true;
+      int g = 0, ti = 0;
+      bool pending = false;             // block g-1's P V is still to be issued
+      int prev_first = 0, prev_ti = 0;  // block g-1: first of its tile?, its tile index
+      auto issue_pv = [&](int gp, bool first, int pti) -> bool {
+        const int st = gp & 1;
+        if (first) {  // overwrites O buffer pti & 1: the epilogue of tile pti - 2 is done
+          if (!ptx::mbar_wait(o_free0 + 8u * (pti & 1), ((pti >> 1) & 1) ^ 1u, abort_flag,
+                              p.status, kTimeoutCycles, DS_ERR_TIMEOUT))
+            return false;
+        }
+        if (!ptx::mbar_wait(p_ready0 + 8u * st, (gp >> 1) & 1, abort_flag, p.status,
+                            kTimeoutCycles, DS_ERR_TIMEOUT) ||
+            !ptx::mbar_wait(v_full0 + 8u * st, (gp >> 1) & 1, abort_flag, p.status,
+                            kTimeoutCycles, DS_ERR_TIMEOUT))
+          return false;
+        ptx::tc_fence_after();
+        const uint32_t pa = tmem + (st ? kSCol1 : kSCol0);
+        const uint32_t vb = sV + st * V_BYTES;
+        const uint32_t od = tmem + ((pti & 1) ? kOCol1 : kOCol0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          ptx::umma_f16_ts(od, pa + kk * 8, ptx::sw128_mnmajor_desc(vb + kk * 16 * 128, CHUNK),
+                           idesc_pv, (!first || kk > 0) ? 1u : 0u);
+        ptx::umma_commit(v_empty0 + 8u * st);
+        ptx::umma_commit(o_done);
+        return true;
+      };
+      for (;; ++ti) {
+        // the last P V of tile ti-1 first: its epilogue must not wait for tile ti's Q
+        if (pending) {
+          if (!issue_pv(g - 1, prev_first != 0, prev_ti)) {
+            ok = false;
+            break;
+          }
+          pending = false;
+        }
+        int k = -1;
+        if (!take_tile(ti, k)) {
+          ok = false;
+          break;
+        }
+        if (k < 0) break;
+        const Tile t = tile_of(k);
+        if (!ptx::mbar_wait(q_full, ti & 1, abort_flag, p.status, kTimeoutCycles,
+                            DS_ERR_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        for (int j = 0; j < t.nblk; ++j, ++g) {
+          const int st = g & 1;
+          if (!ptx::mbar_wait(k_full0 + 8u * st, (g >> 1) & 1, abort_flag, p.status,
                               kTimeoutCycles, DS_ERR_TIMEOUT)) {
             ok = false;
             break;
@@ -208,32 +327,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::umma_commit(k_empty0 + 8u * st);
           ptx::umma_commit(s_full0 + 8u * st);
-        }
-        if (j >= 1) {
-          const int jp = j - 1;
-          const int st = jp & 1;
-          if (!ptx::mbar_wait(p_ready0 + 8u * st, (jp >> 1) & 1, abort_flag, p.status,
-                              kTimeoutCycles, DS_ERR_TIMEOUT) ||
-              !ptx::mbar_wait(v_full0 + 8u * st, (jp >> 1) & 1, abort_flag, p.status,
-                              kTimeoutCycles, DS_ERR_TIMEOUT)) {
+          if (j == t.nblk - 1) ptx::umma_commit(q_empty);  // the tile's last read of Q
+          if (pending && !issue_pv(g - 1, prev_first != 0, prev_ti)) {
             ok = false;
             break;
           }
-          ptx::tc_fence_after();
-          const uint32_t pa = tmem + (st ? kSCol1 : kSCol0);
-          const uint32_t vb = sV + st * V_BYTES;
-          // B = V_j [128 kv (K) x 128 dims (N)] MN-major: dims 0-63 of a kv row in one
-          // 128-byte row of the first box, dims 64-127 one box (LBO) on; 16 kv rows per step
-          constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32_bmn(128, 128);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            ptx::umma_f16_ts(tmem + kOCol, pa + kk * 8,
-                             ptx::sw128_mnmajor_desc(vb + kk * 16 * 128, CHUNK), idesc_pv,
-                             (jp > 0 || kk > 0) ? 1u : 0u);
-          ptx::umma_commit(v_empty0 + 8u * st);
-          ptx::umma_commit(o_done);
+          pending = true;
+          prev_first = j == 0;
+          prev_ti = ti;
         }
+        if (!ok) break;
       }
+      if (ok && pending) issue_pv(g - 1, prev_first != 0, prev_ti);
       // no MMA may still be running when TMEM is released
       ptx::umma_commit(drain_bar);
       ptx::mbar_wait(drain_bar, 0, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
@@ -242,158 +347,180 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ softmax (warps 2-9)
     // Two warps per 32-row TMEM quarter: `half` 0 takes S columns 0..63 (and O columns
     // 0..63), half 1 columns 64..127.  Each thread holds one row's 64 values; the pair
-    // exchanges its partial row max through shared memory (named barrier 1 + quarter, 64
-    // threads), which also orders both warps' S loads before either writes P over S.
+    // exchanges its partial row max and its wait result through shared memory (one named
+    // barrier, 1 + quarter, 64 threads, per block), which also orders both warps' S loads
+    // before either writes P over S.
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // q row within the tile (= TMEM lane)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t ob = tmem + lane_off + kOCol + half * 64;
     float* red = reinterpret_cast<float*>(tail + 256);  // [2 parity][2 half][128 rows]
+    int* red_ok = reinterpret_cast<int*>(tail + 256 + 6 * 128 * 4);  // [2 parity][2 half][4]
     const uint32_t pair_bar = 1 + quarter;
     // m: the max the row's P values are taken against (log2 domain).  It is raised only when
     // the row max grows by more than kLazy (so P <= 2^kLazy), which leaves O untouched on
     // most blocks; l and O always refer to the same m, and the final O / l is exact.
     constexpr float kLazy = 8.f;
-    float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      const int st = j & 1;
-      int w_ok = 1;
-      if (lane == 0)
-        w_ok = ptx::mbar_wait(s_full0 + 8u * st, (j >> 1) & 1, abort_flag, p.status,
-                              kTimeoutCycles, DS_ERR_TIMEOUT)
-                   ? 1
-                   : 0;
-      // the partner warp must not block in the named barrier below: the pair agrees first
-      w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-      red[(st * 2 + half) * 128 + r] = w_ok ? 0.f : 1.f;
+    int g = 0, ti = 0;
+    int* tile_x = reinterpret_cast<int*>(tail + 256 + 6 * 128 * 4 + 64);  // [2][2 half][4]
+    // the tile loop is left only where the pair has agreed (the tile exchange below, or
+    // after the sum exchange), so neither warp of a pair is left waiting in a named barrier
+    for (;; ++ti) {
+      int k = -1;
+      if (lane == 0 && ok && !take_tile(ti, k)) k = -1;
+      k = __shfl_sync(0xffffffffu, k, 0);
+      tile_x[((ti & 1) * 2 + half) * 4 + quarter] = k;
       ptx::named_bar_sync(pair_bar, 64);
-      const bool pair_ok = w_ok && red[(st * 2 + (half ^ 1)) * 128 + r] == 0.f;
-      ptx::named_bar_sync(pair_bar, 64);
-      if (!pair_ok) {
-        ok = false;
-        break;
-      }
-      ptx::tc_fence_after();
-      const uint32_t sb = tmem + lane_off + (st ? kSCol1 : kSCol0);
-      uint32_t v[2][32];
-      ptx::tmem_ld32(sb + half * 64, v[0]);
-      ptx::tmem_ld32(sb + half * 64 + 32, v[1]);
-      ptx::tmem_wait_ld2(v[0], v[1]);
-      if (j == qt) {  // diagonal block: kv column > q row is masked
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (half * 64 + c * 32 + i > r) v[c][i] = __float_as_uint(-INFINITY);
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        mx0 = fmaxf(mx0, __uint_as_float(v[0][i]));
-        mx1 = fmaxf(mx1, __uint_as_float(v[0][16 + i]));
-        mx2 = fmaxf(mx2, __uint_as_float(v[1][i]));
-        mx3 = fmaxf(mx3, __uint_as_float(v[1][16 + i]));
-      }
-      // exchange the partial max (double-buffered by block parity); the barrier also puts
-      // both warps' S loads before any P store below
-      red[(st * 2 + half) * 128 + r] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      ptx::tc_fence_before();
-      ptx::named_bar_sync(pair_bar, 64);
-      ptx::tc_fence_after();
-      const float mcand = fmaxf(red[(st * 2) * 128 + r], red[(st * 2 + 1) * 128 + r]) * p.scale_log2;
-      float alpha = 1.f;
-      if (mcand > m + kLazy) {
-        alpha = ptx::ex2(m - mcand);  // 0 on the first block (m = -inf)
-        m = mcand;
-      }
-      const float neg = -m;
-      // P = 2^(s*scale - m) as bf16: this half's 64 values -> P columns half*32 .. +32
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ptx::ex2(fmaf(__uint_as_float(v[c][2 * i]), p.scale_log2, neg));
-          const float p1 = ptx::ex2(fmaf(__uint_as_float(v[c][2 * i + 1]), p.scale_log2, neg));
-          sum0 += p0;
-          sum1 += p1;
-          const __nv_bfloat162 hp = __floats2bfloat162_rn(p0, p1);
-          w[i] = *reinterpret_cast<const uint32_t*>(&hp);
-        }
-        ptx::tmem_st16(sb + half * 32 + c * 16, w);
-      }
-      l = l * alpha + (sum0 + sum1);  // this half's share of the row sum
-      // The P V of block j-1 must have landed before O is touched.  o_done is waited at every
-      // block, in order: the P V of block j cannot start before this warp's p_ready arrival,
-      // so o_done is never more than one phase past the phase waited for.
-      if (j > 0) {
-        int o_ok = 1;
-        if (lane == 0)
-          o_ok = ptx::mbar_wait(o_done, (j - 1) & 1, abort_flag, p.status, kTimeoutCycles,
-                                DS_ERR_TIMEOUT)
+      k = min(k, tile_x[((ti & 1) * 2 + (half ^ 1)) * 4 + quarter]);
+      if (k < 0) break;  // no more tiles, or a failed wait in either warp
+      const Tile t = tile_of(k);
+      const uint32_t ob = tmem + lane_off + ((ti & 1) ? kOCol1 : kOCol0) + half * 64;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < t.nblk; ++j, ++g) {
+        const int st = g & 1;
+        int w_ok = 0;
+        if (lane == 0 && ok)
+          w_ok = ptx::mbar_wait(s_full0 + 8u * st, (g >> 1) & 1, abort_flag, p.status,
+                                kTimeoutCycles, DS_ERR_TIMEOUT)
                      ? 1
                      : 0;
-        // a failed wait does not leave the loop here (the partner warp would then wait in
-        // the named barrier for good): the abort flag is set, so the next block's s_full
-        // wait fails at once and the pair leaves together after its flag exchange
-        if (!__shfl_sync(0xffffffffu, o_ok, 0)) ok = false;
+        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         ptx::tc_fence_after();
-        if (ok && __any_sync(0xffffffffu, alpha != 1.f)) {
-          uint32_t o[2][32];
-          ptx::tmem_ld32(ob, o[0]);
-          ptx::tmem_ld32(ob + 32, o[1]);
-          ptx::tmem_wait_ld2(o[0], o[1]);
+        // S is read even after a failed wait (then discarded), so the pair stays in step
+        const uint32_t sb = tmem + lane_off + (st ? kSCol1 : kSCol0);
+        uint32_t v[2][32];
+        ptx::tmem_ld32(sb + half * 64, v[0]);
+        ptx::tmem_ld32(sb + half * 64 + 32, v[1]);
+        ptx::tmem_wait_ld2(v[0], v[1]);
+        if (j == t.qt) {  // diagonal block: kv column > q row is masked
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
-            ptx::tmem_st32(ob + c * 32, o[c]);
+            for (int i = 0; i < 32; ++i)
+              if (half * 64 + c * 32 + i > r) v[c][i] = __float_as_uint(-INFINITY);
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          mx0 = fmaxf(mx0, __uint_as_float(v[0][i]));
+          mx1 = fmaxf(mx1, __uint_as_float(v[0][16 + i]));
+          mx2 = fmaxf(mx2, __uint_as_float(v[1][i]));
+          mx3 = fmaxf(mx3, __uint_as_float(v[1][16 + i]));
+        }
+        // exchange the partial max and the wait result (double-buffered by block parity);
+        // the barrier also puts both warps' S loads before any P store below
+        red[(st * 2 + half) * 128 + r] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        if (lane == 0) red_ok[(st * 2 + half) * 4 + quarter] = w_ok;
+        ptx::tc_fence_before();
+        ptx::named_bar_sync(pair_bar, 64);
+        ptx::tc_fence_after();
+        if (!(w_ok && red_ok[(st * 2 + (half ^ 1)) * 4 + quarter])) {  // the pair agrees
+          ok = false;
+          break;
+        }
+        const float mcand = fmaxf(red[(st * 2) * 128 + r], red[(st * 2 + 1) * 128 + r]) * p.scale_log2;
+        float alpha = 1.f;
+        if (mcand > m + kLazy) {
+          alpha = ptx::ex2(m - mcand);  // 0 on the first block (m = -inf)
+          m = mcand;
+        }
+        const float neg = -m;
+        // P = 2^(s*scale - m) as bf16: this half's 64 values -> P columns half*32 .. +32
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = ptx::ex2(fmaf(__uint_as_float(v[c][2 * i]), p.scale_log2, neg));
+            const float p1 = ptx::ex2(fmaf(__uint_as_float(v[c][2 * i + 1]), p.scale_log2, neg));
+            sum0 += p0;
+            sum1 += p1;
+            const __nv_bfloat162 hp = __floats2bfloat162_rn(p0, p1);
+            w[i] = *reinterpret_cast<const uint32_t*>(&hp);
+          }
+          ptx::tmem_st16(sb + half * 32 + c * 16, w);
+        }
+        l = l * alpha + (sum0 + sum1);  // this half's share of the row sum
+        // The P V of block g-1 (same tile) must have landed before O is touched.  o_done is
+        // waited at every block but a tile's first, in order: the P V of block g cannot start
+        // before this warp's p_ready arrival and that of block g-2 finished before S_g, so
+        // o_done is never more than one phase past the phase waited for.
+        if (j > 0) {
+          int o_ok = 1;
+          if (lane == 0)
+            o_ok = ptx::mbar_wait(o_done, (g - 1) & 1, abort_flag, p.status, kTimeoutCycles,
+                                  DS_ERR_TIMEOUT)
+                       ? 1
+                       : 0;
+          // a failed wait does not leave the loop here: it is carried into the next
+          // block's exchange (or the tile's sum exchange), where the pair leaves together
+          if (!__shfl_sync(0xffffffffu, o_ok, 0)) ok = false;
+          ptx::tc_fence_after();
+          if (ok && __any_sync(0xffffffffu, alpha != 1.f)) {
+            uint32_t o[2][32];
+            ptx::tmem_ld32(ob, o[0]);
+            ptx::tmem_ld32(ob + 32, o[1]);
+            ptx::tmem_wait_ld2(o[0], o[1]);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
+              ptx::tmem_st32(ob + c * 32, o[c]);
+            }
           }
         }
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(p_ready0 + 8u * st);
       }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(p_ready0 + 8u * st);
-    }
-    // the row sum is the two halves' shares (same m); exchanged once more
-    red[(2 * 2 + half) * 128 + r] = ok ? l : -1.f;
-    ptx::named_bar_sync(pair_bar, 64);
-    const float l_other = red[(2 * 2 + (half ^ 1)) * 128 + r];
-    if (ok && l_other >= 0.f) {
+      // the row sum is the two halves' shares (same m); exchanged once more (a negative
+      // share marks a failed warp, and the pair then leaves together)
+      red[(2 * 2 + half) * 128 + r] = ok ? l : -1.f;
+      ptx::named_bar_sync(pair_bar, 64);
+      const float l_other = red[(2 * 2 + (half ^ 1)) * 128 + r];
+      // the partner's share has been read before either warp can write the next tile's
+      ptx::named_bar_sync(pair_bar, 64);
+      ok = ok && __all_sync(0xffffffffu, l_other >= 0.f);
+      if (!ok) break;
       int o_ok = 1;
       if (lane == 0)
-        o_ok = ptx::mbar_wait(o_done, (nblk - 1) & 1, abort_flag, p.status, kTimeoutCycles,
+        o_ok = ptx::mbar_wait(o_done, (g - 1) & 1, abort_flag, p.status, kTimeoutCycles,
                               DS_ERR_TIMEOUT)
                    ? 1
                    : 0;
-      if (__shfl_sync(0xffffffffu, o_ok, 0)) {
-        ptx::tc_fence_after();
-        const float inv = 1.f / (l + l_other);
-        const bool valid = q0 + r < p.seq;
-        __nv_bfloat16* dst = p.out + static_cast<int64_t>(row0 + q0 + r) * p.ldo +
-                             static_cast<int64_t>(h) * 128 + half * 64;
-        uint32_t o[2][32];
-        ptx::tmem_ld32(ob, o[0]);
-        ptx::tmem_ld32(ob + 32, o[1]);
-        ptx::tmem_wait_ld2(o[0], o[1]);
-        if (valid) {
+      if (!__shfl_sync(0xffffffffu, o_ok, 0)) {
+        ok = false;  // the next tile's first exchange takes the pair out together
+        continue;
+      }
+      ptx::tc_fence_after();
+      const float inv = 1.f / (l + l_other);
+      const bool valid = t.q0 + r < p.seq;
+      __nv_bfloat16* dst = p.out + static_cast<int64_t>(t.row0 + t.q0 + r) * p.ldo +
+                           static_cast<int64_t>(t.h) * 128 + half * 64;
+      uint32_t o[2][32];
+      ptx::tmem_ld32(ob, o[0]);
+      ptx::tmem_ld32(ob + 32, o[1]);
+      ptx::tmem_wait_ld2(o[0], o[1]);
+      // this O buffer may be overwritten by the tile after next
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(o_free0 + 8u * (ti & 1));
+      if (valid) {
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t w[16];
-            float r0, r1;
+        for (int c = 0; c < 2; ++c) {
+          uint32_t w[16];
+          float r0, r1;
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              w[i] = pack_bf16(__uint_as_float(o[c][2 * i]) * inv,
-                               __uint_as_float(o[c][2 * i + 1]) * inv, r0, r1);
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack_bf16(__uint_as_float(o[c][2 * i]) * inv,
+                             __uint_as_float(o[c][2 * i + 1]) * inv, r0, r1);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-          }
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
     }
@@ -509,7 +636,8 @@ int tmap_2d(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t
 // Attention over qkv (RoPE already applied in place) and kv
 // [batch*heads*128, seq]; out [batch*seq, heads*128].
 int launch_attention(const void* qkv, int ldq, const void* kv, void* out, int batch,
-                     int seq, int heads, float softmax_scale, cudaStream_t s) {
+                     int seq, int heads, float softmax_scale, int* tile_counter,
+                     cudaStream_t s) {
   DS_REQUIRE(batch >= 1 && seq >= 1 && heads >= 1, "mla_attention: bad shape");
   DS_REQUIRE(seq % 8 == 0, "mla_attention: seq_len must be a multiple of 8");
   DS_REQUIRE(ldq % 8 == 0 && ldq >= heads * 192 + 512 + 64, "mla_attention: bad qkv stride");
@@ -538,10 +666,16 @@ int launch_attention(const void* qkv, int ldq, const void* kv, void* out, int ba
   p.scale_log2 = static_cast<float>(static_cast<double>(softmax_scale) * 1.4426950408889634);
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = heads * 128;
+  p.tile_counter = tile_counter;
   p.status = device_status_ptr();
   if (p.status == nullptr) return fail(DS_ERR_CUDA, "device status word unavailable");
-  const int ntq = (seq + BQ - 1) / BQ;
-  mla_attention_kernel<<<ntq * batch * heads, kThreads, kSmemBytes, s>>>(tq, tkv, p);
+  DS_REQUIRE(tile_counter != nullptr, "mla_attention: no tile counter");
+  DS_CUDA(cudaMemsetAsync(tile_counter, 0, sizeof(int), s));
+  // persistent: one CTA per SM (the shared memory allows no more) walks its tiles
+  const int64_t ntiles = static_cast<int64_t>((seq + BQ - 1) / BQ) * batch * heads;
+  DS_REQUIRE(ntiles < (int64_t(1) << 31), "mla_attention: too many tiles");
+  const int grid = static_cast<int>(ntiles < di.num_sms ? ntiles : di.num_sms);
+  mla_attention_kernel<<<grid, kThreads, kSmemBytes, s>>>(tq, tkv, p);
   DS_LAUNCH_CHECK("mla_attention_kernel");
   return DS_OK;
 }
@@ -571,6 +705,7 @@ struct MlaBuffers {
   void* lat;  // bf16 [M, 512]
   void* kv;   // bf16 [M, heads*256]
   void* o;    // bf16 [M, heads*128]
+  int* tiles;  // the attention's tile counter
 };
 
 constexpr int kLatent = 512;
@@ -584,6 +719,7 @@ size_t carve_mla(ds::Carve& c, MlaBuffers* b, int batch, int seq, int heads) {
   x.lat = c.take<__nv_bfloat16>(M * kLatent);
   x.kv = c.take<__nv_bfloat16>(M * heads * 256);
   x.o = c.take<__nv_bfloat16>(M * heads * 128);
+  x.tiles = c.take<int>(64);
   if (b) *b = x;
   return ds::align_up(c.used, 256);
 }
@@ -618,7 +754,7 @@ size_t ds_mla_attention_workspace_size(int batch, int seq, int heads) {
   (void)batch;
   (void)seq;
   (void)heads;
-  return 0;  // the attention reads v in place: no scratch
+  return 256;  // the tile counter (v is read in place)
 }
 
 int ds_mla_attention(const void* qkv_bf16, int qkv_ld, const void* kv_bf16, void* out_bf16,
@@ -627,10 +763,12 @@ int ds_mla_attention(const void* qkv_bf16, int qkv_ld, const void* kv_bf16, void
   DS_REQUIRE(batch >= 0 && seq >= 0 && heads >= 1, "mla_attention: bad shape");
   if (batch == 0 || seq == 0) return DS_OK;
   DS_REQUIRE(qkv_bf16 && kv_bf16 && out_bf16, "mla_attention: null pointer");
-  (void)workspace;
-  (void)workspace_bytes;
+  DS_REQUIRE(workspace != nullptr && workspace_bytes >= 256 &&
+                 (reinterpret_cast<uintptr_t>(workspace) & 3u) == 0,
+             "mla_attention: workspace needs 256 bytes");
   return ds::attn::launch_attention(qkv_bf16, qkv_ld, kv_bf16, out_bf16, batch, seq, heads,
-                                    softmax_scale, static_cast<cudaStream_t>(stream));
+                                    softmax_scale, static_cast<int*>(workspace),
+                                    static_cast<cudaStream_t>(stream));
 }
 
 size_t ds_mla_forward_workspace_size(int batch, int seq, int hidden, int heads) {
@@ -709,7 +847,7 @@ int mla_forward_impl(const void* x_bf16, const void* w_qkv_a_bf16, const float* 
   DS_TRY(ds::attn::launch_mla_rope(b.qkv, ldq, M, seq, heads, cos_bf16, sin_bf16, positions, s));
   DS_TRY(mark(4));
   DS_TRY(ds::attn::launch_attention(b.qkv, ldq, b.kv, b.o, batch, seq, heads,
-                                    softmax_scale, s));
+                                    softmax_scale, b.tiles, s));
   DS_TRY(mark(5));
   DS_TRY(ds::gemm::launch(dense_problem(b.o, M, heads * 128, w_o_bf16, hidden, out_bf16), s));
   DS_TRY(mark(6));

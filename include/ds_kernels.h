@@ -222,8 +222,10 @@ DS_API int ds_rope(const void* q_pe_bf16, const void* k_pe_bf16, const void* cos
  * 128 nope then 64 RoPE-rotated), then the 512-wide latent, then the 64-wide rotated k_pe;
  * kv bf16 [batch*seq, heads*256] holds per head 128 k_nope then 128 v; out bf16
  * [batch*seq, heads*128] (head h in columns h*128 ..).  Causal; seq % 8 == 0.  v is read in
- * place, so ds_mla_attention_workspace_size returns 0 and workspace may be NULL (both stay in
- * the signature for callers written against the earlier form). */
+ * place; workspace (ds_mla_attention_workspace_size bytes, 4-byte aligned) holds the counter
+ * from which the persistent kernel's CTAs take their (batch, head, q tile) work items; it is
+ * zeroed on `stream` before the launch, so calls on different streams need different
+ * workspaces. */
 DS_API size_t ds_mla_attention_workspace_size(int batch, int seq, int heads);
 DS_API int ds_mla_attention(const void* qkv_bf16, int qkv_ld, const void* kv_bf16,
                             void* out_bf16, int batch, int seq, int heads, float softmax_scale,
