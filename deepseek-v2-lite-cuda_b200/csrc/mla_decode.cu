@@ -16,22 +16,26 @@
 //   out   = o_lat @ W_ouv^T    W_ouv_h = W_o_h W_uv_h diag(g)
 // and the attention reads the cache once: it is HBM-bound (576 bf16 + 68 bytes per token).
 //
-// Attention kernel: one CTA per (sequence, split of the positions), 192 threads, ~95 KB of
-// shared memory, so two CTAs share an SM and one CTA's chunk load overlaps the other's
-// chain of MMAs and softmax (a CTA's own chunks run one after another).
-//   warp 0   TMA producer: the sequence's Q (16 heads x 576: nine 16x64 boxes) once, then per
-//            64-token chunk the latent (eight 64x64 boxes) and k_pe_rot (one box).
-//   warp 1   MMA issuer: S^T = C Q'^T (M = 64 tokens, N = 16 heads, K = 512) and the RoPE
-//            part (K = 64) into two TMEM accumulators (M = 64 puts token r in lane
-//            32 (r / 16) + r % 16); after the softmax, O^T += C^T P^T (M = 128 latent dims x 4
-//            blocks, N = 16 heads, K = 64 tokens) with the SAME latent tile read as an
-//            MN-major A operand (no second copy of the cache).  These N = 16 MMAs are bound
-//            by the tensor cores' shared-memory operand reads, so each one reads only the
-//            chunk's 64 token rows: every latent byte is read once per phase.
-//   warps 2-5  softmax, one token per thread (lanes 0-15 of each warp): s = rstd*S1 + S2 for
-//            the 16 heads, per-head max over the chunk (shuffles + shared memory), lazy running max
+// Attention kernel: one CTA per (sequence, split of the positions) and per SM, 192 threads,
+// 128-token chunks streamed box by box (~167 KB of shared memory).  A chunk is nine TMA
+// boxes of 128 token rows x 64 columns (latent 0..7, k_pe_rot), each with its own full and
+// empty barrier: the S^T MMAs of a box are issued as soon as it lands, and a box of the next
+// chunk is loaded as soon as the MMAs of this chunk that read it are done (k_pe_rot after
+// S^T, latent boxes 2i and 2i+1 after the O^T block i), so the loads run under the MMAs and
+// the softmax.  The MMAs have N = 16 (the heads): each costs the tensor pipe's ~46-cycle
+// floor whatever M, so M = 128 tokens per S^T instruction halves their count per token.
+//   warp 0   TMA producer: the sequence's Q (16 heads x 576: nine 16x64 boxes) once, then
+//            per chunk the k_pe_rot box and the eight latent boxes, each once its previous
+//            chunk's readers are done.
+//   warp 1   MMA issuer: S^T = C Q'^T (M = 128 tokens, N = 16 heads, K = 512) and the RoPE
+//            part (K = 64) into two TMEM accumulators (token r in lane r); after the softmax,
+//            O^T += C^T P^T (M = 128 latent dims x 4 blocks, N = 16 heads, K = 128 tokens)
+//            with the SAME latent boxes read as an MN-major A operand (no second copy of
+//            the cache).
+//   warps 2-5  softmax, one token per thread: s = rstd*S1 + S2 for the 16 heads, per-head
+//            max over the chunk (shuffles + shared memory), lazy running max
 //            (O^T rescaled in TMEM only when a head's max grows by more than 2^8), P^T (times
-//            rstd) as bf16 into a 16 x 64 shared-memory tile; at the end the O^T rows (one
+//            rstd) as bf16 into a 16 x 128 shared-memory tile; at the end the O^T rows (one
 //            latent dim per thread), maxima and sums go to a per-split partial.
 // A combine kernel merges the splits per (sequence, head) into o_lat (bf16).
 #include <cuda.h>
@@ -51,14 +55,15 @@ constexpr int kLatent = 512;
 constexpr int kRope = 64;
 constexpr int kQCols = kLatent + kRope;  // 576
 constexpr int kHeads = 16;               // N of the attention MMAs
-constexpr int kChunk = 64;
+constexpr int kChunk = 128;
 constexpr int kThreads = 192;
-constexpr uint32_t kBox = 64 * 64 * 2;         // 64 rows x 64 columns bf16: 8 KiB
+constexpr int kBoxes = 9;                      // latent 0..7, k_pe_rot
+constexpr uint32_t kBox = kChunk * 64 * 2;     // 128 rows x 64 columns bf16: 16 KiB
 constexpr uint32_t kQBox = 16 * 64 * 2;        // 16 rows x 64 columns: 2 KiB
 constexpr uint32_t kQBytes = 9 * kQBox;        // 18 KiB
-constexpr uint32_t kCBytes = 9 * kBox;         // 8 latent boxes + k_pe_rot: 72 KiB
-constexpr uint32_t kPBytes = kQBox;            // P^T: 16 heads x 64 tokens, one 16x64 box
-constexpr uint32_t kTail = 512;
+constexpr uint32_t kCBytes = kBoxes * kBox;    // 144 KiB
+constexpr uint32_t kPBytes = 2 * kQBox;        // P^T: 16 heads x 128 tokens, two 16x64 atoms
+constexpr uint32_t kTail = 1024;  // barriers, TMEM address, flags, then the maxima exchange
 constexpr size_t kSmemBytes = 1024 + kCBytes + kQBytes + kPBytes + kTail;
 constexpr uint32_t kTmemCols = 128;
 constexpr uint32_t kColS1 = 0, kColS2 = 16, kColO = 32;  // O^T: 4 blocks x 16 columns
@@ -74,7 +79,7 @@ struct Params {
   int* status;
 };
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     mla_decode_attn_kernel(const __grid_constant__ CUtensorMap tmQ,   // Q [batch*16, 576]
                            const __grid_constant__ CUtensorMap tmC,   // latent [batch*max_seq, 512]
                            const __grid_constant__ CUtensorMap tmKr,  // k_pe_rot [batch*max_seq, 64]
@@ -84,15 +89,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t sC = ptx::smem_u32(smem);        // 9 boxes: latent 0..7, k_pe_rot
   const uint32_t sQ = sC + kCBytes;               // 9 boxes of 16 x 64
-  const uint32_t sP = sQ + kQBytes;               // 2 boxes of 16 x 64
+  const uint32_t sP = sQ + kQBytes;               // P^T: 2 atoms of 16 x 64
   uint8_t* tail = smem + kCBytes + kQBytes + kPBytes;
   const uint32_t bar0 = ptx::smem_u32(tail);
-  const uint32_t q_full = bar0, c_full = bar0 + 8, c_empty = bar0 + 16, s_full = bar0 + 24;
-  const uint32_t p_ready = bar0 + 32, o_done = bar0 + 40, drain_bar = bar0 + 48;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 56);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 60);
-  volatile int* never_flag = reinterpret_cast<volatile int*>(tail + 64);
-  float* red = reinterpret_cast<float*>(tail + 128);  // [4 warps][16 heads] per-chunk maxima
+  // barriers: box_full[9], box_empty[9], q_full, s_full, p_ready, o_done, drain
+  const uint32_t box_full0 = bar0, box_empty0 = bar0 + 8 * kBoxes;
+  const uint32_t q_full = bar0 + 16 * kBoxes, s_full = q_full + 8, p_ready = q_full + 16;
+  const uint32_t o_done = q_full + 24, drain_bar = q_full + 32;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tail + 192);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 196);
+  volatile int* never_flag = reinterpret_cast<volatile int*>(tail + 200);
+  float* red = reinterpret_cast<float*>(tail + 256);  // [4 warps][16 heads] per-chunk maxima
   uint8_t* sPgen = smem + kCBytes + kQBytes;
 
   const int warp = threadIdx.x >> 5;
@@ -106,9 +113,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int row0 = b * p.max_seq;
 
   if (threadIdx.x == 0) {
+    for (int c = 0; c < kBoxes; ++c) {
+      ptx::mbar_init(box_full0 + 8u * c, 1);
+      ptx::mbar_init(box_empty0 + 8u * c, 1);
+    }
     ptx::mbar_init(q_full, 1);
-    ptx::mbar_init(c_full, 1);
-    ptx::mbar_init(c_empty, 1);
     ptx::mbar_init(s_full, 1);
     ptx::mbar_init(p_ready, 4);
     ptx::mbar_init(o_done, 1);
@@ -136,66 +145,81 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0 && nchunk > 0) {
       ptx::mbar_arrive_expect_tx(q_full, kQBytes);
       for (int c = 0; c < 9; ++c) ptx::tma_load_2d(sQ + c * kQBox, &tmQ, q_full, c * 64, b * kHeads);
-      int issued = 0;
-      for (int j = 0; j < nchunk; ++j) {
-        // the single chunk buffer is free once the previous chunk's O^T MMAs have read it
-        if (!ptx::mbar_wait(c_empty, (j & 1) ^ 1u, abort_flag, p.status, kTimeoutCycles,
-                            DS_ERR_TIMEOUT))
-          break;
-        ptx::mbar_arrive_expect_tx(c_full, kCBytes);
+      // boxes in the order their previous readers finish: k_pe_rot (S^T), then the latent
+      // boxes in O^T block order; box c of chunk j waits for its chunk j-1 readers
+      int loaded[kBoxes] = {};  // loads issued per box
+      bool ok = true;
+      for (int j = 0; ok && j < nchunk; ++j) {
         const int y = row0 + t_begin + j * kChunk;
-        for (int c = 0; c < 8; ++c) ptx::tma_load_2d(sC + c * kBox, &tmC, c_full, c * 64, y);
-        ptx::tma_load_2d(sC + 8 * kBox, &tmKr, c_full, 0, y);
-        issued = j + 1;
+        for (int o = 0; o < kBoxes; ++o) {
+          const int c = o == 0 ? 8 : o - 1;
+          if (!ptx::mbar_wait(box_empty0 + 8u * c, (j & 1) ^ 1u, abort_flag, p.status,
+                              kTimeoutCycles, DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = box_full0 + 8u * c;
+          ptx::mbar_arrive_expect_tx(fb, kBox);
+          if (c < 8) ptx::tma_load_2d(sC + c * kBox, &tmC, fb, c * 64, y);
+          else ptx::tma_load_2d(sC + c * kBox, &tmKr, fb, 0, y);
+          ++loaded[c];
+        }
       }
+      // no copy may still be in flight when the CTA exits: the last load of each box
       ptx::mbar_wait(q_full, 0, never_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
-      if (issued > 0)
-        ptx::mbar_wait(c_full, (issued - 1) & 1, never_flag, p.status, kTimeoutCycles,
-                       DS_ERR_TIMEOUT);
+      for (int c = 0; c < kBoxes; ++c)
+        if (loaded[c] > 0)
+          ptx::mbar_wait(box_full0 + 8u * c, (loaded[c] - 1) & 1, never_flag, p.status,
+                         kTimeoutCycles, DS_ERR_TIMEOUT);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0 && nchunk > 0) {
-      constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(64, kHeads);
+      constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(128, kHeads);
       constexpr uint32_t idesc_o = ptx::idesc_bf16_f32_amn(128, kHeads);
       bool ok = ptx::mbar_wait(q_full, 0, abort_flag, p.status, kTimeoutCycles, DS_ERR_TIMEOUT);
       for (int j = 0; ok && j < nchunk; ++j) {
-        if (!ptx::mbar_wait(c_full, j & 1, abort_flag, p.status, kTimeoutCycles,
-                            DS_ERR_TIMEOUT))
-          break;
-        ptx::tc_fence_after();
-        // S1^T = C Q'^T over the 512 latent columns, S2^T = K_rot Q_pe^T over the 64 RoPE ones
-#pragma unroll 1
-        for (int kk = 0; kk < 32; ++kk) {
-          const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-          const uint32_t qoff = (kk >> 2) * kQBox + (kk & 3) * 32;
-          ptx::umma_f16(tmem + kColS1, ptx::sw128_kmajor_desc(sC + off),
-                        ptx::sw128_kmajor_desc(sQ + qoff), idesc_s, kk > 0 ? 1u : 0u);
-        }
+        // S2^T = K_rot Q_pe^T over the 64 RoPE columns, then S1^T = C Q'^T over the 512
+        // latent ones, box by box as the boxes land
+        for (int o = 0; o < kBoxes; ++o) {
+          const int c = o == 0 ? 8 : o - 1;
+          if (!ptx::mbar_wait(box_full0 + 8u * c, j & 1, abort_flag, p.status, kTimeoutCycles,
+                              DS_ERR_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t cb = sC + c * kBox, qb = sQ + c * kQBox;
+          const uint32_t d = tmem + (c == 8 ? kColS2 : kColS1);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          ptx::umma_f16(tmem + kColS2, ptx::sw128_kmajor_desc(sC + 8 * kBox + kk * 32),
-                        ptx::sw128_kmajor_desc(sQ + 8 * kQBox + kk * 32), idesc_s,
-                        kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)
+            ptx::umma_f16(d, ptx::sw128_kmajor_desc(cb + kk * 32),
+                          ptx::sw128_kmajor_desc(qb + kk * 32), idesc_s,
+                          (kk > 0 || o > 1) ? 1u : 0u);
+          if (c == 8) ptx::umma_commit(box_empty0 + 8u * 8);  // k_pe_rot: read only by S^T
+        }
+        if (!ok) break;
         ptx::umma_commit(s_full);
         if (!ptx::mbar_wait(p_ready, j & 1, abort_flag, p.status, kTimeoutCycles,
                             DS_ERR_TIMEOUT))
           break;
         ptx::tc_fence_after();
-        // O^T (4 blocks of 128 latent dims) += C^T P^T: A = the latent tile read MN-major
-        // (64 dims per 128-byte row, the next 64 one box = 8 KiB on; tokens 128 bytes
-        // apart), B = P^T [16 heads x 64 tokens] K-major
+        // O^T (4 blocks of 128 latent dims) += C^T P^T: A = latent boxes 2i, 2i+1 read
+        // MN-major (64 dims per 128-byte row, the next 64 one box = 16 KiB on; tokens 128
+        // bytes apart), B = P^T [16 heads x 128 tokens] K-major (two 64-token atoms); the
+        // two boxes go back to the producer as soon as the block's MMAs are done
 #pragma unroll 1
         for (int i = 0; i < 4; ++i) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
+          for (int kk = 0; kk < 8; ++kk) {
             const uint32_t a = sC + (2 * i) * kBox + kk * 16 * 128;
-            const uint32_t pb = sP + kk * 32;
+            const uint32_t pb = sP + (kk >> 2) * kQBox + (kk & 3) * 32;
             ptx::umma_f16(tmem + kColO + i * kHeads, ptx::sw128_mnmajor_desc(a, kBox),
                           ptx::sw128_kmajor_desc(pb), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
           }
+          ptx::umma_commit(box_empty0 + 8u * (2 * i));
+          ptx::umma_commit(box_empty0 + 8u * (2 * i + 1));
         }
-        ptx::umma_commit(c_empty);
         ptx::umma_commit(o_done);
       }
       ptx::umma_commit(drain_bar);
@@ -204,8 +228,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else {
     // ------------------------------------------------------------------ softmax (warps 2-5)
     const int quarter = warp & 3;
-    const int tl = quarter * 32 + lane;  // TMEM lane = latent dim within an O^T block
-    const int tok = quarter * 16 + (lane & 15);  // token of S lane tl (lanes 0-15 of a warp)
+    const int tl = quarter * 32 + lane;  // TMEM lane: token of S, latent dim of an O^T block
+    const int tok = tl;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     constexpr float kLazy = 8.f;
     float m[kHeads], lsum[kHeads];
@@ -217,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = nchunk > 0;
     for (int j = 0; ok && j < nchunk; ++j) {
       const int t = t_begin + j * kChunk + tok;
-      const bool live = lane < 16 && t < t_end;  // lanes 16-31 of each quarter hold no token
+      const bool live = t < t_end;
       const float r = live ? __ldg(p.rstd + row0 + t) : 0.f;  // in flight during the wait
       int w_ok = 1;
       if (lane == 0)
@@ -269,17 +293,18 @@ __global__ void __launch_bounds__(kThreads, 2)
           any_rescale = true;
         }
       }
-      // P^T (times rstd) into the 16 x 64 shared tile: head h is row h, token tok is element
-      // tok of the row's 128 bytes, 16-byte chunks XOR-swizzled by (h & 7) as the
-      // SWIZZLE_128B operand layout expects
+      // P^T (times rstd) into the 16 x 128 shared tile: head h is row h of atom tok / 64,
+      // token tok is element tok % 64 of the row's 128 bytes, 16-byte chunks XOR-swizzled
+      // by (h & 7) as the SWIZZLE_128B operand layout expects
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) {
         const float pv = ptx::ex2(s[h] - m[h]);  // 0 for a token that is not live
         lsum[h] = lsum[h] * alpha[h] + pv;
-        if (lane < 16) {
-          const uint32_t chunk = (static_cast<uint32_t>(tok >> 3) ^ static_cast<uint32_t>(h & 7));
-          __nv_bfloat16* dst =
-              reinterpret_cast<__nv_bfloat16*>(sPgen + h * 128 + chunk * 16) + (tok & 7);
+        {
+          const int w = tok & 63;
+          const uint32_t chunk = (static_cast<uint32_t>(w >> 3) ^ static_cast<uint32_t>(h & 7));
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sPgen + (tok >> 6) * kQBox +
+                                                                 h * 128 + chunk * 16) + (w & 7);
           *dst = __float2bfloat16_rn(pv * r);
         }
       }
@@ -513,8 +538,8 @@ int tmap_2d(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, uint32_
 
 int nsplit_for(int batch, int len, int num_sms, int* chunks_per_split) {
   const int chunks = (len + kChunk - 1) / kChunk;
-  // one wave of two CTAs per SM, at least one chunk per split
-  int want = (2 * num_sms) / batch;
+  // one wave of one CTA per SM, at least one chunk per split
+  int want = num_sms / batch;
   if (want > chunks) want = chunks;
   if (want < 1) want = 1;
   *chunks_per_split = (chunks + want - 1) / want;
