@@ -2,6 +2,7 @@
 // status word, the hello stub and the bounded-wait probe.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -82,6 +83,21 @@ int device_info(DeviceInfo* out) {
 __device__ int g_ds_device_status;
 
 namespace ds {
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("DS_PDL");
+    return e != nullptr && atoi(e) != 0;
+  }();
+  return on;
+}
+
+void add_pdl_attr(cudaLaunchAttribute* attrs, unsigned int& n) {
+  if (!pdl_enabled()) return;
+  attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+}
+
 int* device_status_ptr() {
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_ds_device_status) != cudaSuccess) return nullptr;

@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(1024, 1)
                    int32_t* __restrict__ offsets, int32_t* __restrict__ blk_base,
                    int32_t* __restrict__ dest_base, int32_t* __restrict__ recv_off, int64_t cap,
                    int* status, long long timeout_cycles) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   constexpr int P = 1024 / kMaxExperts;
   __shared__ int part[P][kMaxExperts];
   __shared__ int pbase[P][kMaxExperts];
@@ -209,6 +211,8 @@ __global__ void __launch_bounds__(256)
                       int32_t* __restrict__ slot_of, const __grid_constant__ PeerTable peers,
                       size_t flags_off,
                       size_t meta_off, size_t rows_off, int64_t cap, int* status) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   __shared__ uint4* rows_of[kMaxRanks];
   __shared__ int* meta_of[kMaxRanks];
   __shared__ int bail;
@@ -503,18 +507,17 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
     DS_TRY(ds::gemm::launch(s1, ss.stream));
     DS_CUDA(cudaEventRecord(ss.join, ss.stream));
   }
-  ep::ep_plan_kernel<<<1, 1024, 0, s>>>(b.blk_hist, nblk, E, El, rank, world, peers, L.flags,
-                                        L.counts, target, b.offsets, b.blk_base, b.dest_base,
-                                        b.recv_off, L.cap, status, timeout_cycles);
-  DS_LAUNCH_CHECK("ep_plan_kernel");
+  DS_CUDA(ds::launch_pdl(ep::ep_plan_kernel, dim3(1), dim3(1024), 0, s, b.blk_hist, nblk, E, El,
+                         rank, world, peers, L.flags, L.counts, target, b.offsets, b.blk_base,
+                         b.dest_base, b.recv_off, L.cap, status, timeout_cycles));
   DS_TRY(mark(2));
   {
     const int grid = T > 0 ? (T + 7) / 8 < 4 * di.num_sms ? (T + 7) / 8 : 4 * di.num_sms : 1;
 #define DS_EP_SCATTER(KK)                                                                     \
-  ep::ep_scatter_kernel<KK><<<grid, 256, 0, s>>>(                                             \
-      static_cast<const uint4*>(x_bf16), T, H / 8, E, El, rank, world, b.idx, b.blk_base,     \
-      b.local_rank, b.offsets, b.dest_base, b.slot_of, peers, L.flags, L.recv_meta,           \
-      L.recv_rows, L.cap, status)
+  DS_CUDA(ds::launch_pdl(ep::ep_scatter_kernel<KK>, dim3(grid), dim3(256), 0, s,               \
+                         static_cast<const uint4*>(x_bf16), T, H / 8, E, El, rank, world,     \
+                         b.idx, b.blk_base, b.local_rank, b.offsets, b.dest_base, b.slot_of,  \
+                         peers, L.flags, L.recv_meta, L.recv_rows, L.cap, status))
     switch (K) {
       case 1: DS_EP_SCATTER(1); break;
       case 2: DS_EP_SCATTER(2); break;

@@ -414,11 +414,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int nunits = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
-  for (int pb = 0; pb < p.nprob; ++pb) {
-    const ProbParams& q = prob_params(p, pb);
-    for (int i = threadIdx.x; i <= q.groups; i += kThreads)
-      goff[pb * kGroupStride + i] = q.offsets ? __ldg(q.offsets + i) : (i == 0 ? 0 : q.dense_rows);
-  }
+  // the next kernel of the stream may begin launching: its CTAs take SMs as this launch's
+  // CTAs retire and run their prologue up to their own pdl_wait
+  ptx::pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
       ptx::mbar_init(full0 + 8u * s, 1);
@@ -449,6 +447,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kTmemCols);
       ptx::tmem_relinquish();
     }
+  }
+  // everything below reads or writes what earlier kernels of the stream produce or read
+  ptx::pdl_wait();
+  for (int pb = 0; pb < p.nprob; ++pb) {
+    const ProbParams& q = prob_params(p, pb);
+    for (int i = threadIdx.x; i <= q.groups; i += kThreads)
+      goff[pb * kGroupStride + i] = q.offsets ? __ldg(q.offsets + i) : (i == 0 ? 0 : q.dense_rows);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -1013,7 +1018,7 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
   }
   if (pair) {
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
@@ -1024,20 +1029,20 @@ int launch_multi(const Problem* const* probs, int n, cudaStream_t s, const Signa
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    add_pdl_attr(attr, cfg.numAttrs);
     if (epi == kSwiGLU)
       DS_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<kSwiGLU, true>, tmA[0], tmB[0], tmA[1],
                                  tmB[1], tmO[0], tmO[1], p));
     else
       DS_CUDA(cudaLaunchKernelEx(&cfg, grouped_gemm_kernel<kPlain, true>, tmA[0], tmB[0], tmA[1],
                                  tmB[1], tmO[0], tmO[1], p));
-  } else if (epi == kSwiGLU) {
-    grouped_gemm_kernel<kSwiGLU, false><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
-  } else if (epi == kRouter) {
-    grouped_gemm_kernel<kRouter, false><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
-  } else if (epi == kPartial) {
-    grouped_gemm_kernel<kPartial, false><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
   } else {
-    grouped_gemm_kernel<kPlain, false><<<grid, kThreads, kSmemBytes, s>>>(tmA[0], tmB[0], tmA[1], tmB[1], tmO[0], tmO[1], p);
+    auto k = epi == kSwiGLU   ? grouped_gemm_kernel<kSwiGLU, false>
+             : epi == kRouter ? grouped_gemm_kernel<kRouter, false>
+             : epi == kPartial ? grouped_gemm_kernel<kPartial, false>
+                               : grouped_gemm_kernel<kPlain, false>;
+    DS_CUDA(launch_pdl(k, dim3(grid), dim3(kThreads), kSmemBytes, s, tmA[0], tmB[0], tmA[1],
+                       tmB[1], tmO[0], tmO[1], p));
   }
   DS_LAUNCH_CHECK("grouped_gemm_kernel");
   return DS_OK;

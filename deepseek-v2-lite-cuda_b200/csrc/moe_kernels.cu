@@ -99,6 +99,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32)
                  float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
                  float* __restrict__ w_out, int32_t* __restrict__ counts,
                  int32_t* __restrict__ blk_hist, int32_t* __restrict__ local_rank) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   __shared__ int sel[kRouteTokens][K];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = lane >> 4, hl = lane & 15;
@@ -220,6 +222,8 @@ __global__ void __launch_bounds__(1024)
     plan_kernel(const int32_t* __restrict__ hist, int nblk, int E,
                 const int32_t* __restrict__ offsets_in, int32_t* __restrict__ counts,
                 int32_t* __restrict__ offsets, int32_t* __restrict__ blk_base) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   constexpr int P = 1024 / kMaxExperts;
   __shared__ int part[P][kMaxExperts];
   __shared__ int pbase[P][kMaxExperts];
@@ -380,6 +384,8 @@ __global__ void __launch_bounds__(256)
                    const int32_t* __restrict__ blk_base, const int32_t* __restrict__ local_rank,
                    uint4* __restrict__ dispatched, int32_t* __restrict__ token_map,
                    float* __restrict__ dw, int32_t* __restrict__ slot_of, int S) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
   for (int t0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t0 < T; t0 += 2 * warps) {
@@ -496,6 +502,8 @@ __global__ void __launch_bounds__(256)
                           const float* __restrict__ w, const uint4* __restrict__ shared_out,
                           uint4* __restrict__ out, int T, int H8, const int* wait_flag,
                           int wait_target, int* status, long long timeout_cycles) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int lane = threadIdx.x & 31;
   if (wait_flag != nullptr) {
     __shared__ int ok;
@@ -774,8 +782,9 @@ int launch_route(const float* logits, int T, int E, int K, int32_t* idx, float* 
                  int32_t* counts, int32_t* blk_hist, int32_t* local_rank, cudaStream_t s) {
   if (T <= 0) return DS_OK;
   const int grid = route_blocks(T);
-  DS_DISPATCH_K(K, route_kernel<KK, false><<<grid, kRouteWarps * 32, 0, s>>>(
-                       logits, T, E, 0, nullptr, idx, w, counts, blk_hist, local_rank));
+  DS_DISPATCH_K(K, DS_CUDA(launch_pdl(route_kernel<KK, false>, dim3(grid), dim3(kRouteWarps * 32),
+                                      0, s, logits, T, E, 0, nullptr, idx, w, counts, blk_hist,
+                                      local_rank)));
   DS_LAUNCH_CHECK("route_kernel");
   return DS_OK;
 }
@@ -785,8 +794,9 @@ int launch_route_partials(const float* partials, int nsplit, int T, int E, int K
                           int32_t* blk_hist, int32_t* local_rank, cudaStream_t s) {
   if (T <= 0) return DS_OK;
   const int grid = route_blocks(T);
-  DS_DISPATCH_K(K, route_kernel<KK, true><<<grid, kRouteWarps * 32, 0, s>>>(
-                       partials, T, E, nsplit, logits_out, idx, w, counts, blk_hist, local_rank));
+  DS_DISPATCH_K(K, DS_CUDA(launch_pdl(route_kernel<KK, true>, dim3(grid), dim3(kRouteWarps * 32),
+                                      0, s, partials, T, E, nsplit, logits_out, idx, w, counts,
+                                      blk_hist, local_rank)));
   DS_LAUNCH_CHECK("route_kernel");
   return DS_OK;
 }
@@ -802,7 +812,8 @@ int launch_rank(const int32_t* idx, int T, int E, int K, int32_t* blk_hist,
 
 int launch_plan(const int32_t* blk_hist, int nblk, int E, const int32_t* offsets_in,
                 int32_t* counts, int32_t* offsets, int32_t* blk_base, cudaStream_t s) {
-  plan_kernel<<<1, 1024, 0, s>>>(blk_hist, nblk, E, offsets_in, counts, offsets, blk_base);
+  DS_CUDA(launch_pdl(plan_kernel, dim3(1), dim3(1024), 0, s, blk_hist, nblk, E, offsets_in,
+                     counts, offsets, blk_base));
   DS_LAUNCH_CHECK("plan_kernel");
   return DS_OK;
 }
@@ -821,10 +832,10 @@ int launch_scatter(const void* x, int T, int H, int E, int K, const int32_t* idx
   DeviceInfo di;
   DS_TRY(device_info(&di));
   const int grid = grid_for(T, 8, di.num_sms, 8);
-  DS_DISPATCH_K(K, scatter_kernel<KK><<<grid, 256, 0, s>>>(
-                       static_cast<const uint4*>(x), T, H / 8, E, idx, w, blk_base,
-                       local_rank, static_cast<uint4*>(dispatched), token_map,
-                       dispatched_weights, slot_of, S));
+  DS_DISPATCH_K(K, DS_CUDA(launch_pdl(scatter_kernel<KK>, dim3(grid), dim3(256), 0, s,
+                                      static_cast<const uint4*>(x), T, H / 8, E, idx, w,
+                                      blk_base, local_rank, static_cast<uint4*>(dispatched),
+                                      token_map, dispatched_weights, slot_of, S)));
   DS_LAUNCH_CHECK("scatter_kernel");
   return DS_OK;
 }
@@ -836,10 +847,11 @@ int launch_combine_gather(const void* eo, const int32_t* slot_of, const float* w
   DeviceInfo di;
   DS_TRY(device_info(&di));
   const int grid = grid_for(T, 8, di.num_sms, 8);
-  DS_DISPATCH_K(K, combine_gather_kernel<KK><<<grid, 256, 0, s>>>(
-                       static_cast<const uint4*>(eo), slot_of, w,
-                       static_cast<const uint4*>(shared_out), static_cast<uint4*>(out), T,
-                       H / 8, wait_flag, wait_target, device_status_ptr(), timeout_cycles));
+  DS_DISPATCH_K(K, DS_CUDA(launch_pdl(combine_gather_kernel<KK>, dim3(grid), dim3(256), 0, s,
+                                      static_cast<const uint4*>(eo), slot_of, w,
+                                      static_cast<const uint4*>(shared_out),
+                                      static_cast<uint4*>(out), T, H / 8, wait_flag,
+                                      wait_target, device_status_ptr(), timeout_cycles)));
   DS_LAUNCH_CHECK("combine_gather_kernel");
   return DS_OK;
 }

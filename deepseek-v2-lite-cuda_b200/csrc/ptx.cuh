@@ -272,6 +272,15 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Programmatic dependent launch: let the stream's next kernel begin launching (its CTAs then
+// run up to their own pdl_wait), and wait until the previous kernel has completed with its
+// memory visible.  Both are no-ops for a launch without the programmatic-serialization
+// attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 2^x (PTX ex2.approx, flush-to-zero); ex2(-inf) = +0.
 __device__ __forceinline__ float ex2(float x) {
   float y;
