@@ -412,9 +412,9 @@ def run_ours(args, rank, world, local_rank):
     xh = x.cpu().pin_memory()
     oh = [torch.empty(Ts, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     pipe = HostPipeline(layer, Ts, H, dev)
-    # warm-up until the caching allocator holds enough output blocks for the steps in flight
-    # (an output is released on the copy stream, so the first steps allocate new blocks and
-    # the host, not the GPU, would set the pace)
+    # warm-up: the pipeline's per-slot buffers are allocated up front and the layer writes
+    # into them, so the timed steps allocate no device memory (an allocation in the loop
+    # could synchronise the device and stall the copy/compute overlap)
     for i in range(max(16, 2 * args.warmup)):
         pipe.submit(xh, oh[i % 2])
     pipe.synchronize()

@@ -948,6 +948,11 @@ def moe_dispatch_routed(idx: torch.Tensor, w: torch.Tensor, x: torch.Tensor, num
     return off, slot_of, tmap, disp
 
 
+def _check_out(out: torch.Tensor, T: int, H: int, device) -> None:
+    _require(out.dtype == torch.bfloat16 and tuple(out.shape) == (T, H) and out.is_contiguous()
+             and out.device == device, "out must be a contiguous bf16 [T, H] tensor on x's device")
+
+
 def moe_layer_forward_from_x(x: torch.Tensor, router_w_split: torch.Tensor, num_experts: int,
                              packed_w1: torch.Tensor, w2: torch.Tensor,
                              shared_w1: Optional[torch.Tensor] = None,
@@ -966,6 +971,8 @@ def moe_layer_forward_from_x(x: torch.Tensor, router_w_split: torch.Tensor, num_
     Is = 0 if shared_w1 is None else shared_w1.shape[0] // 2
     if out is None:
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    else:
+        _check_out(out, T, H, x.device)
     if T == 0:
         return out
     need = moe_layer_workspace_size(T, H, E, top_k, I, Is)
@@ -1099,6 +1106,8 @@ def ep_layer_forward(x: torch.Tensor, router_w_split: torch.Tensor, num_experts:
     Is = 0 if shared_w1 is None else shared_w1.shape[0] // 2
     if out is None:
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    else:
+        _check_out(out, T, H, x.device)
     need = ep_layer_workspace_size(max_tokens, H, E, top_k, I, Is, world)
     _require(workspace.numel() >= need, f"ep_layer_forward: workspace needs {need} bytes")
     ev = None

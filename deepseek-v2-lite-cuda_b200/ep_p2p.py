@@ -102,7 +102,8 @@ class P2PEPMoELayer(torch.nn.Module):
                 dist.barrier(group=self.group)
 
     def forward(self, x: torch.Tensor, events=None,
-                logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                logits_out: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self._segment is None:
             raise RuntimeError("P2PEPMoELayer: closed")
         if x.shape[0] > self.max_tokens:
@@ -111,7 +112,7 @@ class P2PEPMoELayer(torch.nn.Module):
         return ds_kernels.ep_layer_forward(
             x, self.router_w_split, self.num_experts, self.w1, self.w2, self.shared_w1,
             self.shared_w2, self.top_k, self.rank, self.world, self.max_tokens, self.sym_bases,
-            self._epoch, self.workspace, timeout_ms=self.timeout_ms, events=events,
+            self._epoch, self.workspace, out=out, timeout_ms=self.timeout_ms, events=events,
             logits_out=logits_out)
 
     def check(self) -> None:

@@ -18,6 +18,7 @@ equals DeepSeekMoE.forward for any n_shared_experts.
 """
 from __future__ import annotations
 
+import inspect
 from typing import Optional
 
 import torch
@@ -40,7 +41,7 @@ class _Workspace:
 
 
 def _layer(hidden_states, router_w_split, num_experts, packed_w1, w2, shared_w1, shared_w2,
-           top_k, ws, events=None, logits_out=None):
+           top_k, ws, events=None, logits_out=None, out=None):
     T, H = hidden_states.shape
     E, twoI, _ = packed_w1.shape
     Is = 0 if shared_w1 is None else shared_w1.shape[0] // 2
@@ -48,7 +49,7 @@ def _layer(hidden_states, router_w_split, num_experts, packed_w1, w2, shared_w1,
     return ds_kernels.moe_layer_forward_from_x(hidden_states, router_w_split, num_experts,
                                                packed_w1, w2, shared_w1, shared_w2, top_k=top_k,
                                                workspace=ws.get(need, hidden_states.device),
-                                               events=events, logits_out=logits_out)
+                                               events=events, logits_out=logits_out, out=out)
 
 
 class FusedMoELayer(nn.Module):
@@ -108,15 +109,17 @@ class FusedMoELayer(nn.Module):
         return idx, w
 
     def forward(self, hidden_states: torch.Tensor, events=None,
-                logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """hidden_states bf16 [T, H] -> bf16 [T, H].  `logits_out` (f32 [T, E]) receives the
-        router logits; `events` (9 CUDA events) are recorded between the phases."""
+                logits_out: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """hidden_states bf16 [T, H] -> bf16 [T, H] (into `out` when given).  `logits_out`
+        (f32 [T, E]) receives the router logits; `events` (9 CUDA events) are recorded between
+        the phases."""
         assert hidden_states.is_cuda, "hidden_states must be on CUDA."
         assert hidden_states.dtype == torch.bfloat16, "hidden_states must be BF16."
         assert hidden_states.dim() == 2, "hidden_states must be 2-D [T, H]."
         return _layer(hidden_states.contiguous(), self.router_w_split, self.num_experts,
                       self.packed_w1, self.w2, self.shared_w1, self.shared_w2, self.top_k,
-                      self._ws, events, logits_out)
+                      self._ws, events, logits_out, out)
 
 
 _WEIGHT_CACHE: dict = {}
@@ -149,7 +152,10 @@ class HostPipeline:
     Each submitted batch is copied host->device on a copy stream, run through the layer on the
     compute stream, and copied device->host on a second copy stream, so the copies of one
     batch overlap the compute of its neighbours (the copy engines and the SMs work
-    concurrently).  Every batch still makes its own round trip.
+    concurrently).  Every batch still makes its own round trip.  Input and output buffers are
+    allocated once per slot (a layer whose forward takes `out=` writes into its slot), so a
+    steady stream of batches allocates no device memory: an allocation in the loop could
+    synchronise the device and stall the pipeline.
 
         pipe = HostPipeline(layer, max_tokens=8192, hidden=2048)
         for x_host, out_host in batches:          # pinned CPU bf16 tensors [T, H]
@@ -167,6 +173,10 @@ class HostPipeline:
         self.d2h = torch.cuda.Stream(dev)
         self.x = [torch.empty((max_tokens, hidden), dtype=torch.bfloat16, device=dev)
                   for _ in range(depth)]
+        self.takes_out = "out" in inspect.signature(layer.forward).parameters
+        self.out = [torch.empty((max_tokens, hidden), dtype=torch.bfloat16, device=dev)
+                    for _ in range(depth)] if self.takes_out else None
+        self.out_free = [torch.cuda.Event() for _ in range(depth)]
         self.in_ready = [torch.cuda.Event() for _ in range(depth)]
         self.x_free = [torch.cuda.Event() for _ in range(depth)]
         self.out_ready = [torch.cuda.Event() for _ in range(depth)]
@@ -184,13 +194,21 @@ class HostPipeline:
             self.in_ready[i].record(self.h2d)
         self.compute.wait_event(self.in_ready[i])
         with torch.cuda.stream(self.compute):
-            out = self.layer(xb)
+            if self.takes_out:
+                if self.used[i]:  # the slot's previous output has been copied out
+                    self.compute.wait_event(self.out_free[i])
+                out = self.layer(xb, out=self.out[i][:T])
+            else:
+                out = self.layer(xb)
             self.x_free[i].record(self.compute)
             self.out_ready[i].record(self.compute)
         self.d2h.wait_event(self.out_ready[i])
         with torch.cuda.stream(self.d2h):
             out_host.copy_(out, non_blocking=True)
-            out.record_stream(self.d2h)
+            if self.takes_out:
+                self.out_free[i].record(self.d2h)
+            else:
+                out.record_stream(self.d2h)
         self.used[i] = True
         self.n += 1
 

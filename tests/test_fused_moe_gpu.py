@@ -185,17 +185,32 @@ def test_cfg2_full_size():
     check(out, ref)
 
 
-def test_host_pipeline_matches_direct_calls():
+class _NoOut(torch.nn.Module):
+    """A layer whose forward takes no `out=`: the pipeline keeps each result alive instead."""
+
+    def __init__(self, layer):
+        super().__init__()
+        self.layer = layer
+
+    def forward(self, x):
+        return self.layer(x)
+
+
+@pytest.mark.parametrize("takes_out", [True, False])
+def test_host_pipeline_matches_direct_calls(takes_out):
     # moe_fused.HostPipeline: pinned host batches -> device -> layer -> pinned host, with the
-    # copies overlapped across batches; results must equal direct device calls bit for bit.
+    # copies overlapped across batches; results must equal direct device calls bit for bit,
+    # whether the layer writes into the pipeline's per-slot outputs or returns its own.
     from moe_fused import FusedMoELayer, HostPipeline
     W = weights(0, 2)
     D = device_weights(W)
     layer = FusedMoELayer.from_packed(D["gate"], D["w1"], D["w2"], D["sw1"], D["sw2"], top_k=K)
     g = torch.Generator().manual_seed(77)
-    xs = [torch.randn(T, H, generator=g).to(torch.bfloat16).pin_memory() for T in (300, 512, 1, 300)]
+    xs = [torch.randn(T, H, generator=g).to(torch.bfloat16).pin_memory()
+          for T in (300, 512, 1, 300, 7, 512)]
     outs = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for x in xs]
-    pipe = HostPipeline(layer, max_tokens=512, hidden=H)
+    pipe = HostPipeline(layer if takes_out else _NoOut(layer), max_tokens=512, hidden=H)
+    assert pipe.takes_out == takes_out
     for x, o in zip(xs, outs):
         pipe.submit(x, o)
     pipe.synchronize()
