@@ -466,7 +466,7 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
     r.B = router_w_split_bf16;
     r.b_rows = 256;
     r.groups = 1;
-    r.n_tiles = ds::kRouterSplits;
+    r.n_tiles = ds::router_splits(H);
     r.b_rows_per_group = 256;
     r.b_tile_stride = 0;
     r.b_half1_off = 128;
@@ -475,7 +475,7 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
     r.epilogue = ds::gemm::kRouter;
     r.logits_out = b.router_part;
     DS_TRY(ds::gemm::launch(r, s));
-    DS_TRY(ds::launch_route_partials(b.router_part, ds::kRouterSplits, T, E, K, logits_out, b.idx,
+    DS_TRY(ds::launch_route_partials(b.router_part, r.n_tiles, T, E, K, logits_out, b.idx,
                                      b.w, nullptr, b.blk_hist, b.local_rank, s));
   }
   DS_TRY(mark(1));

@@ -24,9 +24,13 @@ int launch_route_partials(const float* partials, int nsplit, int T, int E, int K
                           float* logits_out, int32_t* idx, float* w, int32_t* counts,
                           int32_t* blk_hist, int32_t* local_rank, cudaStream_t s);
 
-// Router GEMM: split K slices; partial buffer floats per token.
+// Router GEMM: split K slices; partial buffer floats per token.  Two slices (more slices at
+// 1024-2048 tokens measured no faster: those launches are bound by their fixed latency, and
+// the routing kernel then sums more partials), one when the hidden size has a single
+// 64-wide k-block, so that no slice is left without k-blocks.
 constexpr int kRouterSplits = 2;
 constexpr int kRouterPartCols = 192;
+inline int router_splits(int hidden) { return hidden > 64 ? kRouterSplits : 1; }
 
 // idx [T, K] -> blk_hist [nblk, E], local_rank [T, K].
 int launch_rank(const int32_t* idx, int T, int E, int K, int32_t* blk_hist,

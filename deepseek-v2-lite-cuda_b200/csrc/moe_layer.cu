@@ -126,7 +126,7 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
     r.b_rows = 256;
     r.offsets = nullptr;
     r.groups = 1;
-    r.n_tiles = ds::kRouterSplits;
+    r.n_tiles = ds::router_splits(H);
     r.b_rows_per_group = 256;
     r.b_tile_stride = 0;
     r.b_half1_off = 128;
@@ -136,7 +136,7 @@ int layer_impl(const float* router_logits, const void* router_w_split, float* lo
     r.epilogue = ds::gemm::kRouter;
     r.logits_out = b.router_part;
     DS_TRY(ds::gemm::launch(r, s));
-    DS_TRY(ds::launch_route_partials(b.router_part, ds::kRouterSplits, T, E, K, logits_out, b.idx,
+    DS_TRY(ds::launch_route_partials(b.router_part, r.n_tiles, T, E, K, logits_out, b.idx,
                                      b.w, nullptr, b.blk_hist, b.local_rank, s));
   } else {
     DS_TRY(ds::launch_route(router_logits, T, E, K, b.idx, b.w, nullptr, b.blk_hist, b.local_rank, s));

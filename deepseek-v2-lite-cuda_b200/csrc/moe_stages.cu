@@ -356,7 +356,7 @@ int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens, 
   p.b_rows = 256;
   p.offsets = nullptr;
   p.groups = 1;
-  p.n_tiles = ds::kRouterSplits;
+  p.n_tiles = ds::router_splits(hidden_size);
   p.b_rows_per_group = 256;
   p.b_tile_stride = 0;
   p.b_half1_off = 128;
@@ -366,7 +366,7 @@ int ds_moe_router(const void* x_bf16, const void* w_split_bf16, int num_tokens, 
   p.epilogue = ds::gemm::kRouter;
   p.logits_out = part;
   DS_TRY(ds::gemm::launch(p, s));
-  return ds::launch_route_partials(part, ds::kRouterSplits, num_tokens, num_experts, top_k,
+  return ds::launch_route_partials(part, p.n_tiles, num_tokens, num_experts, top_k,
                                    logits_out, topk_indices, topk_weights, nullptr, nullptr,
                                    nullptr, s);
 }
