@@ -71,12 +71,25 @@ def test_workspace_queries_are_host_only():
     (lambda L: L.ds_moe_combine(None, None, None, None, 6, 2048, 0, None, 0, None), 1),
     (lambda L: L.ds_moe_dispatch(None, None, None, None, None, None, None, 4, 2047, 64, 6,
                                  None, 0, None), 1),
+    # the persistent attention kernel's work counter lives in the workspace: none, or too
+    # small, is refused before anything touches the device
+    (lambda L: L.ds_mla_attention(ctypes.c_void_p(256), 3648, ctypes.c_void_p(512),
+                                  ctypes.c_void_p(768), 1, 128, 16, ctypes.c_float(0.1), None,
+                                  256, None), 1),
+    (lambda L: L.ds_mla_attention(ctypes.c_void_p(256), 3648, ctypes.c_void_p(512),
+                                  ctypes.c_void_p(768), 1, 128, 16, ctypes.c_float(0.1),
+                                  ctypes.c_void_p(1024), 128, None), 1),
 ])
 def test_argument_validation_without_gpu(call, code):
     import ds_kernels
     lib = ds_kernels.library()
     assert call(lib) == code
     assert lib.ds_last_error().decode()
+
+
+def test_mla_attention_workspace_is_the_tile_counter():
+    import ds_kernels
+    assert ds_kernels.library().ds_mla_attention_workspace_size(4, 4096, 16) == 256
 
 
 def test_zero_size_calls_are_no_ops_without_gpu():
