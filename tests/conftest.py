@@ -44,6 +44,19 @@ def golden_dir():
     return GOLDEN
 
 
+def _record(max_abs, rel, ref_max, atol):
+    """With DS_RECORD_ERRORS=<file>, append the check's max-abs and relative-L2 errors (and
+    the reference's largest magnitude) as one JSON line per check, keyed by the test."""
+    path = os.environ.get("DS_RECORD_ERRORS")
+    if not path:
+        return
+    import json
+    with open(path, "a") as f:
+        f.write(json.dumps({"test": os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0],
+                            "max_abs": max_abs, "rel_l2": rel, "ref_max_abs": ref_max,
+                            "atol": atol}) + "\n")
+
+
 def assert_bf16_close(out, ref, atol, rel_l2_max=1e-2):
     """bf16 output vs f32 reference: |out - ref| <= atol + 2^-8 |ref| elementwise (2^-8 is the
     relative half-ulp of bf16 round-to-nearest, so large outputs are held to their own
@@ -55,5 +68,6 @@ def assert_bf16_close(out, ref, atol, rel_l2_max=1e-2):
     bound = atol + (2.0 ** -8) * r.abs()
     worst = (err - bound).max().item()
     rel = (torch.linalg.vector_norm(o - r) / torch.linalg.vector_norm(r).clamp_min(1e-30)).item()
+    _record(err.max().item(), rel, r.abs().max().item(), atol)
     assert worst <= 0 and rel <= rel_l2_max, (
         f"max excess over atol+2^-8|ref|: {worst:.3e}, max-abs {err.max().item():.3e}, rel-L2 {rel:.3e}")
