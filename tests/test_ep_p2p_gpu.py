@@ -62,6 +62,35 @@ def test_one_rank_equals_fused_layer():
         ep.close()
 
 
+def test_one_rank_host_pipeline_writes_into_slot_outputs():
+    # HostPipeline hands the layer its per-slot output buffers (out=); the pipelined results
+    # must equal direct calls bit for bit, and the layer must write into the buffer it got
+    import ds_kernels
+    import synthetic
+    from moe_fused import HostPipeline
+    ds_kernels.clear_device_status()
+    dev = torch.device("cuda:0")
+    _, ref, ep = _layers(33, dev, 0, 1, 1024)
+    try:
+        xs = [synthetic.make_tokens(200 + i, T, H, dev).cpu().pin_memory()
+              for i, T in enumerate((1024, 17, 512, 1024, 1))]
+        outs = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for x in xs]
+        pipe = HostPipeline(ep, max_tokens=1024, hidden=H)
+        assert pipe.takes_out
+        for x, o in zip(xs, outs):
+            pipe.submit(x, o)
+        pipe.synchronize()
+        for x, o in zip(xs, outs):
+            assert torch.equal(o, ref(x.to(dev)).cpu())
+        buf = torch.empty(300, H, dtype=torch.bfloat16, device=dev)
+        x = synthetic.make_tokens(9, 300, H, dev)
+        assert ep(x, out=buf).data_ptr() == buf.data_ptr()
+        assert torch.equal(buf, ref(x))
+        ep.check()
+    finally:
+        ep.close()
+
+
 def test_one_rank_matches_oracle():
     import ds_kernels
     import oracle
