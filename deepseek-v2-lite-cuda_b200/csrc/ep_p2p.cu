@@ -12,8 +12,9 @@
 //             owner's receive buffer (expert-major, source rank minor, ascending token within)
 //             together with its return address (source rank, slot); the launch's last CTA
 //             raises every rank's arrival flag.
-//   GEMM1   : shared-expert tiles first; the producer of the routed tiles waits for the
-//             arrival flag (every rank's rows are in), so the transfer hides behind them.
+//   GEMM1   : the shared expert's GEMM1 runs on a side stream from the start of the forward,
+//             beside the routing, plan and scatter; the routed GEMM1's producer waits for
+//             the arrival flag (every rank's rows are in) before its first load.
 //   GEMM2   : routed tiles store each output row straight into the source rank's return
 //             buffer at its slot; the launch's last CTA raises every rank's return flag.
 //   combine : waits for the return flag, then gathers in ascending slot order as on one GPU.
@@ -458,30 +459,10 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
   int* my_flags = reinterpret_cast<int*>(mine + L.flags);
 
   DS_TRY(mark(0));
-  if (T > 0) {
-    ds::gemm::Problem r{};
-    r.A = x_bf16;
-    r.a_rows = T;
-    r.K = H;
-    r.B = router_w_split_bf16;
-    r.b_rows = 256;
-    r.groups = 1;
-    r.n_tiles = ds::router_splits(H);
-    r.b_rows_per_group = 256;
-    r.b_tile_stride = 0;
-    r.b_half1_off = 128;
-    r.weight_group_mod = 1;
-    r.ldo = 8;
-    r.epilogue = ds::gemm::kRouter;
-    r.logits_out = b.router_part;
-    DS_TRY(ds::gemm::launch(r, s));
-    DS_TRY(ds::launch_route_partials(b.router_part, r.n_tiles, T, E, K, logits_out, b.idx,
-                                     b.w, nullptr, b.blk_hist, b.local_rank, s));
-  }
-  DS_TRY(mark(1));
   // the shared expert's GEMM1 (SwiGLU) needs only this rank's tokens: it runs on a side
-  // stream, capped below the SM count, while the plan and the dispatch kernel (which is
-  // bound by NVLink, not by SMs) run here; joined back before GEMM2
+  // stream, capped below the SM count, while the router GEMM and routing (a few CTAs at few
+  // tokens per rank), the plan and the dispatch kernel (bound by NVLink, not by SMs) run on
+  // the SMs it leaves; joined back before GEMM2
   const bool side = has_shared && T > 0;
   if (side) {
     ds::SideStream ss;
@@ -507,6 +488,27 @@ int ds_ep_layer_forward(const void* x_bf16, int num_tokens, const void* router_w
     DS_TRY(ds::gemm::launch(s1, ss.stream));
     DS_CUDA(cudaEventRecord(ss.join, ss.stream));
   }
+  if (T > 0) {
+    ds::gemm::Problem r{};
+    r.A = x_bf16;
+    r.a_rows = T;
+    r.K = H;
+    r.B = router_w_split_bf16;
+    r.b_rows = 256;
+    r.groups = 1;
+    r.n_tiles = ds::router_splits(H);
+    r.b_rows_per_group = 256;
+    r.b_tile_stride = 0;
+    r.b_half1_off = 128;
+    r.weight_group_mod = 1;
+    r.ldo = 8;
+    r.epilogue = ds::gemm::kRouter;
+    r.logits_out = b.router_part;
+    DS_TRY(ds::gemm::launch(r, s));
+    DS_TRY(ds::launch_route_partials(b.router_part, r.n_tiles, T, E, K, logits_out, b.idx,
+                                     b.w, nullptr, b.blk_hist, b.local_rank, s));
+  }
+  DS_TRY(mark(1));
   DS_CUDA(ds::launch_pdl(ep::ep_plan_kernel, dim3(1), dim3(1024), 0, s, b.blk_hist, nblk, E, El,
                          rank, world, peers, L.flags, L.counts, target, b.offsets, b.blk_base,
                          b.dest_base, b.recv_off, L.cap, status, timeout_cycles));

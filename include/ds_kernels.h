@@ -466,8 +466,8 @@ DS_API size_t ds_ep_layer_workspace_size(int max_tokens, int hidden_size, int nu
  * must call it for every forward, with epoch = 1, 2, 3, ...).  w1_local [El*2I, H] and
  * w2_local [El*H, I] hold experts [rank*El, (rank+1)*El) in the prepacked layout; router,
  * shared expert, logits_out and out as ds_moe_layer_forward_from_x.  The shared expert's
- * GEMM1 runs on an internal second stream beside the dispatch (forked from and joined back
- * into `stream` with events; one forward at a time per device).  events: NULL or
+ * GEMM1 runs on an internal second stream beside the routing and the dispatch (forked from
+ * and joined back into `stream` with events; one forward at a time per device).  events: NULL or
  * DS_EP_NUM_EVENTS handles bracketing route | plan+count exchange | dispatch+send |
  * routed GEMM1 | GEMM2 (+shared, return) | combine. */
 DS_API int ds_ep_layer_forward(const void* x_bf16, int num_tokens,
